@@ -1,0 +1,173 @@
+/*
+ * b200conv.h -- C ABI of libb200conv.so, the sm_100a kernels behind the
+ * amd_tuned_torch conv/norm hot path (F.conv1d depthwise, F.conv3d,
+ * F.group_norm).
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are raw DEVICE pointers owned by the caller; the
+ *     library never allocates or frees caller memory.  Where an op needs
+ *     scratch, a *_workspace_bytes() query tells the caller how much to pass.
+ *   - Sizes are int64_t element counts; dtypes are B200_DTYPE_* codes.
+ *   - `stream` is a cudaStream_t passed as void* (torch's
+ *     torch.cuda.current_stream().cuda_stream); every launch goes on it.
+ *   - Return value: 0 = launched, > 0 = B200_UNSUPPORTED (the call is outside
+ *     what the kernel handles -- the Python candidate declines and the contest
+ *     moves on), < 0 = error (-1 bad argument, -(1000 + cudaError_t) for a
+ *     CUDA runtime error).  b200_last_error() returns a message for the
+ *     calling thread's last non-zero status.
+ *
+ * Each declaration cites the reference interface it replaces
+ * (WifiLast/rocm-kernel-select, path:line).
+ */
+#ifndef B200CONV_H
+#define B200CONV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_DTYPE_F32 0
+#define B200_DTYPE_F16 1
+#define B200_DTYPE_BF16 2
+
+#define B200_OK 0
+#define B200_UNSUPPORTED 1
+#define B200_ERR_ARG (-1)
+
+/* Library version (major*10000 + minor*100 + patch). No reference
+ * counterpart: the reference ships pybind11 modules, see
+ * amd_tuned_torch/_native_loader.py:56-147 for its loader. */
+int b200_version(void);
+
+/* Message for the calling thread's last non-zero status. */
+const char* b200_last_error(void);
+
+/* Reads and clears the device-side fault word that bounded waits inside the
+ * kernels set when a wait runs out (0 = none).  Synchronizes `stream`. */
+int b200_read_device_flags(void* stream, int* flags_out);
+
+/* Number of SMs on the current device (grid sizing). */
+int b200_sm_count(void);
+
+/* ------------------------------------------------------------------ */
+/* GroupNorm forward.
+ * Replaces _C.group_norm(input, num_groups, weight?, bias?, eps)
+ * (src/main_rocm.cpp:556-599) and its kernel group_norm_kernel
+ * (src/cuda/group_norm.cu:40-104).  x, y: contiguous [N, C, S] with
+ * S = product of spatial dims; gamma/beta: [C] of `affine_dtype` or NULL.
+ * variant: 0 auto, 1 split (stats + apply, uses workspace),
+ *          16 + k: single-read cluster kernel with k CTAs per group
+ *          (k in {1, 2, 4, 8, 16}; group slice held in shared memory). */
+size_t b200_gn_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int dtype,
+                               int variant);
+int b200_gn_fwd(const void* x, const void* gamma, const void* beta, void* y, int dtype,
+                int affine_dtype, int64_t N, int64_t C, int64_t S, int64_t G, float eps,
+                int variant, void* workspace, size_t workspace_bytes, void* stream);
+
+/* GroupNorm statistics only: per (n, g) mean and rstd (fp32, [N*G] each).
+ * Used by the fused GroupNorm->SiLU->conv3d producer and by the T-sharded
+ * stack, which merges per-rank partial statistics.  Partial form: writes
+ * (count, mean, M2) triples per (n, g) of THIS tensor without finalising.
+ * No single reference counterpart: it is the first pass of
+ * src/cuda/group_norm.cu:55-90 exposed on its own. */
+size_t b200_gn_stats_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int dtype);
+int b200_gn_partial_stats(const void* x, float* partial_out, int dtype, int64_t N, int64_t C,
+                          int64_t S, int64_t G, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* Normalise + affine + optional SiLU, reading x NCDHW ([N, C, S]) and writing
+ * y either NCDHW (to_channels_last = 0) or channels-last [N, S, C]
+ * (to_channels_last = 1, the conv3d operand layout).  stats: (count, mean,
+ * M2) triples per (n, g) as produced by b200_gn_partial_stats (possibly merged
+ * across ranks).  Reference analogue: ck_norm_ops.group_norm_silu
+ * (amd_tuned_torch/ck_norm_ops.py:93-103) and the GN->SiLU prologue of
+ * conv_fusion_ops.group_norm_silu (amd_tuned_torch/conv_fusion_ops.py:245-353). */
+int b200_gn_apply(const void* x, const float* stats, const void* gamma, const void* beta,
+                  void* y, int dtype, int affine_dtype, int64_t N, int64_t C, int64_t S,
+                  int64_t G, float eps, int silu, int to_channels_last, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Depthwise conv1d forward, stride 1, dilation 1, zero padding:
+ *   y[b,c,l] = bias[c] + sum_k w[c,k] * x[b,c,l - pad + k],  l < L_out.
+ * Replaces _native_depthwise_conv1d.conv1d_forward(u, weight[C,K], bias[C],
+ * padding, is_bhl=True) (amd_tuned_torch/_vendor/flashfftconv_depthwise_conv1d/
+ * host.cpp:7-11 -> conv1d.h:56-83 -> conv1d_bhl.cu:100-140).  x: [B, C, L],
+ * w: [C, K], bias: [C] or NULL (w_dtype for both), y: [B, C, L_out]. */
+int b200_dwconv1d_fwd(const void* x, const void* w, const void* bias, void* y, int dtype,
+                      int w_dtype, int64_t B, int64_t C, int64_t L, int64_t K, int64_t pad,
+                      int64_t L_out, int variant, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Dense conv3d (groups = 1) as an implicit GEMM on tcgen05 tensor cores.
+ * Replaces _C.conv3d(input, weight, bias?, stride, padding, dilation)
+ * (src/main_rocm.cpp:798-854 -> run_conv3d_fp16 :514-548 ->
+ * src/cuda/generated/conv3d_fp16_bm256_bn128_bk32_s2.cu:84-380).
+ *
+ * b200_conv3d_pack_weight: w [Cout, Cin, KD, KH, KW] -> packed
+ *   [KD*KH*KW, Cout_pad, Cin_pad] (K-major GEMM B operand, zero padded).
+ * b200_conv3d_fwd: x [N, Cin, D, H, W] (x_channels_last = 0) or
+ *   [N, D, H, W, Cin] (x_channels_last = 1); y [N, Cout, Do, Ho, Wo] or
+ *   channels-last.  Scratch: the channels-last copy of x when x is NCDHW.
+ *   params: {stride d,h,w, pad d,h,w, dil d,h,w}. fp16/bf16 only. */
+size_t b200_conv3d_packed_weight_bytes(int64_t Cout, int64_t Cin, int64_t KD, int64_t KH,
+                                       int64_t KW);
+int b200_conv3d_pack_weight(const void* w, void* wp, int dtype, int64_t Cout, int64_t Cin,
+                            int64_t KD, int64_t KH, int64_t KW, void* stream);
+size_t b200_conv3d_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                                   int x_channels_last);
+int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, int dtype,
+                    int bias_dtype, int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                    int64_t Cout, int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,
+                    int x_channels_last, int y_channels_last, int variant, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* NCDHW -> channels-last copy ([N, C, S] -> [N, S, C]); conv3d operand layout. */
+int b200_to_channels_last(const void* x, void* y, int dtype, int64_t N, int64_t C, int64_t S,
+                          void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Long-filter depthwise conv1d through the FFT (cross-correlation with a
+ * zero-padded transform of length nfft, nfft >= L + 2*pad, nfft in
+ * 2^a 3^b 5^c).  Replaces fftconv_ops.fftconv1d_candidate -> fft_conv
+ * (amd_tuned_torch/fftconv_ops.py:889-942, :603-746) for groups == C.
+ * b200_fftconv1d_prepare: w [C, K] -> spectrum [C, nfft/2 + 1] complex fp32
+ *   (conjugated, i.e. ready to multiply).  b200_fftconv1d_fwd consumes it. */
+int b200_fft_supported_length(int64_t n);
+size_t b200_fftconv1d_spectrum_bytes(int64_t C, int64_t nfft);
+int b200_fftconv1d_prepare(const void* w, void* spectrum, int w_dtype, int64_t C, int64_t K,
+                           int64_t nfft, void* stream);
+int b200_fftconv1d_fwd(const void* x, const void* spectrum, const void* bias, void* y,
+                       int dtype, int bias_dtype, int64_t B, int64_t C, int64_t L,
+                       int64_t pad, int64_t L_out, int64_t nfft, void* stream);
+
+/* Dense (groups = 1) conv3d through the FFT for large kernels:
+ * rfft3(x) . conj(rfft3(w)) summed over Cin per frequency bin, irfft3,
+ * crop, + bias.  Replaces fftconv_ops.fft_conv3d (fftconv_ops.py:749-781)
+ * with complex_matmul (:480-543).  Transform extents (fd, fh, fw) are
+ * chosen by the caller (fw even).
+ * b200_fftconv3d_prepare: w [Cout, Cin, KD, KH, KW] -> conjugated spectrum,
+ *   layout [bins][Cout][Cin] complex fp32 with bins = fd*fh*(fw/2+1).
+ * Workspace: input spectrum [bins][N][Cin] + output spectrum [bins][N][Cout]
+ *   + a real staging volume. */
+size_t b200_fftconv3d_spectrum_bytes(int64_t Cout, int64_t Cin, int64_t fd, int64_t fh,
+                                     int64_t fw);
+int b200_fftconv3d_prepare(const void* w, void* spectrum, int w_dtype, int64_t Cout,
+                           int64_t Cin, int64_t KD, int64_t KH, int64_t KW, int64_t fd,
+                           int64_t fh, int64_t fw, void* workspace, size_t workspace_bytes,
+                           void* stream);
+size_t b200_fftconv3d_workspace_bytes(int64_t N, int64_t Cin, int64_t Cout, int64_t fd,
+                                      int64_t fh, int64_t fw);
+int b200_fftconv3d_fwd(const void* x, const void* spectrum, const void* bias, void* y,
+                       int dtype, int bias_dtype, int64_t N, int64_t Cin, int64_t D,
+                       int64_t H, int64_t W, int64_t Cout, int64_t KD, int64_t KH, int64_t KW,
+                       const int64_t* pad3, int64_t fd, int64_t fh, int64_t fw,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200CONV_H */

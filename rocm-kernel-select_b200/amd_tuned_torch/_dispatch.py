@@ -1,0 +1,392 @@
+"""enable()/disable() and the patched F.conv3d / F.group_norm / F.conv1d.
+
+Mirrors the reference's amd_tuned_torch/_dispatch.py for the conv/norm path:
+`_ORIGINALS` / `_install` / `_restore` (:662-672), `_grad_safe` (:528-553),
+`_usable` + the exact-type tensor guard (:643-659), `_patched_conv3d` with
+`_Conv3dFn` (:2029-2093), `_patched_group_norm` with `_GroupNormFn` and its
+torch-ops backward (:2118-2370), `enable`/`disable`/`is_enabled`
+(:2913-3050).  The candidate lists differ: every contested kernel is one of
+this project's sm_100a kernels, with stock torch kept last as kernel_select's
+verification reference.
+
+F.conv1d: the reference installs its conv1d wrapper at import from
+miopen_fallback.py (:492-519) outside enable()/disable().  Here it is part of
+enable()/disable() like the other two ops (so disable() restores it);
+`enable_conv1d_fallback()` / `disable_conv1d_fallback()` remain in
+conv1d_dispatch for callers that toggle it on its own.
+"""
+from __future__ import annotations
+
+import atexit
+import math
+import os
+import sys
+from collections import Counter
+from typing import Any, Callable
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib, fftconv_ops, kernel_select, ops
+
+_ORIGINALS: dict = {}
+_ENABLED = False
+
+_GROUPNORM_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+_CONV_TC_DTYPES = (torch.float16, torch.bfloat16)
+_FFTCONV_CONV_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+_CONV3D_KIND = "conv3d"
+
+_FFTCONV_CONV3D_ENABLED = os.environ.get("AMD_TUNED_TORCH_FFTCONV3D", "1") != "0"
+_FFTCONV_CONV3D_MIN_KERNEL = int(os.environ.get("AMD_TUNED_TORCH_FFTCONV3D_MIN_KERNEL", "6"))
+_FFTCONV_CONV3D_MIN_POSITIONS = int(
+    os.environ.get("AMD_TUNED_TORCH_FFTCONV3D_MIN_POSITIONS", "2048"))
+
+# ------------------------------------------------------- routing debug log ---
+_DEBUG = os.environ.get("AMD_TUNED_TORCH_DISPATCH_DEBUG", "0") not in ("", "0")
+_DEBUG_FILE = os.environ.get("AMD_TUNED_TORCH_DISPATCH_DEBUG_FILE")
+_route_counts: Counter = Counter()
+
+
+def _debug(op: str, route: str, why: str, **info: Any) -> None:
+    _route_counts[(op, route)] += 1
+    parts = [f"{k}={tuple(v.shape) if isinstance(v, torch.Tensor) else v}" for k, v in info.items()]
+    line = f"[amd_tuned_torch] {op} -> {route}: {why} {' '.join(parts)}\n"
+    if _DEBUG_FILE:
+        with open(_DEBUG_FILE, "a") as f:
+            f.write(line)
+    else:
+        sys.stderr.write(line)
+
+
+def route_counts() -> dict:
+    return dict(_route_counts)
+
+
+@atexit.register
+def _report() -> None:
+    if _DEBUG and _route_counts:
+        sys.stderr.write("[amd_tuned_torch] routes: " + ", ".join(
+            f"{op}/{r}={n}" for (op, r), n in sorted(_route_counts.items())) + "\n")
+
+
+# ----------------------------------------------------------- eligibility ---
+_PLAIN_TENSOR_TYPES = (torch.Tensor, torch.nn.Parameter)
+
+
+def _is_plain_tensor(t: Any) -> bool:
+    """Exact type match: Tensor subclasses (quantized, DTensor, FakeTensor)
+    have their own dispatch and go to stock."""
+    return type(t) in _PLAIN_TENSOR_TYPES
+
+
+def _usable(*tensors: Any, dtypes: tuple = _GROUPNORM_DTYPES) -> bool:
+    for t in tensors:
+        if not isinstance(t, torch.Tensor):
+            continue
+        if not _is_plain_tensor(t):
+            return False
+        if not t.is_cuda or t.dtype not in dtypes:
+            return False
+    return True
+
+
+def _grad_safe(*tensors: Any) -> bool:
+    """True when nothing will backprop through the call (the accelerated
+    forward can be called directly); False routes through the autograd
+    wrapper instead of declining."""
+    if torch.is_inference_mode_enabled() or not torch.is_grad_enabled():
+        return True
+    return not any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors)
+
+
+def _install(target: Any, name: str, wrapper: Callable) -> None:
+    key = (target, name)
+    if key not in _ORIGINALS:
+        _ORIGINALS[key] = getattr(target, name)
+    setattr(target, name, wrapper)
+
+
+def _restore(target: Any, name: str) -> None:
+    original = _ORIGINALS.pop((target, name), None)
+    if original is not None:
+        setattr(target, name, original)
+
+
+def _triple(v):
+    if isinstance(v, int):
+        return (v, v, v)
+    v = tuple(v)
+    return v if len(v) == 3 else (v[0],) * 3
+
+
+def _is_compiling() -> bool:
+    return torch.compiler.is_compiling()
+
+
+# ---------------------------------------------------------------- conv3d ---
+def _conv3d_tc_thunk(input, weight, bias, stride, padding, dilation, variant=0):
+    def run():
+        if isinstance(padding, str):
+            return None
+        x, cl = input, False
+        if not input.is_contiguous() and input.is_contiguous(memory_format=torch.channels_last_3d):
+            x, cl = input.permute(0, 2, 3, 4, 1), True
+        elif not input.is_contiguous():
+            return None
+        out = ops.conv3d(x, weight, bias, _triple(stride), _triple(padding), _triple(dilation),
+                         variant=variant, x_channels_last=cl, out_channels_last=cl)
+        if out is None:
+            return None
+        return out.permute(0, 4, 1, 2, 3) if cl else out
+    return run
+
+
+def _fftconv3d_candidate(input, weight, bias, stride, padding, dilation, groups):
+    if not _FFTCONV_CONV3D_ENABLED or input.dim() != 5 or weight.dim() != 5:
+        return None
+    if input.shape[0] * math.prod(input.shape[2:]) < _FFTCONV_CONV3D_MIN_POSITIONS:
+        return None
+    if isinstance(padding, str) or min(weight.shape[2:]) < _FFTCONV_CONV3D_MIN_KERNEL:
+        return None
+    if not _usable(input, weight, dtypes=_FFTCONV_CONV_DTYPES):
+        return None
+
+    def thunk():
+        try:
+            return fftconv_ops.fft_conv3d(input, weight, bias, padding=padding, stride=stride,
+                                          dilation=dilation, groups=groups)
+        except (RuntimeError, ValueError, TypeError) as exc:
+            if isinstance(exc, _lib.NativeError):
+                raise
+            return None
+    return ("fftconv", thunk)
+
+
+def _conv3d_candidates(input, weight, bias, stride, padding, dilation, groups):
+    orig = _ORIGINALS[(F, "conv3d")]
+    cands = []
+    if _usable(input, weight, bias, dtypes=_CONV_TC_DTYPES) and _lib.available():
+        cands.append(("tcgen05", _conv3d_tc_thunk(input, weight, bias, stride, padding, dilation)))
+    fft = _fftconv3d_candidate(input, weight, bias, stride, padding, dilation, groups)
+    if fft is not None:
+        cands.append(fft)
+    cands.append(("stock", lambda: orig(input, weight, bias, stride, padding, dilation, groups)))
+    return cands, fft
+
+
+def _conv3d_accelerated_forward(input, weight, bias, stride, padding, dilation, groups):
+    orig = _ORIGINALS[(F, "conv3d")]
+    if groups != 1 or not _usable(input, weight, bias, dtypes=_FFTCONV_CONV_DTYPES):
+        if _DEBUG:
+            _debug("conv3d", "stock", "groups != 1 or not a plain CUDA fp tensor", input=input)
+        return orig(input, weight, bias, stride, padding, dilation, groups)
+    if kernel_select.enabled():
+        won = kernel_select.cached(_CONV3D_KIND, input, weight, stride, padding, dilation)
+        if won == "stock":
+            if _DEBUG:
+                _debug("conv3d", "stock", "cached winner", input=input)
+            return orig(input, weight, bias, stride, padding, dilation, groups)
+        if won == "tcgen05":
+            out = _conv3d_tc_thunk(input, weight, bias, stride, padding, dilation)()
+            if out is not None:
+                if _DEBUG:
+                    _debug("conv3d", "tcgen05", "cached winner", input=input)
+                return out
+        cands, fft = _conv3d_candidates(input, weight, bias, stride, padding, dilation, groups)
+        if _DEBUG:
+            _debug("conv3d", "contest", "first call for this shape", input=input,
+                   candidates=",".join(n for n, _ in cands))
+        out = kernel_select.pick(_CONV3D_KIND, input, weight, stride, padding, dilation, cands,
+                                 tolerance=fftconv_ops.fftconv_tolerance(input.dtype)
+                                 if fft is not None else None)
+        if out is not None:
+            return out
+    # kernel_select off: fixed order, own kernels first.
+    cands, _ = _conv3d_candidates(input, weight, bias, stride, padding, dilation, groups)
+    for name, thunk in cands:
+        out = thunk()
+        if out is not None:
+            if _DEBUG:
+                _debug("conv3d", name, "fixed order (kernel_select off)", input=input)
+            return out
+    return orig(input, weight, bias, stride, padding, dilation, groups)
+
+
+class _Conv3dFn(torch.autograd.Function):
+    """Accelerated forward, stock aten.convolution_backward backward (the
+    reference's choice too, _dispatch.py:2029-2075)."""
+
+    @staticmethod
+    def forward(ctx, input, weight, bias, stride, padding, dilation, groups):
+        ctx.save_for_backward(input, weight)
+        ctx.bias_sizes = [bias.shape[0]] if bias is not None else None
+        ctx.stride, ctx.padding, ctx.dilation, ctx.groups = stride, padding, dilation, groups
+        return _conv3d_accelerated_forward(input, weight, bias, stride, padding, dilation, groups)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        input, weight = ctx.saved_tensors
+        needs = [bool(ctx.needs_input_grad[0]), bool(ctx.needs_input_grad[1]),
+                 ctx.bias_sizes is not None and bool(ctx.needs_input_grad[2])]
+        if not any(needs):
+            return None, None, None, None, None, None, None
+        padding = ctx.padding
+        if isinstance(padding, str):
+            k = weight.shape[2:]
+            padding = tuple((d * (kk - 1)) // 2 for d, kk in zip(_triple(ctx.dilation), k))
+        gi, gw, gb = torch.ops.aten.convolution_backward(
+            grad_output.contiguous(), input, weight, ctx.bias_sizes, list(_triple(ctx.stride)),
+            list(_triple(padding)), list(_triple(ctx.dilation)), False, [0, 0, 0], ctx.groups,
+            needs)
+        return gi, gw, gb, None, None, None, None
+
+
+def _patched_conv3d(input, weight, bias=None, stride=1, padding=0, dilation=1, groups=1):
+    if _grad_safe(input, weight, bias):
+        return _conv3d_accelerated_forward(input, weight, bias, stride, padding, dilation, groups)
+    if groups != 1:
+        return _ORIGINALS[(F, "conv3d")](input, weight, bias, stride, padding, dilation, groups)
+    return _Conv3dFn.apply(input, weight, bias, stride, padding, dilation, groups)
+
+
+# ------------------------------------------------------------ group_norm ---
+def _gn_thunk(input, num_groups, weight, bias, eps, variant):
+    def run():
+        return ops.group_norm(input, num_groups, weight, bias, eps, variant=variant)
+    return run
+
+
+def _group_norm_candidates(input, num_groups, weight, bias, eps):
+    orig = _ORIGINALS[(F, "group_norm")]
+    cands = []
+    if input.is_contiguous() and _lib.available():
+        cands.append(("native", _gn_thunk(input, num_groups, weight, bias, eps, ops.GN_AUTO)))
+        for k in (4, 8, 16):
+            cands.append((f"native_c{k}", _gn_thunk(input, num_groups, weight, bias, eps,
+                                                    ops.gn_cluster_variant(k))))
+        cands.append(("native_split", _gn_thunk(input, num_groups, weight, bias, eps,
+                                                ops.GN_SPLIT)))
+    cands.append(("stock", lambda: orig(input, num_groups, weight, bias, eps)))
+    return cands
+
+
+def _group_norm_accelerated_forward(input, num_groups, weight, bias, eps):
+    orig = _ORIGINALS[(F, "group_norm")]
+    if (input.dim() < 2 or input.shape[1] % num_groups != 0 or not input.is_contiguous()
+            or not _usable(input, weight, bias, dtypes=_GROUPNORM_DTYPES)):
+        if _DEBUG:
+            _debug("group_norm", "stock", "layout/dtype outside this tier", input=input)
+        return orig(input, num_groups, weight, bias, eps)
+    if kernel_select.enabled():
+        key = (input.dtype, tuple(input.shape), int(num_groups), False)
+        won = kernel_select.cached_key("group_norm", key)
+        if won == "stock":
+            return orig(input, num_groups, weight, bias, eps)
+        cands = _group_norm_candidates(input, num_groups, weight, bias, eps)
+        if won is not None:
+            for name, thunk in cands:
+                if name == won:
+                    out = thunk()
+                    if out is not None:
+                        if _DEBUG:
+                            _debug("group_norm", name, "cached winner", input=input)
+                        return out
+        out = kernel_select.pick_key("group_norm", key, cands)
+        if out is not None:
+            return out
+    out = ops.group_norm(input, num_groups, weight, bias, eps) if _lib.available() else None
+    if out is not None:
+        return out
+    return orig(input, num_groups, weight, bias, eps)
+
+
+def _group_norm_backward(grad_output, input, num_groups, weight, eps, needs, bias_dtype=None):
+    """GroupNorm's derivative in torch ops, each gradient in its own input's
+    dtype; reductions accumulate in fp32 for fp16/bf16 (an fp16 sum over a
+    large group overflows).  Same math as the reference's
+    _group_norm_backward (_dispatch.py:2212-2302)."""
+    N, C = input.shape[0], input.shape[1]
+    M = C // num_groups
+    dtype = input.dtype
+    acc = torch.float32 if dtype in (torch.float16, torch.bfloat16) else dtype
+    x = input.reshape(N, num_groups, M, -1)
+    dy = grad_output.reshape(N, num_groups, M, -1)
+    need_x, need_w, need_b = needs
+    gx = gw = gb = None
+    if need_b:
+        gb = dy.sum(dim=(0, 3), dtype=acc).reshape(C).to(bias_dtype or dtype)
+    if not (need_x or need_w):
+        return gx, gw, gb
+    mean = x.mean(dim=(2, 3), keepdim=True, dtype=acc)
+    xc = x - mean.to(dtype)
+    var = xc.square().mean(dim=(2, 3), keepdim=True, dtype=acc)
+    rstd = (var + eps).rsqrt().to(dtype)
+    xhat = xc * rstd
+    if need_w and weight is not None:
+        gw = (dy * xhat).sum(dim=(0, 3), dtype=acc).reshape(C).to(weight.dtype)
+    if need_x:
+        wdy = dy if weight is None else dy * weight.reshape(1, num_groups, M, 1).to(dtype)
+        c1 = wdy.mean(dim=(2, 3), keepdim=True, dtype=acc).to(dtype)
+        c2 = (wdy * xhat).mean(dim=(2, 3), keepdim=True, dtype=acc).to(dtype)
+        gx = ((wdy - c1 - xhat * c2) * rstd).reshape(input.shape)
+    return gx, gw, gb
+
+
+class _GroupNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, input, weight, bias, num_groups, eps):
+        ctx.save_for_backward(input, weight)
+        ctx.num_groups, ctx.eps = num_groups, eps
+        ctx.has_bias = bias is not None
+        ctx.bias_dtype = bias.dtype if bias is not None else None
+        return _group_norm_accelerated_forward(input, num_groups, weight, bias, eps)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        input, weight = ctx.saved_tensors
+        needs = (ctx.needs_input_grad[0], weight is not None and ctx.needs_input_grad[1],
+                 ctx.has_bias and ctx.needs_input_grad[2])
+        return _group_norm_backward(grad_output.contiguous(), input, ctx.num_groups, weight,
+                                    ctx.eps, needs, bias_dtype=ctx.bias_dtype) + (None, None)
+
+
+def _patched_group_norm(input, num_groups, weight=None, bias=None, eps=1e-5):
+    if _grad_safe(input, weight, bias):
+        return _group_norm_accelerated_forward(input, num_groups, weight, bias, eps)
+    return _GroupNormFn.apply(input, weight, bias, num_groups, eps)
+
+
+# ------------------------------------------------------------ enable etc ---
+def enable() -> None:
+    """Patch F.conv1d / F.conv3d / F.group_norm to route eligible calls here."""
+    global _ENABLED
+    if _ENABLED:
+        return
+    from . import conv1d_dispatch
+    _install(F, "group_norm", _patched_group_norm)
+    _install(F, "conv3d", _patched_conv3d)
+    if not getattr(F.conv1d, "_amd_tuned_torch_wrapper", False):
+        _install(F, "conv1d", conv1d_dispatch.make_wrapper(lambda: _ORIGINALS[(F, "conv1d")]))
+    _ENABLED = True
+
+
+def disable() -> None:
+    """Restore every patched function to stock PyTorch."""
+    global _ENABLED
+    for target, name in list(_ORIGINALS.keys()):
+        _restore(target, name)
+    _ENABLED = False
+
+
+def is_enabled() -> bool:
+    return _ENABLED
+
+
+__all__ = [
+    "enable", "disable", "is_enabled", "route_counts", "_ORIGINALS", "_install", "_restore",
+    "_grad_safe", "_usable", "_is_plain_tensor", "_patched_conv3d", "_patched_group_norm",
+    "_Conv3dFn", "_GroupNormFn", "_group_norm_backward", "_conv3d_accelerated_forward",
+    "_group_norm_accelerated_forward", "_GROUPNORM_DTYPES", "_CONV_TC_DTYPES",
+    "_FFTCONV_CONV_DTYPES",
+]

@@ -1,0 +1,523 @@
+// Dense conv3d (groups = 1, stride 1, any padding/dilation) as an implicit
+// GEMM on the sm_100a tensor cores.
+//
+// Reference role: custom_conv3d_forward -> run_conv3d_fp16 ->
+// conv3d_fp16_kernel_bm256_bn128_bk32_s2 (src/main_rocm.cpp:798-854, :514-548;
+// src/cuda/generated/conv3d_fp16_bm256_bn128_bk32_s2.cu:84-380), an rocWMMA
+// implicit GEMM with M = N*Do*Ho*Wo, N = Cout, K = Cin*KD*KH*KW, fp32
+// accumulation and a bias epilogue.  Same GEMM view here, built for Blackwell:
+//
+//  * Operand A comes from a channels-last copy of the input ([N, D, H, W, C],
+//    made by b200_to_channels_last or the fused GroupNorm producer).  For
+//    every filter tap (kd, kh, kw) and 64-channel chunk, ONE TMA tiled load
+//    fetches the box {64 channels, BW, BH, 1, 1} at the tap-shifted output
+//    coordinates.  The innermost coordinate is the channel offset (a multiple
+//    of 64, so always 16-byte aligned); the spatial shift lands on W/H/D,
+//    which carry no alignment rule, and the padding is the TMA zero fill of
+//    out-of-range coordinates.  The 128 rows of the box are the 128 output
+//    positions of the tile, each a 128-byte K-major row, SWIZZLE_128B.
+//  * Operand B is the weight packed as [tap][Cout][Cin_pad] (K-major), one
+//    TMA box {64, BN, 1} per k-block.
+//  * tcgen05.mma (kind::f16, M = 128, N = BN, K = 16) issued by one thread,
+//    fp32 accumulators in TMEM, double-buffered so the epilogue of tile i
+//    overlaps the MMAs of tile i + 1 in a persistent CTA.
+//  * Warp roles (6 warps): 0 = TMA producer, 1 = MMA issuer (+ TMEM
+//    allocation), 2-5 = epilogue (tcgen05.ld -> + bias -> fp16/bf16 store,
+//    NCDHW or channels-last).
+//  * Every mbarrier wait is bounded (kWaitLimitNs); running out records a
+//    fault code and unwinds: the MMA thread drains its in-flight MMAs through
+//    a final commit before TMEM is released.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+#include <type_traits>
+
+#include "sm100_ptx.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kConvThreads = 192;  // 6 warps
+constexpr int kBM = 128;
+constexpr int kBK = 64;            // channels per k-block (one 128-byte swizzle row)
+constexpr int kABytes = kBM * kBK * 2;
+
+struct ConvParams {
+  int Do, Ho, Wo, Cout;
+  int KH, KW;
+  int pd, ph, pw, dd, dh, dw;
+  int BW, BH;
+  int tiles_w, tiles_h, tiles_n, num_tiles;
+  int cchunks, kblocks;
+  void* y;
+  const void* bias;
+  int bias_dt;
+  int y_cl;
+  int* flags;
+};
+
+struct TileCoord {
+  int n, od, oh0, ow0, n0;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(int t, const ConvParams& p, int BN) {
+  TileCoord c;
+  const int nt = t % p.tiles_n;
+  t /= p.tiles_n;
+  const int tw = t % p.tiles_w;
+  t /= p.tiles_w;
+  const int th = t % p.tiles_h;
+  t /= p.tiles_h;
+  c.od = t % p.Do;
+  c.n = t / p.Do;
+  c.oh0 = th * p.BH;
+  c.ow0 = tw * p.BW;
+  c.n0 = nt * BN;
+  return c;
+}
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kConvThreads, 1)
+conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+                 const ConvParams p) {
+  constexpr int kBBytes = BN * kBK * 2;
+  constexpr int kStage = kABytes + kBBytes;
+  constexpr uint32_t kIdesc = umma_idesc_f16(sizeof(T) == 2 && std::is_same<T, __half>::value ? 0 : 1, kBM, BN);
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStage);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;      // [2]
+  uint64_t* drain = tempty + 2;      // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmx);
+    prefetch_tmap(&tmw);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const int taps_hw = p.KH * p.KW;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        const TileCoord tc = decode_tile(t, p, BN);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          const int tap = kb / p.cchunks, cc = kb - tap * p.cchunks;
+          const int kd = tap / taps_hw, r = tap - kd * taps_hw;
+          const int kh = r / p.KW, kw = r - kh * p.KW;
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, p.flags, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], kStage);
+          tma_load_5d(sA + stage * kABytes, &tmx, &full[stage], cc * kBK,
+                      tc.ow0 - p.pw + kw * p.dw, tc.oh0 - p.ph + kh * p.dh,
+                      tc.od - p.pd + kd * p.dd, tc.n);
+          tma_load_3d(sB + stage * kBBytes, &tmw, &full[stage], cc * kBK, tc.n0, tap);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the loads already issued land before shared memory goes away.
+        const int last = (stage + STAGES - 1) % STAGES;
+        mbar_wait_bounded(&full[last], (stage == 0 ? phase ^ 1u : phase), nullptr, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t aphase = static_cast<uint32_t>(it >> 1) & 1u;
+        if (!mbar_wait_bounded(&tempty[acc], aphase ^ 1u, abort, p.flags, 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort, p.flags, 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * kABytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // +32 bytes along K inside the swizzled 128-byte row = +2 in the
+            // descriptor's address field.
+            umma_f16_ss(d_tmem, adesc + static_cast<uint64_t>(2 * k),
+                        bdesc + static_cast<uint64_t>(2 * k), kIdesc,
+                        (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+      // Drain: every MMA issued above has completed once `drain` flips.
+      umma_commit(drain);
+      mbar_wait_bounded(drain, 0, nullptr, nullptr, 0);
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row = quarter * 32 + lane;
+    int it = 0;
+    T* y = static_cast<T*>(p.y);
+    const int64_t plane = static_cast<int64_t>(p.Ho) * p.Wo;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t aphase = static_cast<uint32_t>(it >> 1) & 1u;
+      if (!mbar_wait_bounded(&tfull[acc], aphase, abort, p.flags, 1)) break;
+      tc_fence_after();
+      const TileCoord tc = decode_tile(t, p, BN);
+      const int oh = tc.oh0 + row / p.BW, ow = tc.ow0 + row % p.BW;
+      const bool valid = oh < p.Ho && ow < p.Wo;
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int64_t pos = (static_cast<int64_t>(tc.od) * p.Ho + oh) * p.Wo + ow;
+#pragma unroll 1
+      for (int j0 = 0; j0 < BN; j0 += 32) {
+        float v0[16], v1[16];
+        tmem_ld16(taddr + j0, v0);
+        tmem_ld16(taddr + j0 + 16, v1);
+        tmem_ld_wait();
+        if (valid) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int co = tc.n0 + j0 + j;
+            if (co < p.Cout) {
+              float v = j < 16 ? v0[j] : v1[j - 16];
+              if (p.bias) v += load_param(p.bias, p.bias_dt, co);
+              int64_t off;
+              if (p.y_cl)
+                off = (static_cast<int64_t>(tc.n) * p.Do * plane + pos) * p.Cout + co;
+              else
+                off = ((static_cast<int64_t>(tc.n) * p.Cout + co) * p.Do) * plane + pos;
+              y[off] = from_f32<T>(v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// --------------------------------------------------------- weight packing ---
+// w [Cout][Cin][taps] -> wp [taps][Cout][Cin_pad], zero beyond Cin.
+template <typename T>
+__global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ wp, int64_t Cout,
+                                   int64_t Cin, int64_t Cin_pad, int64_t taps) {
+  const int64_t total = taps * Cout * Cin_pad;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t ci = i % Cin_pad;
+    const int64_t co = (i / Cin_pad) % Cout;
+    const int64_t tap = i / (Cin_pad * Cout);
+    wp[i] = ci < Cin ? w[(co * Cin + ci) * taps + tap] : from_f32<T>(0.f);
+  }
+}
+
+// ------------------------------------------------------ NCDHW -> N[S]C ---
+// 64 x 64 tiles of 16-bit elements through shared memory.
+template <typename T>
+__global__ void __launch_bounds__(256)
+to_cl_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t C, int64_t S) {
+  __shared__ T tile[64][66];
+  const int64_t n = blockIdx.z;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 64;
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  for (int cc = ty; cc < 64; cc += 4) {
+    const int64_t c = c0 + cc, q = p0 + tx;
+    tile[cc][tx] = (c < C && q < S) ? x[(n * C + c) * S + q] : from_f32<T>(0.f);
+  }
+  __syncthreads();
+  for (int pp = ty; pp < 64; pp += 4) {
+    const int64_t q = p0 + pp, c = c0 + tx;
+    if (q < S && c < C) y[(n * S + q) * C + c] = tile[tx][pp];
+  }
+}
+
+// ------------------------------------------------------------ host side ---
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+template <typename T, int BN, int STAGES>
+int launch_conv(const CUtensorMap& tmx, const CUtensorMap& tmw, const ConvParams& prm,
+                cudaStream_t stream) {
+  constexpr int kStage = kABytes + BN * kBK * 2;
+  constexpr size_t smem = static_cast<size_t>(STAGES) * kStage + 1024 + 256;
+  auto kern = conv3d_tc_kernel<T, BN, STAGES>;
+  B200_CUDA_CHECK(
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int grid = std::min(prm.num_tiles, sm_count());
+  kern<<<grid, kConvThreads, smem, stream>>>(tmx, tmw, prm);
+  B200_LAUNCH_CHECK("conv3d_tc_kernel");
+  return B200_OK;
+}
+
+int pick_bn(int64_t Cout, int code) {
+  if (code == 1) return 64;
+  if (code == 2) return 128;
+  if (code == 3) return 256;
+  if (Cout <= 64) return 64;
+  if (Cout <= 128) return 128;
+  return 256;
+}
+
+template <typename T>
+int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int bias_dt,
+                 int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int64_t Cout,
+                 int64_t KD, int64_t KH, int64_t KW, const int64_t* prm9, int x_cl, int y_cl,
+                 int variant, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  const int64_t sd = prm9[0], sh = prm9[1], sw = prm9[2];
+  const int64_t pd = prm9[3], ph = prm9[4], pw = prm9[5];
+  const int64_t dd = prm9[6], dh = prm9[7], dw = prm9[8];
+  if (sd != 1 || sh != 1 || sw != 1) return fail_unsupported("conv3d tensor-core path: stride != 1");
+  if (pd < 0 || ph < 0 || pw < 0 || dd < 1 || dh < 1 || dw < 1) return fail_arg("bad padding/dilation");
+  if (Cin % 8 != 0) return fail_unsupported("conv3d tensor-core path: Cin % 8 != 0");
+  const int64_t Do = D + 2 * pd - dd * (KD - 1);
+  const int64_t Ho = H + 2 * ph - dh * (KH - 1);
+  const int64_t Wo = W + 2 * pw - dw * (KW - 1);
+  if (Do <= 0 || Ho <= 0 || Wo <= 0) return fail_arg("conv3d output size must be positive");
+  const int64_t lim = 1LL << 30;
+  if (N >= 65536 || D >= lim || H >= lim || W >= lim || Cout >= lim || Cin >= lim)
+    return fail_unsupported("conv3d size out of range");
+  auto encode = get_encode_fn();
+  if (!encode) return fail_unsupported("cuTensorMapEncodeTiled unavailable");
+
+  const void* xcl = x;
+  if (!x_cl) {
+    const size_t need = static_cast<size_t>(N * D * H * W * Cin) * sizeof(T);
+    if (ws == nullptr || ws_bytes < need) return fail_arg("conv3d workspace too small");
+    const int64_t S = D * H * W;
+    dim3 grid(static_cast<unsigned>((S + 63) / 64), static_cast<unsigned>((Cin + 63) / 64),
+              static_cast<unsigned>(N));
+    if ((S + 63) / 64 > 0x7fffffffLL || (Cin + 63) / 64 > 65535)
+      return fail_unsupported("transpose grid too large");
+    to_cl_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
+    B200_LAUNCH_CHECK("to_cl_kernel");
+    xcl = ws;
+  }
+  if (!aligned16(xcl) || !aligned16(wp)) return fail_unsupported("operands not 16-byte aligned");
+
+  const int BN = pick_bn(Cout, variant & 0xF);
+  int BW;
+  const int bw_code = (variant >> 4) & 0xF;
+  if (bw_code) {
+    BW = 1 << bw_code;
+    if (BW > 128) return fail_arg("conv3d tile width code");
+  } else {
+    BW = 8;
+    while (BW < Wo && BW < 128) BW *= 2;
+  }
+  const int BH = kBM / BW;
+  const int64_t Cin_pad = (Cin + kBK - 1) / kBK * kBK;
+  const int64_t taps = KD * KH * KW;
+
+  CUtensorMap tmx, tmw;
+  const CUtensorMapDataType dt =
+      std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  {
+    cuuint64_t dims[5] = {(cuuint64_t)Cin, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)N};
+    cuuint64_t strides[4] = {(cuuint64_t)(Cin * 2), (cuuint64_t)(W * Cin * 2),
+                             (cuuint64_t)(H * W * Cin * 2), (cuuint64_t)(D * H * W * Cin * 2)};
+    cuuint32_t box[5] = {(cuuint32_t)kBK, (cuuint32_t)BW, (cuuint32_t)BH, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = encode(&tmx, dt, 5, const_cast<void*>(xcl), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail_unsupported("input tensor map rejected");
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)Cin_pad, (cuuint64_t)Cout, (cuuint64_t)taps};
+    cuuint64_t strides[2] = {(cuuint64_t)(Cin_pad * 2), (cuuint64_t)(Cout * Cin_pad * 2)};
+    cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)BN, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = encode(&tmw, dt, 3, const_cast<void*>(wp), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail_unsupported("weight tensor map rejected");
+  }
+
+  ConvParams prm;
+  prm.Do = (int)Do;
+  prm.Ho = (int)Ho;
+  prm.Wo = (int)Wo;
+  prm.Cout = (int)Cout;
+  prm.KH = (int)KH;
+  prm.KW = (int)KW;
+  prm.pd = (int)pd;
+  prm.ph = (int)ph;
+  prm.pw = (int)pw;
+  prm.dd = (int)dd;
+  prm.dh = (int)dh;
+  prm.dw = (int)dw;
+  prm.BW = BW;
+  prm.BH = BH;
+  prm.tiles_w = (int)((Wo + BW - 1) / BW);
+  prm.tiles_h = (int)((Ho + BH - 1) / BH);
+  prm.tiles_n = (int)((Cout + BN - 1) / BN);
+  const int64_t nt = N * Do * prm.tiles_h * prm.tiles_w * prm.tiles_n;
+  if (nt > 0x7fffffffLL) return fail_unsupported("too many tiles");
+  prm.num_tiles = (int)nt;
+  prm.cchunks = (int)(Cin_pad / kBK);
+  prm.kblocks = (int)(taps * prm.cchunks);
+  prm.y = y;
+  prm.bias = bias;
+  prm.bias_dt = bias_dt;
+  prm.y_cl = y_cl;
+  prm.flags = device_flags_ptr();
+  if (BN == 64) return launch_conv<T, 64, 8>(tmx, tmw, prm, stream);
+  if (BN == 128) return launch_conv<T, 128, 6>(tmx, tmw, prm, stream);
+  return launch_conv<T, 256, 4>(tmx, tmw, prm, stream);
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+size_t b200_conv3d_packed_weight_bytes(int64_t Cout, int64_t Cin, int64_t KD, int64_t KH,
+                                       int64_t KW) {
+  const int64_t Cin_pad = (Cin + kBK - 1) / kBK * kBK;
+  return static_cast<size_t>(KD * KH * KW * Cout * Cin_pad) * 2;
+}
+
+int b200_conv3d_pack_weight(const void* w, void* wp, int dtype, int64_t Cout, int64_t Cin,
+                            int64_t KD, int64_t KH, int64_t KW, void* stream) {
+  if (!w || !wp) return fail_arg("w/wp is NULL");
+  if (dtype != B200_DTYPE_F16 && dtype != B200_DTYPE_BF16)
+    return fail_unsupported("conv3d tensor-core path: fp16/bf16 only");
+  if (Cout <= 0 || Cin <= 0 || KD <= 0 || KH <= 0 || KW <= 0) return fail_arg("bad size");
+  const int64_t Cin_pad = (Cin + kBK - 1) / kBK * kBK;
+  const int64_t taps = KD * KH * KW;
+  const int64_t total = taps * Cout * Cin_pad;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 65536));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B200_DTYPE_F16)
+    pack_weight_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(w),
+                                                    static_cast<__half*>(wp), Cout, Cin, Cin_pad, taps);
+  else
+    pack_weight_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(wp), Cout, Cin, Cin_pad, taps);
+  B200_LAUNCH_CHECK("pack_weight_kernel");
+  return B200_OK;
+}
+
+size_t b200_conv3d_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                                   int x_channels_last) {
+  if (x_channels_last) return 0;
+  return static_cast<size_t>(N * Cin * D * H * W) * 2;
+}
+
+int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, int dtype,
+                    int bias_dtype, int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                    int64_t Cout, int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,
+                    int x_channels_last, int y_channels_last, int variant, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (!x || !wp || !y || !params9) return fail_arg("NULL pointer");
+  if (dtype != B200_DTYPE_F16 && dtype != B200_DTYPE_BF16)
+    return fail_unsupported("conv3d tensor-core path: fp16/bf16 only");
+  if (bias && !dtype_ok(bias_dtype)) return fail_arg("bad bias dtype");
+  if (N <= 0 || Cin <= 0 || D <= 0 || H <= 0 || W <= 0 || Cout <= 0 || KD <= 0 || KH <= 0 ||
+      KW <= 0)
+    return fail_arg("bad size");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B200_DTYPE_F16)
+    return conv3d_typed<__half>(x, wp, bias, y, bias_dtype, N, Cin, D, H, W, Cout, KD, KH, KW,
+                                params9, x_channels_last, y_channels_last, variant, workspace,
+                                workspace_bytes, s);
+  return conv3d_typed<__nv_bfloat16>(x, wp, bias, y, bias_dtype, N, Cin, D, H, W, Cout, KD, KH,
+                                     KW, params9, x_channels_last, y_channels_last, variant,
+                                     workspace, workspace_bytes, s);
+}
+
+int b200_to_channels_last(const void* x, void* y, int dtype, int64_t N, int64_t C, int64_t S,
+                          void* stream) {
+  if (!x || !y) return fail_arg("NULL pointer");
+  if (N <= 0 || C <= 0 || S <= 0) return fail_arg("bad size");
+  if ((S + 63) / 64 > 0x7fffffffLL || (C + 63) / 64 > 65535 || N > 65535)
+    return fail_unsupported("transpose grid too large");
+  dim3 grid(static_cast<unsigned>((S + 63) / 64), static_cast<unsigned>((C + 63) / 64),
+            static_cast<unsigned>(N));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B200_DTYPE_F32)
+    to_cl_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), static_cast<float*>(y), C, S);
+  else if (dtype == B200_DTYPE_F16)
+    to_cl_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y), C, S);
+  else if (dtype == B200_DTYPE_BF16)
+    to_cl_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                    static_cast<__nv_bfloat16*>(y), C, S);
+  else
+    return fail_arg("bad dtype");
+  B200_LAUNCH_CHECK("to_cl_kernel");
+  return B200_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,626 @@
+// GroupNorm forward for sm_100a.
+//
+// Semantics follow the reference kernel group_norm_kernel
+// (src/cuda/group_norm.cu:40-104): one (n, g) group = Cg = C/G consecutive
+// channels x S spatial elements, contiguous in an NCHW/NCDHW tensor; biased
+// variance, eps inside the square root, per-channel affine; fp32 statistics.
+// The reference computes var = E[x^2] - mean^2 in two strided passes over
+// global memory with one 256-thread block per group.  Here:
+//
+//  * gn_cluster_kernel -- single HBM read.  A thread-block cluster of k CTAs
+//    owns one group; each CTA streams its slice of the group into shared
+//    memory with 16-byte loads while summing it, the cluster exchanges
+//    partial sums through distributed shared memory (DSMEM), each CTA then
+//    computes sum((x - mean)^2) from shared memory (exact two-pass variance,
+//    no E[x^2] - mean^2 cancellation), exchanges again, and writes the
+//    normalised slice back with 16-byte streaming stores.  HBM traffic is
+//    the algorithmic minimum: one read + one write.
+//  * gn_partial_stats_kernel + gn_apply_kernel -- the general fallback for
+//    groups too large for a cluster's shared memory: per-chunk shifted sums
+//    merged with Chan's formula, then a normalising pass (one extra read).
+//    The same pair serves the fused GroupNorm -> SiLU -> channels-last
+//    producer of the conv3d stack, and the cross-rank statistics merge of
+//    the T-sharded stack (partials are (count, mean, M2) triples).
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace b200 {
+namespace {
+
+constexpr int kGnThreads = 512;
+constexpr int kGnUnroll = 4;
+
+__device__ __forceinline__ float silu(float v) { return v / (1.f + __expf(-v)); }
+
+// ------------------------------------------------------------ cluster ----
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kGnThreads)
+gn_cluster_kernel(const T* __restrict__ x, const void* __restrict__ gamma,
+                  const void* __restrict__ beta, T* __restrict__ y, int affine_dt, int64_t S,
+                  int G, int Cg, float eps, int slice, int csize) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float scratch[33];
+  __shared__ float part[2];   // this CTA's partial sum and partial M2 (read by peers)
+  __shared__ float stat[2];   // mean, rstd
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int64_t ng = blockIdx.x / csize;
+  const int g = static_cast<int>(ng % G);
+  const int64_t M = static_cast<int64_t>(Cg) * S;
+  const int64_t beg = static_cast<int64_t>(rank) * slice;
+  const int cnt = static_cast<int>(max64(0, min64(slice, M - beg)));
+  const T* src = x + ng * M + beg;
+  T* dst = y + ng * M + beg;
+  T* sx = reinterpret_cast<T*>(smem_raw);
+  constexpr int V = Vec16<T>::N;
+
+  // Pass 0: HBM -> shared memory, summing on the way.
+  float s = 0.f;
+  if (VEC) {
+    const int nv = cnt / V;
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(sx);
+    for (int i0 = threadIdx.x; i0 < nv; i0 += kGnThreads * kGnUnroll) {
+      uint4 r[kGnUnroll];
+#pragma unroll
+      for (int u = 0; u < kGnUnroll; ++u) {
+        const int i = i0 + u * kGnThreads;
+        if (i < nv) r[u] = ld_stream16(s4 + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kGnUnroll; ++u) {
+        const int i = i0 + u * kGnThreads;
+        if (i < nv) {
+          d4[i] = r[u];
+          float v[V];
+          unpack16<T>(r[u], v);
+#pragma unroll
+          for (int e = 0; e < V; ++e) s += v[e];
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < cnt; i += kGnThreads) {
+      const T v = src[i];
+      sx[i] = v;
+      s += to_f32(v);
+    }
+  }
+  s = block_sum<kGnThreads>(s, scratch);
+  if (threadIdx.x == 0) part[0] = s;
+  cluster.sync();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int r = 0; r < csize; ++r) tot += *cluster.map_shared_rank(&part[0], r);
+    stat[0] = tot / static_cast<float>(M);
+  }
+  __syncthreads();
+  const float mean = stat[0];
+
+  // Pass 1: sum of squared deviations from shared memory.
+  float q = 0.f;
+  if (VEC) {
+    const int nv = cnt / V;
+    const uint4* d4 = reinterpret_cast<const uint4*>(sx);
+    for (int i = threadIdx.x; i < nv; i += kGnThreads) {
+      float v[V];
+      unpack16<T>(d4[i], v);
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        const float d = v[e] - mean;
+        q = fmaf(d, d, q);
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < cnt; i += kGnThreads) {
+      const float d = to_f32(sx[i]) - mean;
+      q = fmaf(d, d, q);
+    }
+  }
+  q = block_sum<kGnThreads>(q, scratch);
+  if (threadIdx.x == 0) part[1] = q;
+  cluster.sync();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int r = 0; r < csize; ++r) tot += *cluster.map_shared_rank(&part[1], r);
+    stat[1] = 1.0f / sqrtf(tot / static_cast<float>(M) + eps);
+  }
+  // Peers may still be reading part[] of this CTA: arrive now, wait at exit.
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  __syncthreads();
+  const float rstd = stat[1];
+
+  // Pass 2: normalise + affine from shared memory -> HBM.
+  const int c0 = g * Cg;
+  if (VEC) {
+    const int nv = cnt / V;
+    const uint4* d4 = reinterpret_cast<const uint4*>(sx);
+    for (int i = threadIdx.x; i < nv; i += kGnThreads) {
+      const int64_t idx = beg + static_cast<int64_t>(i) * V;
+      const int c = c0 + static_cast<int>(idx / S);
+      float a = rstd, b = -mean * rstd;
+      if (gamma) {
+        const float gm = load_param(gamma, affine_dt, c);
+        a = rstd * gm;
+        b = -mean * a;
+      }
+      if (beta) b += load_param(beta, affine_dt, c);
+      float v[V];
+      unpack16<T>(d4[i], v);
+#pragma unroll
+      for (int e = 0; e < V; ++e) v[e] = fmaf(v[e], a, b);
+      st_stream16(reinterpret_cast<uint4*>(dst) + i, pack16<T>(v));
+    }
+  } else {
+    for (int i = threadIdx.x; i < cnt; i += kGnThreads) {
+      const int c = c0 + static_cast<int>((beg + i) / S);
+      float a = rstd, b = -mean * rstd;
+      if (gamma) {
+        a = rstd * load_param(gamma, affine_dt, c);
+        b = -mean * a;
+      }
+      if (beta) b += load_param(beta, affine_dt, c);
+      dst[i] = from_f32<T>(fmaf(to_f32(sx[i]), a, b));
+    }
+  }
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------- split: stats ----
+// One CTA per (group, chunk).  Shifted sums around the chunk's first value
+// keep the single-pass variance well conditioned; the chunk's (count, mean,
+// M2) triple goes to `part`.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256)
+gn_partial_stats_kernel(const T* __restrict__ x, float* __restrict__ part, int64_t M,
+                        int64_t chunk, int chunks) {
+  __shared__ float scratch[33];
+  const int64_t ng = blockIdx.x / chunks;
+  const int ch = blockIdx.x % chunks;
+  const int64_t beg = static_cast<int64_t>(ch) * chunk;
+  const int64_t cnt = max64(0, min64(chunk, M - beg));
+  const T* src = x + ng * M + beg;
+  const float shift = cnt > 0 ? to_f32(src[0]) : 0.f;
+  float s1 = 0.f, s2 = 0.f;
+  constexpr int V = Vec16<T>::N;
+  if (VEC) {
+    const int64_t nv = cnt / V;
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    for (int64_t i0 = threadIdx.x; i0 < nv; i0 += 256 * kGnUnroll) {
+      uint4 r[kGnUnroll];
+#pragma unroll
+      for (int u = 0; u < kGnUnroll; ++u) {
+        const int64_t i = i0 + u * 256;
+        if (i < nv) r[u] = ld_stream16(s4 + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kGnUnroll; ++u) {
+        const int64_t i = i0 + u * 256;
+        if (i < nv) {
+          float v[V];
+          unpack16<T>(r[u], v);
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            const float d = v[e] - shift;
+            s1 += d;
+            s2 = fmaf(d, d, s2);
+          }
+        }
+      }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < cnt; i += 256) {
+      const float d = to_f32(src[i]) - shift;
+      s1 += d;
+      s2 = fmaf(d, d, s2);
+    }
+  }
+  s1 = block_sum<256>(s1, scratch);
+  s2 = block_sum<256>(s2, scratch);
+  if (threadIdx.x == 0) {
+    const float n = static_cast<float>(cnt);
+    float* o = part + (ng * chunks + ch) * 3;
+    o[0] = n;
+    o[1] = cnt > 0 ? shift + s1 / n : 0.f;
+    o[2] = cnt > 0 ? fmaxf(s2 - s1 * s1 / n, 0.f) : 0.f;
+  }
+}
+
+// Merges `chunks` (count, mean, M2) triples of each group into one (Chan et
+// al. pairwise update, fixed order, fp64).  One thread per group.
+__global__ void gn_merge_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                int64_t groups, int chunks) {
+  const int64_t ng = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (ng >= groups) return;
+  double n = 0.0, mean = 0.0, m2 = 0.0;
+  for (int c = 0; c < chunks; ++c) {
+    const float* p = part + (ng * chunks + c) * 3;
+    const double nb = p[0];
+    if (nb <= 0.0) continue;
+    const double mb = p[1], qb = p[2];
+    const double tot = n + nb;
+    const double d = mb - mean;
+    mean += d * nb / tot;
+    m2 += qb + d * d * n * nb / tot;
+    n = tot;
+  }
+  out[ng * 3 + 0] = static_cast<float>(n);
+  out[ng * 3 + 1] = static_cast<float>(mean);
+  out[ng * 3 + 2] = static_cast<float>(m2);
+}
+
+// ------------------------------------------------------- split: apply ----
+// y = (x - mean) * rstd * gamma + beta, optional SiLU; NC[S] layout out.
+template <typename T, bool VEC, bool SILU>
+__global__ void __launch_bounds__(256)
+gn_apply_kernel(const T* __restrict__ x, const float* __restrict__ stats,
+                const void* __restrict__ gamma, const void* __restrict__ beta,
+                T* __restrict__ y, int affine_dt, int64_t S, int G, int Cg, float eps,
+                int64_t chunk, int chunks) {
+  const int64_t ng = blockIdx.x / chunks;
+  const int ch = blockIdx.x % chunks;
+  const int64_t M = static_cast<int64_t>(Cg) * S;
+  const int64_t beg = static_cast<int64_t>(ch) * chunk;
+  const int64_t cnt = max64(0, min64(chunk, M - beg));
+  const float n = stats[ng * 3 + 0];
+  const float mean = stats[ng * 3 + 1];
+  const float rstd = 1.0f / sqrtf(stats[ng * 3 + 2] / n + eps);
+  const int c0 = static_cast<int>(ng % G) * Cg;
+  const T* src = x + ng * M + beg;
+  T* dst = y + ng * M + beg;
+  constexpr int V = Vec16<T>::N;
+  if (VEC) {
+    const int64_t nv = cnt / V;
+    for (int64_t i = threadIdx.x; i < nv; i += 256) {
+      const int64_t idx = beg + i * V;
+      const int c = c0 + static_cast<int>(idx / S);
+      float a = rstd, b = -mean * rstd;
+      if (gamma) {
+        a = rstd * load_param(gamma, affine_dt, c);
+        b = -mean * a;
+      }
+      if (beta) b += load_param(beta, affine_dt, c);
+      float v[V];
+      unpack16<T>(ld_stream16(reinterpret_cast<const uint4*>(src) + i), v);
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        v[e] = fmaf(v[e], a, b);
+        if (SILU) v[e] = silu(v[e]);
+      }
+      st_stream16(reinterpret_cast<uint4*>(dst) + i, pack16<T>(v));
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < cnt; i += 256) {
+      const int c = c0 + static_cast<int>((beg + i) / S);
+      float a = rstd, b = -mean * rstd;
+      if (gamma) {
+        a = rstd * load_param(gamma, affine_dt, c);
+        b = -mean * a;
+      }
+      if (beta) b += load_param(beta, affine_dt, c);
+      float v = fmaf(to_f32(src[i]), a, b);
+      if (SILU) v = silu(v);
+      dst[i] = from_f32<T>(v);
+    }
+  }
+}
+
+// Normalise (+SiLU) and transpose NC[S] -> N[S]C in one pass: the conv3d
+// operand producer of the fused GroupNorm -> SiLU -> conv3d path.  Tile of
+// 32 channels x 64 positions through shared memory; grid (S/64, C/32, N).
+template <typename T, bool SILU>
+__global__ void __launch_bounds__(256)
+gn_apply_cl_kernel(const T* __restrict__ x, const float* __restrict__ stats,
+                   const void* __restrict__ gamma, const void* __restrict__ beta,
+                   T* __restrict__ y, int affine_dt, int64_t C, int64_t S, int G, int Cg,
+                   float eps) {
+  __shared__ float tile[32][65];
+  const int64_t n = blockIdx.z;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 32;
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
+  for (int cc = ty; cc < 32; cc += 4) {
+    const int64_t c = c0 + cc;
+    const int64_t p = p0 + tx;
+    float v = 0.f;
+    if (c < C && p < S) {
+      const int64_t ng = n * G + c / Cg;
+      const float cntf = stats[ng * 3 + 0];
+      const float mean = stats[ng * 3 + 1];
+      const float rstd = 1.0f / sqrtf(stats[ng * 3 + 2] / cntf + eps);
+      float a = rstd, b = -mean * rstd;
+      if (gamma) {
+        a = rstd * load_param(gamma, affine_dt, c);
+        b = -mean * a;
+      }
+      if (beta) b += load_param(beta, affine_dt, c);
+      v = fmaf(to_f32(x[(n * C + c) * S + p]), a, b);
+      if (SILU) v = silu(v);
+    }
+    tile[cc][tx] = v;
+  }
+  __syncthreads();
+  const int lc = threadIdx.x & 31, lp = threadIdx.x >> 5;  // 32 x 8
+  for (int pp = lp; pp < 64; pp += 8) {
+    const int64_t p = p0 + pp, c = c0 + lc;
+    if (p < S && c < C) y[(n * S + p) * C + c] = from_f32<T>(tile[lc][pp]);
+  }
+}
+
+// ----------------------------------------------------------- host side ---
+struct GnShape {
+  int64_t N, C, S, G, Cg, M, groups;
+};
+
+int check_shape(int64_t N, int64_t C, int64_t S, int64_t G, GnShape* sh) {
+  if (N <= 0 || C <= 0 || S <= 0 || G <= 0) return fail_arg("non-positive GroupNorm size");
+  if (C % G != 0) return fail_arg("C must be divisible by num_groups");
+  sh->N = N;
+  sh->C = C;
+  sh->S = S;
+  sh->G = G;
+  sh->Cg = C / G;
+  sh->M = sh->Cg * S;
+  sh->groups = N * G;
+  return B200_OK;
+}
+
+// Split-path chunking: ~64K elements per CTA, at least one chunk.
+int64_t split_chunk(const GnShape& sh, int V) {
+  int64_t chunk = 65536;
+  if (sh.M < chunk) chunk = sh.M;
+  chunk = (chunk + V - 1) / V * V;
+  return chunk;
+}
+
+template <typename T>
+bool vec_ok(const void* x, const void* y, const GnShape& sh) {
+  constexpr int V = Vec16<T>::N;
+  return aligned16(x) && (y == nullptr || aligned16(y)) && sh.S % V == 0;
+}
+
+template <typename T>
+int launch_cluster(const T* x, const void* gamma, const void* beta, T* y, int affine_dt,
+                   const GnShape& sh, float eps, int csize, cudaStream_t stream) {
+  constexpr int V = Vec16<T>::N;
+  const bool vec = vec_ok<T>(x, y, sh);
+  int64_t slice = (sh.M + csize - 1) / csize;
+  slice = (slice + V - 1) / V * V;
+  const int64_t smem = slice * static_cast<int64_t>(sizeof(T));
+  if (smem > max_smem_optin() - 4096) return fail_unsupported("group slice exceeds shared memory");
+  if (sh.groups * csize > 0x7fffffffLL) return fail_unsupported("grid too large");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(sh.groups * csize));
+  cfg.blockDim = dim3(kGnThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto kern = vec ? gn_cluster_kernel<T, true> : gn_cluster_kernel<T, false>;
+  B200_CUDA_CHECK(
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (csize > 8)
+    B200_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+    cudaGetLastError();
+    return fail_unsupported("cluster configuration cannot be scheduled");
+  }
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, x, gamma, beta, y, affine_dt, sh.S,
+                                     static_cast<int>(sh.G), static_cast<int>(sh.Cg), eps,
+                                     static_cast<int>(slice), csize));
+  return B200_OK;
+}
+
+template <typename T>
+int launch_stats(const T* x, float* stats_out, const GnShape& sh, void* ws, size_t ws_bytes,
+                 cudaStream_t stream) {
+  constexpr int V = Vec16<T>::N;
+  const bool vec = vec_ok<T>(x, nullptr, sh);
+  const int64_t chunk = split_chunk(sh, vec ? V : 1);
+  const int64_t chunks = (sh.M + chunk - 1) / chunk;
+  const size_t need = static_cast<size_t>(sh.groups * chunks * 3) * sizeof(float);
+  if (ws_bytes < need || ws == nullptr) return fail_arg("GroupNorm workspace too small");
+  if (sh.groups * chunks > 0x7fffffffLL) return fail_unsupported("grid too large");
+  float* part = static_cast<float*>(ws);
+  const unsigned grid = static_cast<unsigned>(sh.groups * chunks);
+  if (vec)
+    gn_partial_stats_kernel<T, true><<<grid, 256, 0, stream>>>(x, part, sh.M, chunk, (int)chunks);
+  else
+    gn_partial_stats_kernel<T, false><<<grid, 256, 0, stream>>>(x, part, sh.M, chunk, (int)chunks);
+  B200_LAUNCH_CHECK("gn_partial_stats_kernel");
+  gn_merge_kernel<<<static_cast<unsigned>((sh.groups + 127) / 128), 128, 0, stream>>>(
+      part, stats_out, sh.groups, static_cast<int>(chunks));
+  B200_LAUNCH_CHECK("gn_merge_kernel");
+  return B200_OK;
+}
+
+size_t stats_ws_bytes(const GnShape& sh, int dtype) {
+  // Sized for the scalar chunking (the larger of the two).
+  const int64_t chunk = split_chunk(sh, 1);
+  const int64_t chunks = (sh.M + chunk - 1) / chunk;
+  (void)dtype;
+  return static_cast<size_t>(sh.groups * (chunks + 1) * 3) * sizeof(float) + 256;
+}
+
+template <typename T>
+int launch_apply(const T* x, const float* stats, const void* gamma, const void* beta, T* y,
+                 int affine_dt, const GnShape& sh, float eps, bool silu, bool to_cl,
+                 cudaStream_t stream) {
+  if (to_cl) {
+    if (sh.S > 0x7fffffffLL * 64 || (sh.C + 31) / 32 > 65535 || sh.N > 65535)
+      return fail_unsupported("channels-last apply grid too large");
+    dim3 grid(static_cast<unsigned>((sh.S + 63) / 64), static_cast<unsigned>((sh.C + 31) / 32),
+              static_cast<unsigned>(sh.N));
+    if (silu)
+      gn_apply_cl_kernel<T, true><<<grid, 256, 0, stream>>>(x, stats, gamma, beta, y, affine_dt,
+                                                            sh.C, sh.S, (int)sh.G, (int)sh.Cg, eps);
+    else
+      gn_apply_cl_kernel<T, false><<<grid, 256, 0, stream>>>(x, stats, gamma, beta, y, affine_dt,
+                                                             sh.C, sh.S, (int)sh.G, (int)sh.Cg, eps);
+    B200_LAUNCH_CHECK("gn_apply_cl_kernel");
+    return B200_OK;
+  }
+  constexpr int V = Vec16<T>::N;
+  const bool vec = vec_ok<T>(x, y, sh);
+  const int64_t chunk = split_chunk(sh, vec ? V : 1);
+  const int64_t chunks = (sh.M + chunk - 1) / chunk;
+  if (sh.groups * chunks > 0x7fffffffLL) return fail_unsupported("grid too large");
+  const unsigned grid = static_cast<unsigned>(sh.groups * chunks);
+  const int G = static_cast<int>(sh.G), Cg = static_cast<int>(sh.Cg), nc = static_cast<int>(chunks);
+  if (vec && silu)
+    gn_apply_kernel<T, true, true><<<grid, 256, 0, stream>>>(x, stats, gamma, beta, y, affine_dt, sh.S, G, Cg, eps, chunk, nc);
+  else if (vec)
+    gn_apply_kernel<T, true, false><<<grid, 256, 0, stream>>>(x, stats, gamma, beta, y, affine_dt, sh.S, G, Cg, eps, chunk, nc);
+  else if (silu)
+    gn_apply_kernel<T, false, true><<<grid, 256, 0, stream>>>(x, stats, gamma, beta, y, affine_dt, sh.S, G, Cg, eps, chunk, nc);
+  else
+    gn_apply_kernel<T, false, false><<<grid, 256, 0, stream>>>(x, stats, gamma, beta, y, affine_dt, sh.S, G, Cg, eps, chunk, nc);
+  B200_LAUNCH_CHECK("gn_apply_kernel");
+  return B200_OK;
+}
+
+// Smallest power-of-two cluster whose per-CTA slice fits `target` bytes.
+int auto_cluster(const GnShape& sh, size_t esize) {
+  const int64_t bytes = sh.M * static_cast<int64_t>(esize);
+  const int64_t target = 64 * 1024;
+  for (int k = 1; k <= 8; k *= 2)
+    if ((bytes + k - 1) / k <= target) return k;
+  if ((bytes + 15) / 16 <= 200 * 1024) return 16;
+  return 0;
+}
+
+template <typename T>
+int gn_fwd_typed(const void* xv, const void* gamma, const void* beta, void* yv, int affine_dt,
+                 const GnShape& sh, float eps, int variant, void* ws, size_t ws_bytes,
+                 cudaStream_t stream) {
+  const T* x = static_cast<const T*>(xv);
+  T* y = static_cast<T*>(yv);
+  if (variant == 0) {
+    const int k = auto_cluster(sh, sizeof(T));
+    if (k > 0) {
+      const int rc = launch_cluster<T>(x, gamma, beta, y, affine_dt, sh, eps, k, stream);
+      if (rc <= 0) return rc;
+    }
+    variant = 1;
+  }
+  if (variant >= 16) {
+    const int k = variant - 16;
+    if (k != 1 && k != 2 && k != 4 && k != 8 && k != 16)
+      return fail_arg("GroupNorm cluster size must be 1, 2, 4, 8 or 16");
+    return launch_cluster<T>(x, gamma, beta, y, affine_dt, sh, eps, k, stream);
+  }
+  if (variant != 1) return fail_arg("unknown GroupNorm variant");
+  // Split path: partials + merged stats in the workspace, then apply.
+  const int64_t chunk = split_chunk(sh, 1);
+  const int64_t chunks = (sh.M + chunk - 1) / chunk;
+  const size_t stats_bytes = static_cast<size_t>(sh.groups * 3) * sizeof(float);
+  const size_t part_bytes = static_cast<size_t>(sh.groups * chunks * 3) * sizeof(float);
+  if (ws == nullptr || ws_bytes < stats_bytes + part_bytes + 16)
+    return fail_arg("GroupNorm workspace too small");
+  float* stats = static_cast<float*>(ws);
+  void* part = static_cast<char*>(ws) + ((stats_bytes + 15) / 16) * 16;
+  const int rc = launch_stats<T>(x, stats, sh, part, ws_bytes - ((stats_bytes + 15) / 16) * 16,
+                                 stream);
+  if (rc != B200_OK) return rc;
+  return launch_apply<T>(x, stats, gamma, beta, y, affine_dt, sh, eps, false, false, stream);
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+size_t b200_gn_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int dtype,
+                               int variant) {
+  GnShape sh;
+  if (check_shape(N, C, S, G, &sh) != B200_OK) return 0;
+  if (variant >= 16) return 0;
+  if (variant == 0 && auto_cluster(sh, dtype_size(dtype)) > 0) {
+    // The cluster path may still decline (scheduling); keep the split
+    // fallback's scratch available.
+  }
+  const size_t stats_bytes = ((static_cast<size_t>(sh.groups * 3) * sizeof(float) + 15) / 16) * 16;
+  return stats_bytes + stats_ws_bytes(sh, dtype);
+}
+
+int b200_gn_fwd(const void* x, const void* gamma, const void* beta, void* y, int dtype,
+                int affine_dtype, int64_t N, int64_t C, int64_t S, int64_t G, float eps,
+                int variant, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !y) return fail_arg("x/y is NULL");
+  if (!dtype_ok(dtype) || ((gamma || beta) && !dtype_ok(affine_dtype)))
+    return fail_arg("bad dtype");
+  GnShape sh;
+  int rc = check_shape(N, C, S, G, &sh);
+  if (rc != B200_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B200_DTYPE_F32)
+    return gn_fwd_typed<float>(x, gamma, beta, y, affine_dtype, sh, eps, variant, workspace,
+                               workspace_bytes, s);
+  if (dtype == B200_DTYPE_F16)
+    return gn_fwd_typed<__half>(x, gamma, beta, y, affine_dtype, sh, eps, variant, workspace,
+                                workspace_bytes, s);
+  return gn_fwd_typed<__nv_bfloat16>(x, gamma, beta, y, affine_dtype, sh, eps, variant,
+                                     workspace, workspace_bytes, s);
+}
+
+size_t b200_gn_stats_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int dtype) {
+  GnShape sh;
+  if (check_shape(N, C, S, G, &sh) != B200_OK) return 0;
+  return stats_ws_bytes(sh, dtype);
+}
+
+int b200_gn_partial_stats(const void* x, float* partial_out, int dtype, int64_t N, int64_t C,
+                          int64_t S, int64_t G, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  if (!x || !partial_out) return fail_arg("x/partial_out is NULL");
+  if (!dtype_ok(dtype)) return fail_arg("bad dtype");
+  GnShape sh;
+  int rc = check_shape(N, C, S, G, &sh);
+  if (rc != B200_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B200_DTYPE_F32)
+    return launch_stats<float>(static_cast<const float*>(x), partial_out, sh, workspace,
+                               workspace_bytes, s);
+  if (dtype == B200_DTYPE_F16)
+    return launch_stats<__half>(static_cast<const __half*>(x), partial_out, sh, workspace,
+                                workspace_bytes, s);
+  return launch_stats<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x), partial_out, sh,
+                                     workspace, workspace_bytes, s);
+}
+
+int b200_gn_apply(const void* x, const float* stats, const void* gamma, const void* beta,
+                  void* y, int dtype, int affine_dtype, int64_t N, int64_t C, int64_t S,
+                  int64_t G, float eps, int silu, int to_channels_last, void* stream) {
+  if (!x || !y || !stats) return fail_arg("x/y/stats is NULL");
+  if (!dtype_ok(dtype) || ((gamma || beta) && !dtype_ok(affine_dtype)))
+    return fail_arg("bad dtype");
+  GnShape sh;
+  int rc = check_shape(N, C, S, G, &sh);
+  if (rc != B200_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B200_DTYPE_F32)
+    return launch_apply<float>(static_cast<const float*>(x), stats, gamma, beta,
+                               static_cast<float*>(y), affine_dtype, sh, eps, silu != 0,
+                               to_channels_last != 0, s);
+  if (dtype == B200_DTYPE_F16)
+    return launch_apply<__half>(static_cast<const __half*>(x), stats, gamma, beta,
+                                static_cast<__half*>(y), affine_dtype, sh, eps, silu != 0,
+                                to_channels_last != 0, s);
+  return launch_apply<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x), stats, gamma, beta,
+                                     static_cast<__nv_bfloat16*>(y), affine_dtype, sh, eps,
+                                     silu != 0, to_channels_last != 0, s);
+}
+
+}  // extern "C"

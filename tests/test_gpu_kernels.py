@@ -1,0 +1,227 @@
+"""Parity of the sm_100a kernels (called through the C ABI via amd_tuned_torch.ops)
+with the oracle: the reference's golden vectors at small sizes, and stock
+torch CPU fp32 at the BASELINE sizes.
+
+Tolerances (rel-L2 in fp64): fp32 <= 1e-5, fp16/bf16
+direct kernels <= 2e-3, FFT routes <= 5e-3."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import load_golden, torch_dtype
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"f32": 1e-5, "f16": 2e-3, "bf16": 2e-3}
+
+
+def _t(a, dt, dev):
+    return torch.as_tensor(np.asarray(a, dtype=np.float32)).to(device=dev, dtype=dt)
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _no_fault():
+    from amd_tuned_torch import ops
+    assert ops.read_device_flags() == 0
+
+
+# ------------------------------------------------------------ GroupNorm ---
+GN_VARIANTS = [0, 1, 17, 18, 20, 24]
+
+
+@pytest.mark.parametrize("variant", GN_VARIANTS)
+@pytest.mark.parametrize("case", list(load_golden("group_norm")))
+def test_group_norm_golden(cuda, case, variant):
+    from amd_tuned_torch import ops
+    d = load_golden("group_norm")[case]
+    dt = torch_dtype(d["dtype"])
+    G, affine = (int(v) for v in d["meta"])
+    x = _t(d["x"], dt, cuda)
+    w = _t(d["w"], dt, cuda) if affine else None
+    b = _t(d["b"], dt, cuda) if affine else None
+    y = ops.group_norm(x, G, w, b, float(d["eps"]), variant=variant)
+    if y is None:   # a cluster size that cannot be scheduled declines
+        assert variant >= 16
+        return
+    torch.cuda.synchronize()
+    assert oracle.rel_l2(_np(y), d["y"]) <= TOL[d["dtype"]]
+    _no_fault()
+
+
+@pytest.mark.parametrize("variant", [0, 1, 20, 24])
+def test_group_norm_cfg3_full_size(cuda, variant):
+    """BASELINE cfg 3: x[4,512,128,128] ~N(0,2) bf16, G=32, eps=1e-6,
+    gamma ~U(0.5,1.5), beta ~N(0,0.1)."""
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(4, 512, 128, 128, generator=g) * 2).to(torch.bfloat16)
+    w = (torch.rand(512, generator=g) + 0.5).to(torch.bfloat16)
+    b = (torch.randn(512, generator=g) * 0.1).to(torch.bfloat16)
+    y = ops.group_norm(x.to(cuda), 32, w.to(cuda), b.to(cuda), 1e-6, variant=variant)
+    assert y is not None
+    ref = oracle.stock_group_norm(x.float().numpy(), 32, w.float().numpy(), b.float().numpy(),
+                                  1e-6)
+    assert oracle.rel_l2(_np(y), ref) <= 2e-3
+    _no_fault()
+
+
+@pytest.mark.parametrize("shape,G", [((3, 6, 5, 7), 3), ((1, 10, 13), 5), ((2, 4, 1, 1), 4),
+                                     ((1, 32, 1031), 8)])
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+def test_group_norm_ragged(cuda, shape, G, dt):
+    """Spatial sizes that are not multiples of the 16-byte vector (scalar path)."""
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(11)
+    x = (torch.randn(*shape, generator=g) + 3.0).to(torch_dtype(dt))
+    w = torch.rand(shape[1], generator=g).to(torch_dtype(dt))
+    b = torch.randn(shape[1], generator=g).to(torch_dtype(dt))
+    ref = oracle.c_group_norm(x.float().numpy(), G, w.float().numpy(), b.float().numpy(), 1e-5)
+    for variant in (0, 1):
+        y = ops.group_norm(x.to(cuda), G, w.to(cuda), b.to(cuda), 1e-5, variant=variant)
+        assert oracle.rel_l2(_np(y), ref) <= TOL[dt]
+
+
+def test_group_norm_stats_and_fused_apply(cuda):
+    """Partial statistics + apply(+SiLU, channels-last) == GroupNorm -> SiLU."""
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(2, 64, 4, 8, 8, generator=g).to(torch.bfloat16)
+    w = (torch.rand(64, generator=g) + 0.5).to(torch.bfloat16)
+    b = (torch.randn(64, generator=g) * 0.1).to(torch.bfloat16)
+    xd = x.to(cuda)
+    st = ops.group_norm_partial_stats(xd, 32)
+    ref = torch.nn.functional.group_norm(x.float(), 32, w.float(), b.float(), 1e-5)
+    ref = torch.nn.functional.silu(ref)
+    y = ops.group_norm_apply(xd, st, 32, w.to(cuda), b.to(cuda), 1e-5, silu=True)
+    assert oracle.rel_l2(_np(y), ref.numpy()) <= 2e-3
+    ycl = ops.group_norm_apply(xd, st, 32, w.to(cuda), b.to(cuda), 1e-5, silu=True,
+                               channels_last_out=True)
+    ref_cl = ref.reshape(2, 64, -1).permute(0, 2, 1).numpy()
+    assert oracle.rel_l2(_np(ycl), ref_cl) <= 2e-3
+
+
+# ----------------------------------------------------- depthwise conv1d ---
+@pytest.mark.parametrize("case", list(load_golden("dwconv1d")))
+def test_dwconv1d_golden(cuda, case):
+    from amd_tuned_torch import ops
+    d = load_golden("dwconv1d")[case]
+    dt = torch_dtype(d["dtype"])
+    B, C, L, K, pad, has_b = (int(v) for v in d["meta"])
+    x = _t(d["x"], dt, cuda)
+    w = _t(d["w"], dt, cuda).reshape(C, K)
+    b = _t(d["b"], dt, cuda) if has_b else None
+    y = ops.depthwise_conv1d(x, w, b, pad)
+    assert oracle.rel_l2(_np(y), d["y"]) <= TOL[d["dtype"]]
+    _no_fault()
+
+
+def _kaiming(shape, g):
+    bound = 1.0 / math.sqrt(math.prod(shape[1:]))
+    return (torch.rand(*shape, generator=g) * 2 - 1) * bound
+
+
+def test_dwconv1d_cfg1_full_size(cuda):
+    """BASELINE cfg 1: x[8,256,2048] fp32, w[256,1,3] kaiming-U, bias, p=1."""
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(8, 256, 2048, generator=g)
+    w = _kaiming((256, 1, 3), g)
+    b = _kaiming((256, 1), g).reshape(256) * math.sqrt(1)
+    y = ops.depthwise_conv1d(x.to(cuda), w.reshape(256, 3).to(cuda), b.to(cuda), 1)
+    ref = oracle.stock_conv1d(x.numpy(), w.numpy(), b.numpy(), 1, 256)
+    assert oracle.rel_l2(_np(y), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("K,pad,L", [(3, 1, 4099), (31, 15, 5000), (2, 0, 17), (64, 40, 100),
+                                     (11, 0, 2048)])
+def test_dwconv1d_shapes(cuda, K, pad, L):
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(K)
+    for dt in ("f32", "bf16"):
+        x = torch.randn(2, 5, L, generator=g).to(torch_dtype(dt))
+        w = _kaiming((5, 1, K), g).to(torch_dtype(dt))
+        b = torch.randn(5, generator=g).to(torch_dtype(dt))
+        y = ops.depthwise_conv1d(x.to(cuda), w.reshape(5, K).to(cuda), b.to(cuda), pad)
+        ref = oracle.c_dwconv1d(x.float().numpy(), w.float().numpy(), b.float().numpy(), pad)
+        assert oracle.rel_l2(_np(y), ref) <= TOL[dt]
+
+
+# --------------------------------------------------------------- conv3d ---
+@pytest.mark.parametrize("case", list(load_golden("conv3d")))
+def test_conv3d_golden(cuda, case):
+    from amd_tuned_torch import ops
+    d = load_golden("conv3d")[case]
+    dt = torch_dtype(d["dtype"])
+    m = [int(v) for v in d["meta"]]
+    p, dil = m[9:12], m[12:15]
+    x, w, b = _t(d["x"], dt, cuda), _t(d["w"], dt, cuda), _t(d["b"], dt, cuda)
+    y = ops.conv3d(x, w, b, (1, 1, 1), p, dil)
+    if d["dtype"] == "f32":
+        assert y is None   # tensor-core path is fp16/bf16 only: declines
+        return
+    torch.cuda.synchronize()
+    assert oracle.rel_l2(_np(y), d["y"]) <= TOL[d["dtype"]]
+    _no_fault()
+
+
+def test_conv3d_cfg2_full_size(cuda):
+    """BASELINE cfg 2: x[1,64,16,32,32] fp16 ~N(0,1), w[64,64,3,3,3] kaiming-U, bias, p1."""
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(1, 64, 16, 32, 32, generator=g).half()
+    w = _kaiming((64, 64, 3, 3, 3), g).half()
+    b = _kaiming((64, 64 * 27), g)[:, 0].half()
+    y = ops.conv3d(x.to(cuda), w.to(cuda), b.to(cuda), (1, 1, 1), (1, 1, 1), (1, 1, 1))
+    ref = oracle.stock_conv3d(x.float().numpy(), w.float().numpy(), b.float().numpy(), (1, 1, 1))
+    assert oracle.rel_l2(_np(y), ref) <= 2e-3
+    _no_fault()
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("N,Cin,D,H,W,Cout,k,p", [
+    (2, 32, 5, 9, 13, 48, (3, 3, 3), (1, 1, 1)),
+    (1, 128, 3, 8, 8, 128, (3, 3, 3), (1, 1, 1)),
+    (1, 64, 2, 3, 200, 80, (1, 1, 3), (0, 0, 1)),
+    (1, 16, 4, 6, 6, 16, (2, 2, 2), (0, 1, 0)),
+    (1, 72, 3, 5, 5, 300, (3, 3, 3), (1, 1, 1)),
+])
+def test_conv3d_shapes(cuda, dt, N, Cin, D, H, W, Cout, k, p):
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(Cin + Cout)
+    x = torch.randn(N, Cin, D, H, W, generator=g).to(torch_dtype(dt))
+    w = _kaiming((Cout, Cin) + k, g).to(torch_dtype(dt))
+    b = torch.randn(Cout, generator=g).to(torch_dtype(dt)) * 0.1
+    y = ops.conv3d(x.to(cuda), w.to(cuda), b.to(cuda), (1, 1, 1), p, (1, 1, 1))
+    ref = oracle.stock_conv3d(x.float().numpy(), w.float().numpy(), b.float().numpy(), p)
+    assert y.shape == ref.shape
+    assert oracle.rel_l2(_np(y), ref) <= TOL[dt]
+
+
+def test_conv3d_channels_last_io(cuda):
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(1, 64, 4, 8, 8, generator=g).half()
+    w = _kaiming((32, 64, 3, 3, 3), g).half()
+    ref = oracle.stock_conv3d(x.float().numpy(), w.float().numpy(), None, (1, 1, 1))
+    xcl = x.permute(0, 2, 3, 4, 1).contiguous().to(cuda)
+    y = ops.conv3d(xcl, w.to(cuda), None, (1, 1, 1), (1, 1, 1), (1, 1, 1),
+                   x_channels_last=True, out_channels_last=True)
+    assert oracle.rel_l2(_np(y.permute(0, 4, 1, 2, 3)), ref) <= 2e-3
+
+
+def test_conv3d_declines_unsupported(cuda):
+    from amd_tuned_torch import ops
+    x = torch.randn(1, 12, 4, 4, 4, device=cuda, dtype=torch.half)   # Cin % 8 != 0
+    w = torch.randn(8, 12, 3, 3, 3, device=cuda, dtype=torch.half)
+    assert ops.conv3d(x, w, None, (1, 1, 1), (1, 1, 1), (1, 1, 1)) is None
+    x = torch.randn(1, 16, 4, 4, 4, device=cuda, dtype=torch.half)
+    w = torch.randn(8, 16, 3, 3, 3, device=cuda, dtype=torch.half)
+    assert ops.conv3d(x, w, None, (2, 2, 2), (1, 1, 1), (1, 1, 1)) is None   # stride 2
