@@ -1,0 +1,435 @@
+"""Benchmark for the conv/norm hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg2] [--no-shapes]
+
+Prints ONE JSON line (rank 0).  The headline workload is BASELINE config 2
+(configs[1]): dense conv3d fp16, x[1,64,16,32,32] ~N(0,1), w[64,64,3,3,3]
+kaiming-uniform, bias, stride 1, padding 1 -- the tcgen05 implicit-GEMM path.
+A step is one conv3d forward over one batch.  `value` is microseconds per op
+for the whole job (N replicas: total time / ops over all ranks; the conv3d
+config is "replicas only"), timed on the device with CUDA events, max over
+ranks, inputs resident in HBM and rotated over more bytes than L2 holds.
+`e2e` is the same op through the public API (patched F.conv3d) with the input
+copied from pinned host memory and the output copied back inside the timed
+region.  `per_shape` adds the other BASELINE configs measured on rank 0.
+
+`--impl reference` times the reference's CPU path for the same workload --
+stock torch CPU fp32 F.conv3d on the cast inputs, which is what the
+reference package executes for CPU tensors (its tiers require CUDA) -- with
+every host thread, each step one full op.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "rocm-kernel-select_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+os.environ.setdefault("AMD_TUNED_TORCH_AUTOPATCH", "0")
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+import torch.nn.functional as F  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+ROTATE_BYTES = 3 * L2_BYTES   # inputs rotated over > L2 so every step reads HBM
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "src": "fallback"}
+
+
+def _traffic(kernel: str):
+    """dram bytes read+write per launch from the committed ncu summary, or None."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get(kernel)
+        except ValueError:
+            return None
+    return None
+
+
+# ------------------------------------------------------------- clocks ---
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock + throttle reasons)."""
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.25)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) != 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[2:]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------- workloads ---
+def _kaiming(shape, g):
+    bound = 1.0 / math.sqrt(math.prod(shape[1:]))
+    return (torch.rand(*shape, generator=g) * 2 - 1) * bound
+
+
+def make_cfg2(seed: int = 2):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(1, 64, 16, 32, 32, generator=g).half()
+    w = _kaiming((64, 64, 3, 3, 3), g).half()
+    b = (_kaiming((64, 64 * 27), g)[:, 0]).half()
+    return x, w, b
+
+
+CFG2_FLOPS = 2 * 16384 * 64 * 1728          # 3,623,878,656
+CFG2_BYTES = 2 * 1048576 * 2 + 27 * 64 * 64 * 2 + 128
+
+
+def _events_time(fn, iters: int, stream) -> float:
+    """Average ms per call of fn over iters calls, CUDA events on `stream`."""
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record(stream)
+    for i in range(iters):
+        fn(i)
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def _graph_time(fn, iters: int, stream, reps: int = 3) -> float:
+    """Average ms per call of fn(i), i < iters, captured once into a CUDA
+    graph and replayed (no host launch overhead in the measurement); best of
+    `reps` replays, each timed with CUDA events on `stream`."""
+    g = torch.cuda.CUDAGraph()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        g.replay()
+        e.record(stream)
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / iters
+        best = ms if best is None else min(best, ms)
+    del g
+    return best
+
+
+def _rel_l2(a, b) -> float:
+    a = a.double().flatten()
+    b = b.double().flatten()
+    return float((a - b).norm() / b.norm().clamp_min(1e-300))
+
+
+# ------------------------------------------------------------ per shape ---
+def per_shape(dev, peaks) -> dict:
+    """Device-timed µs/op, roofline fraction and rel-L2 for BASELINE configs 1-3."""
+    from amd_tuned_torch import ops
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    hbm = peaks["hbm_gbs"]
+
+    # cfg1: depthwise conv1d fp32 [8,256,2048] k3 p1
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(8, 256, 2048, generator=g)
+    w = _kaiming((256, 1, 3), g)
+    b = _kaiming((256, 1), g).reshape(256)
+    nbuf = max(2, ROTATE_BYTES // (x.numel() * 4 * 2))
+    xs = [x.to(dev) for _ in range(nbuf)]
+    wd, bd = w.reshape(256, 3).to(dev), b.to(dev)
+    ys = [torch.empty(8, 256, 2048, device=dev) for _ in range(nbuf)]
+    y = ops.depthwise_conv1d(xs[0], wd, bd, 1)
+    ref = F.conv1d(x, w, b, padding=1, groups=256)
+    err = _rel_l2(y.cpu(), ref)
+    for i in range(3):
+        ops.depthwise_conv1d(xs[i % nbuf], wd, bd, 1)
+    ms = _graph_time(lambda i: ops.depthwise_conv1d(xs[i % nbuf], wd, bd, 1, out=ys[i % nbuf]),
+                     200, stream)
+    byt = 33558528
+    out["cfg1_dwconv1d_fp32"] = {"us_per_op": ms * 1e3, "bound": "hbm",
+                                 "achieved_gbs": byt / (ms * 1e-3) / 1e9,
+                                 "frac": byt / (ms * 1e-3) / 1e9 / hbm, "rel_l2": err}
+    del xs, ys
+
+    # cfg3: GroupNorm bf16 [4,512,128,128] G32 eps 1e-6
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(4, 512, 128, 128, generator=g) * 2).bfloat16()
+    w = (torch.rand(512, generator=g) + 0.5).bfloat16()
+    b = (torch.randn(512, generator=g) * 0.1).bfloat16()
+    nbuf = max(2, ROTATE_BYTES // (x.numel() * 2 * 2))
+    xs = [x.to(dev) for _ in range(nbuf)]
+    ys = [torch.empty_like(xs[0]) for _ in range(nbuf)]
+    wd, bd = w.to(dev), b.to(dev)
+    ref = F.group_norm(x.float(), 32, w.float(), b.float(), 1e-6)
+    byt = 134219776
+    best = None
+    for name, var in (("auto", ops.GN_AUTO), ("cluster4", ops.gn_cluster_variant(4)),
+                      ("cluster8", ops.gn_cluster_variant(8)), ("split", ops.GN_SPLIT)):
+        y = ops.group_norm(xs[0], 32, wd, bd, 1e-6, variant=var)
+        if y is None:
+            continue
+        err = _rel_l2(y.float().cpu(), ref)
+        for i in range(3):
+            ops.group_norm(xs[i % nbuf], 32, wd, bd, 1e-6, variant=var)
+        ms = _graph_time(lambda i: ops.group_norm(xs[i % nbuf], 32, wd, bd, 1e-6, variant=var,
+                                                  out=ys[i % nbuf]), 100, stream)
+        rec = {"variant": name, "us_per_op": ms * 1e3, "bound": "hbm",
+               "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
+               "rel_l2": err}
+        out[f"cfg3_group_norm_bf16_{name}"] = rec
+    del xs, ys
+    torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------- main ---
+def run_ours(args, rank, world, dev) -> dict:
+    import amd_tuned_torch
+    from amd_tuned_torch import ops
+    peaks = _peaks()
+    stream = torch.cuda.current_stream(dev)
+    x, w, b = make_cfg2()
+    xd, wd, bd = x.to(dev), w.to(dev), b.to(dev)
+    nbuf = max(4, ROTATE_BYTES // (x.numel() * 2 * 2))
+    xs = [xd.clone() for _ in range(nbuf)]
+    ys = [torch.empty_like(xd) for _ in range(nbuf)]
+
+    y = ops.conv3d(xd, wd, bd, (1, 1, 1), (1, 1, 1), (1, 1, 1))
+    err = _rel_l2(y.float().cpu(), F.conv3d(x.float(), w.float(), b.float(), padding=1))
+
+    def step(i):
+        ops.conv3d(xs[i % nbuf], wd, bd, (1, 1, 1), (1, 1, 1), (1, 1, 1), out=ys[i % nbuf])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    # The K timed steps are captured once into a CUDA graph and replayed: the
+    # device executes exactly K steps with no host launch gaps between them.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(args.steps):
+            step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        s.record(stream)
+        graph.replay()
+        e.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e)
+    del graph
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+    value = ms_max * 1e3 / (args.steps * world)
+
+    # Dominant kernel alone (the tcgen05 GEMM on a channels-last operand).
+    xcl = [ops.to_channels_last(xs[i]).reshape(1, 16, 32, 32, 64) for i in range(nbuf)]
+    for i in range(3):
+        ops.conv3d(xcl[i % nbuf], wd, bd, (1, 1, 1), (1, 1, 1), (1, 1, 1), x_channels_last=True,
+                   out=ys[i % nbuf])
+    k_ms = _graph_time(lambda i: ops.conv3d(xcl[i % nbuf], wd, bd, (1, 1, 1), (1, 1, 1),
+                                            (1, 1, 1), x_channels_last=True, out=ys[i % nbuf]),
+                       max(args.steps, 50), stream)
+    achieved = CFG2_FLOPS / (k_ms * 1e-3) / 1e12
+    del xcl
+
+    # e2e through the public API: pinned host input -> F.conv3d -> pinned host output.
+    amd_tuned_torch.enable()
+    hx = x.pin_memory()
+    hy = torch.empty_like(x).pin_memory()
+    dx = torch.empty_like(xd)
+    for i in range(max(3, args.warmup)):
+        dx.copy_(hx, non_blocking=True)
+        hy.copy_(F.conv3d(dx, wd, bd, padding=1), non_blocking=True)
+    e2e_iters = args.steps
+    e2e_ms = _events_time(lambda i: hy.copy_(F.conv3d(dx.copy_(hx, non_blocking=True), wd, bd,
+                                                      padding=1), non_blocking=True),
+                          e2e_iters, stream)
+    amd_tuned_torch.disable()
+    t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = float(t.item()) * 1e3 / world
+
+    shapes = per_shape(dev, peaks) if (rank == 0 and not args.no_shapes) else {}
+    cpu = cpu_baseline(x, w, b) if (rank == 0 and world == 1) else None
+    tr = _traffic("conv3d_tc_kernel")
+    return {
+        "metric": "conv3d fp16 cfg2 (N=1,C64->64,16x32x32,k3,p1) us/op",
+        "value": value, "unit": "us/op", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32 accumulate",
+        "data": "synthetic (seeded torch.Generator, kaiming-uniform weights)",
+        "config": {"workload": "cfg2 dense conv3d fp16 [1,64,16,32,32] x [64,64,3,3,3] p1 + bias",
+                   "global_batch": world, "l2": f"inputs rotated over {nbuf} buffers (> L2)",
+                   "parallelism": f"replicas x{world}"},
+        "rel_l2": err,
+        "roofline": {"bound": "tensor", "achieved": achieved,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"],
+                     "traffic": tr, "kernel": "conv3d_tc_kernel",
+                     "kernel_us": k_ms * 1e3, "peak_src": peaks["src"] + " burst bf16"},
+        "e2e": {"value": e2e_value, "unit": "us/op",
+                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
+                "path": "amd_tuned_torch patched F.conv3d (kernel_select winner)"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+        "per_shape": shapes,
+    }
+
+
+def cpu_baseline(x, w, b, budget_s: float = 10.0) -> dict:
+    """Stock torch CPU fp32 F.conv3d (the reference's CPU path), all host threads."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    xf, wf, bf = x.float(), w.float(), b.float()
+    F.conv3d(xf, wf, bf, padding=1)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end and len(times) < 50:
+        t0 = time.perf_counter()
+        F.conv3d(xf, wf, bf, padding=1)
+        times.append(time.perf_counter() - t0)
+    return {"value": min(times) * 1e6, "unit": "us/op", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} full cfg2 ops, min; stock torch CPU fp32 "
+                      "(the reference package's CPU route)"}
+
+
+def run_reference(args, rank, world) -> dict | None:
+    if rank != 0:
+        return None
+    x, w, b = make_cfg2()
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    xf, wf, bf = x.float(), w.float(), b.float()
+    for _ in range(args.warmup):
+        F.conv3d(xf, wf, bf, padding=1)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        F.conv3d(xf, wf, bf, padding=1)
+    dt = time.perf_counter() - t0
+    v = dt * 1e6 / args.steps
+    return {
+        "metric": "conv3d fp16 cfg2 (N=1,C64->64,16x32x32,k3,p1) us/op", "impl": "reference",
+        "value": v, "unit": "us/op", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": v / 1e3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (CPU)", "data": "synthetic",
+        "config": {"workload": "cfg2 dense conv3d fp16 [1,64,16,32,32] x [64,64,3,3,3] p1 + bias"},
+        "cpu_baseline": {"value": v, "unit": "us/op", "cores": threads, "kind": "port",
+                         "sample": "each step one full cfg2 op; stock torch CPU fp32 = the "
+                                   "reference package's route for CPU tensors"},
+        "e2e": {"value": v, "unit": "us/op", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-shapes", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        rec = run_reference(args, rank, world)
+        if rec is not None:
+            print(json.dumps(rec), flush=True)
+        return 0
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        rec = run_ours(args, rank, world, dev)
+        if rank == 0:
+            print(json.dumps(rec), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -142,29 +142,22 @@ gn_cluster_kernel(const T* __restrict__ x, const void* __restrict__ gamma,
     for (int i = threadIdx.x; i < nv; i += kGnThreads) {
       const int64_t idx = beg + static_cast<int64_t>(i) * V;
       const int c = c0 + static_cast<int>(idx / S);
-      float a = rstd, b = -mean * rstd;
-      if (gamma) {
-        const float gm = load_param(gamma, affine_dt, c);
-        a = rstd * gm;
-        b = -mean * a;
-      }
-      if (beta) b += load_param(beta, affine_dt, c);
+      // (x - mean) * (rstd * gamma) + beta: subtracting first keeps full
+      // precision when rstd is large (near-constant groups).
+      const float a = gamma ? rstd * load_param(gamma, affine_dt, c) : rstd;
+      const float b = beta ? load_param(beta, affine_dt, c) : 0.f;
       float v[V];
       unpack16<T>(d4[i], v);
 #pragma unroll
-      for (int e = 0; e < V; ++e) v[e] = fmaf(v[e], a, b);
+      for (int e = 0; e < V; ++e) v[e] = fmaf(v[e] - mean, a, b);
       st_stream16(reinterpret_cast<uint4*>(dst) + i, pack16<T>(v));
     }
   } else {
     for (int i = threadIdx.x; i < cnt; i += kGnThreads) {
       const int c = c0 + static_cast<int>((beg + i) / S);
-      float a = rstd, b = -mean * rstd;
-      if (gamma) {
-        a = rstd * load_param(gamma, affine_dt, c);
-        b = -mean * a;
-      }
-      if (beta) b += load_param(beta, affine_dt, c);
-      dst[i] = from_f32<T>(fmaf(to_f32(sx[i]), a, b));
+      const float a = gamma ? rstd * load_param(gamma, affine_dt, c) : rstd;
+      const float b = beta ? load_param(beta, affine_dt, c) : 0.f;
+      dst[i] = from_f32<T>(fmaf(to_f32(sx[i]) - mean, a, b));
     }
   }
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -278,17 +271,13 @@ gn_apply_kernel(const T* __restrict__ x, const float* __restrict__ stats,
     for (int64_t i = threadIdx.x; i < nv; i += 256) {
       const int64_t idx = beg + i * V;
       const int c = c0 + static_cast<int>(idx / S);
-      float a = rstd, b = -mean * rstd;
-      if (gamma) {
-        a = rstd * load_param(gamma, affine_dt, c);
-        b = -mean * a;
-      }
-      if (beta) b += load_param(beta, affine_dt, c);
+      const float a = gamma ? rstd * load_param(gamma, affine_dt, c) : rstd;
+      const float b = beta ? load_param(beta, affine_dt, c) : 0.f;
       float v[V];
       unpack16<T>(ld_stream16(reinterpret_cast<const uint4*>(src) + i), v);
 #pragma unroll
       for (int e = 0; e < V; ++e) {
-        v[e] = fmaf(v[e], a, b);
+        v[e] = fmaf(v[e] - mean, a, b);
         if (SILU) v[e] = silu(v[e]);
       }
       st_stream16(reinterpret_cast<uint4*>(dst) + i, pack16<T>(v));
@@ -296,13 +285,9 @@ gn_apply_kernel(const T* __restrict__ x, const float* __restrict__ stats,
   } else {
     for (int64_t i = threadIdx.x; i < cnt; i += 256) {
       const int c = c0 + static_cast<int>((beg + i) / S);
-      float a = rstd, b = -mean * rstd;
-      if (gamma) {
-        a = rstd * load_param(gamma, affine_dt, c);
-        b = -mean * a;
-      }
-      if (beta) b += load_param(beta, affine_dt, c);
-      float v = fmaf(to_f32(src[i]), a, b);
+      const float a = gamma ? rstd * load_param(gamma, affine_dt, c) : rstd;
+      const float b = beta ? load_param(beta, affine_dt, c) : 0.f;
+      float v = fmaf(to_f32(src[i]) - mean, a, b);
       if (SILU) v = silu(v);
       dst[i] = from_f32<T>(v);
     }
@@ -332,13 +317,9 @@ gn_apply_cl_kernel(const T* __restrict__ x, const float* __restrict__ stats,
       const float cntf = stats[ng * 3 + 0];
       const float mean = stats[ng * 3 + 1];
       const float rstd = 1.0f / sqrtf(stats[ng * 3 + 2] / cntf + eps);
-      float a = rstd, b = -mean * rstd;
-      if (gamma) {
-        a = rstd * load_param(gamma, affine_dt, c);
-        b = -mean * a;
-      }
-      if (beta) b += load_param(beta, affine_dt, c);
-      v = fmaf(to_f32(x[(n * C + c) * S + p]), a, b);
+      const float a = gamma ? rstd * load_param(gamma, affine_dt, c) : rstd;
+      const float b = beta ? load_param(beta, affine_dt, c) : 0.f;
+      v = fmaf(to_f32(x[(n * C + c) * S + p]) - mean, a, b);
       if (SILU) v = silu(v);
     }
     tile[cc][tx] = v;

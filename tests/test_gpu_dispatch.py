@@ -1,0 +1,123 @@
+"""The drop-in path on a GPU: after amd_tuned_torch.enable(), F.conv1d /
+F.conv3d / F.group_norm run this project's kernels (kernel_select winners)
+and match stock torch CPU fp32; disable() restores stock."""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def patched():
+    import amd_tuned_torch
+    from amd_tuned_torch import kernel_select
+    kernel_select.reset()
+    amd_tuned_torch.enable()
+    yield amd_tuned_torch
+    amd_tuned_torch.disable()
+    kernel_select.reset()
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def test_group_norm_through_patch(cuda, patched):
+    from amd_tuned_torch import kernel_select
+    x = torch.randn(2, 64, 32, 32, generator=torch.Generator().manual_seed(0)).bfloat16()
+    w = torch.rand(64).bfloat16() + 0.5
+    b = torch.randn(64).bfloat16() * 0.1
+    y = F.group_norm(x.to(cuda), 32, w.to(cuda), b.to(cuda), 1e-6)
+    ref = oracle.stock_group_norm(x.float().numpy(), 32, w.float().numpy(), b.float().numpy(), 1e-6)
+    assert oracle.rel_l2(_np(y), ref) <= 2e-3
+    winners = kernel_select.debug_winners()
+    assert any(k[0] == "group_norm" and v.startswith("native") for k, v in winners.items())
+    y2 = F.group_norm(x.to(cuda), 32, w.to(cuda), b.to(cuda), 1e-6)   # cached winner path
+    assert oracle.rel_l2(_np(y2), ref) <= 2e-3
+
+
+def test_conv3d_through_patch(cuda, patched):
+    from amd_tuned_torch import kernel_select
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(1, 64, 8, 16, 16, generator=g).half()
+    w = ((torch.rand(64, 64, 3, 3, 3, generator=g) * 2 - 1) / math.sqrt(64 * 27)).half()
+    b = (torch.randn(64, generator=g) * 0.1).half()
+    y = F.conv3d(x.to(cuda), w.to(cuda), b.to(cuda), padding=1)
+    ref = oracle.stock_conv3d(x.float().numpy(), w.float().numpy(), b.float().numpy(), (1, 1, 1))
+    assert oracle.rel_l2(_np(y), ref) <= 2e-3
+    assert "tcgen05" in kernel_select.debug_winners().values()
+
+
+def test_conv3d_channels_last_through_patch(cuda, patched):
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(1, 32, 4, 8, 8, generator=g).half()
+    w = ((torch.rand(48, 32, 3, 3, 3, generator=g) * 2 - 1) / math.sqrt(32 * 27)).half()
+    xd = x.to(cuda).contiguous(memory_format=torch.channels_last_3d)
+    y = F.conv3d(xd, w.to(cuda), None, padding=1)
+    assert y.is_contiguous(memory_format=torch.channels_last_3d)
+    ref = oracle.stock_conv3d(x.float().numpy(), w.float().numpy(), None, (1, 1, 1))
+    assert oracle.rel_l2(_np(y), ref) <= 2e-3
+
+
+def test_conv3d_training_backward(cuda, patched):
+    """Accelerated forward + stock backward (as in the reference's _Conv3dFn)."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(1, 16, 4, 6, 6, generator=g).half().to(cuda).requires_grad_()
+    w = (torch.randn(16, 16, 3, 3, 3, generator=g) * 0.05).half().to(cuda).requires_grad_()
+    y = F.conv3d(x, w, None, padding=1)
+    y.float().square().sum().backward()
+    x2 = x.detach().float().cpu().requires_grad_()
+    w2 = w.detach().float().cpu().requires_grad_()
+    import amd_tuned_torch
+    amd_tuned_torch.disable()
+    y2 = F.conv3d(x2, w2, None, padding=1)
+    y2.square().sum().backward()
+    assert oracle.rel_l2(_np(y), _np(y2)) <= 2e-3
+    assert oracle.rel_l2(_np(x.grad), _np(x2.grad)) <= 1e-2
+    assert oracle.rel_l2(_np(w.grad), _np(w2.grad)) <= 1e-2
+
+
+def test_depthwise_conv1d_through_patch(cuda, patched):
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(8, 256, 2048, generator=g)
+    w = torch.randn(256, 1, 3, generator=g) * 0.5
+    b = torch.randn(256, generator=g)
+    y = F.conv1d(x.to(cuda), w.to(cuda), b.to(cuda), padding=1, groups=256)
+    ref = oracle.stock_conv1d(x.numpy(), w.numpy(), b.numpy(), 1, 256)
+    assert oracle.rel_l2(_np(y), ref) <= 1e-5
+
+
+def test_long_filter_conv1d_through_patch(cuda, patched):
+    from amd_tuned_torch import kernel_select
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(4, 16, 4096, generator=g).half()
+    w = (torch.randn(16, 1, 512, generator=g) / 22.6).half()
+    y = F.conv1d(x.to(cuda), w.to(cuda), None, padding=256, groups=16)
+    ref = oracle.fft_conv_np(x.float().numpy(), w.float().numpy(), None, (256,), groups=16)
+    assert oracle.rel_l2(_np(y), ref) <= 5e-3
+    assert set(kernel_select.debug_winners().values()) & {"fftconv", "depthwise"}
+
+
+def test_dense_conv1d_and_cpu_tensors_go_to_stock(cuda, patched):
+    x = torch.randn(2, 8, 64)
+    w = torch.randn(4, 8, 3)
+    torch.testing.assert_close(F.conv1d(x, w, padding=1),
+                               torch.conv1d(x, w, None, 1, 1, 1, 1))
+    y = F.conv1d(x.to(cuda), w.to(cuda), padding=1)
+    torch.testing.assert_close(y.cpu(), torch.conv1d(x, w, None, 1, 1, 1, 1), rtol=1e-4, atol=1e-4)
+
+
+def test_disable_restores_stock(cuda):
+    import amd_tuned_torch
+    stock = (F.conv1d, F.conv3d, F.group_norm)
+    amd_tuned_torch.enable()
+    assert F.conv3d is not stock[1]
+    amd_tuned_torch.disable()
+    assert (F.conv1d, F.conv3d, F.group_norm) == stock

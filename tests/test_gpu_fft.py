@@ -1,0 +1,95 @@
+"""Parity of the FFT convolution kernels with the oracle: the reference's own
+FFT route outputs (tests/golden) at small sizes, the float64 numpy
+restatement of that route at other sizes, and at the BASELINE size a slice of
+the full-size output (the per-channel computation is independent of the
+others, so a slice checks the full-size launch).  FFT-route bar: rel-L2 <= 5e-3."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import load_golden, torch_dtype
+
+pytestmark = pytest.mark.gpu
+
+FFT_TOL = 5e-3
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _kaiming(shape, g):
+    bound = 1.0 / math.sqrt(math.prod(shape[1:]))
+    return (torch.rand(*shape, generator=g) * 2 - 1) * bound
+
+
+@pytest.mark.parametrize("case", list(load_golden("fftconv1d")))
+def test_fftconv1d_golden(cuda, case):
+    from amd_tuned_torch import fftconv_ops
+    d = load_golden("fftconv1d")[case]
+    dt = torch_dtype(d["dtype"])
+    B, C, L, K, pad = (int(v) for v in d["meta"])
+    x = torch.as_tensor(d["x"]).to(cuda, dt)
+    w = torch.as_tensor(d["w"]).to(cuda, dt)
+    b = torch.as_tensor(d["b"]).to(cuda, dt)
+    y = fftconv_ops.fftconv1d(x, w, b, pad)
+    assert y is not None and tuple(y.shape) == d["y"].shape
+    tol = 1e-5 if d["dtype"] == "f32" else FFT_TOL
+    assert oracle.rel_l2(_np(y), d["y_fft"]) <= tol   # the reference's FFT route
+    assert oracle.rel_l2(_np(y), d["y"]) <= tol       # and direct convolution
+
+
+@pytest.mark.parametrize("B,C,L,K,pad,dt", [
+    (1, 3, 1000, 257, 128, "f32"), (3, 2, 4000, 64, 0, "bf16"), (2, 4, 5000, 999, 499, "f16"),
+    (5, 1, 100, 100, 99, "f32"), (4, 8, 16384, 2048, 1024, "f16"),
+])
+def test_fftconv1d_shapes(cuda, B, C, L, K, pad, dt):
+    from amd_tuned_torch import fftconv_ops
+    g = torch.Generator().manual_seed(L + K)
+    x = torch.randn(B, C, L, generator=g).to(torch_dtype(dt))
+    w = _kaiming((C, 1, K), g).to(torch_dtype(dt))
+    b = torch.randn(C, generator=g).to(torch_dtype(dt))
+    y = fftconv_ops.fftconv1d(x.to(cuda), w.to(cuda), b.to(cuda), pad)
+    ref = oracle.fft_conv_np(x.float().numpy(), w.float().numpy(), b.float().numpy(), (pad,),
+                             groups=C)
+    tol = 1e-5 if dt == "f32" else FFT_TOL
+    assert oracle.rel_l2(_np(y), ref) <= tol
+
+
+def test_fftconv1d_cfg4b_full_size(cuda):
+    """BASELINE cfg 4b: x[16,1024,16384] fp16 ~N(0,1), w[1024,1,2048] kaiming-U,
+    bias, groups 1024, padding 1024 -> L_out 16385.  Checked on a slice of
+    batches/channels against the float64 oracle."""
+    from amd_tuned_torch import fftconv_ops, ops
+    g = torch.Generator().manual_seed(44)
+    x = torch.randn(16, 1024, 16384, generator=g).half()
+    w = _kaiming((1024, 1, 2048), g).half()
+    b = _kaiming((1024, 2048), g)[:, 0].half()
+    y = fftconv_ops.fftconv1d(x.to(cuda), w.to(cuda), b.to(cuda), 1024)
+    assert tuple(y.shape) == (16, 1024, 16385)
+    bs, cs = [0, 7, 15], [0, 1, 511, 1023]
+    xs = x[bs][:, cs].float().numpy()
+    ref = oracle.fft_conv_np(xs, w[cs].float().numpy(), b[cs].float().numpy(), (1024,),
+                             groups=len(cs))
+    got = y[bs][:, cs]
+    assert oracle.rel_l2(_np(got), ref) <= FFT_TOL
+    assert torch.isfinite(y).all()
+    assert ops.read_device_flags() == 0
+
+
+def test_fftconv1d_spectrum_cache_follows_weight(cuda):
+    """A new weight at a reused address must get its own spectrum."""
+    from amd_tuned_torch import fftconv_ops
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 4, 500, generator=g).to(cuda)
+    for s in range(3):
+        w = torch.randn(4, 1, 65, generator=torch.Generator().manual_seed(s)).to(cuda)
+        y = fftconv_ops.fftconv1d(x, w, None, 32)
+        ref = oracle.fft_conv_np(x.cpu().numpy(), w.cpu().numpy(), None, (32,), groups=4)
+        assert oracle.rel_l2(_np(y), ref) <= 1e-5
+        del w
