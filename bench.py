@@ -228,7 +228,8 @@ def per_shape(dev, peaks) -> dict:
     byt = 134219776
     best = None
     for name, var in (("auto", ops.GN_AUTO), ("cluster4", ops.gn_cluster_variant(4)),
-                      ("cluster8", ops.gn_cluster_variant(8)), ("split", ops.GN_SPLIT)):
+                      ("cluster8", ops.gn_cluster_variant(8)),
+                      ("cluster16", ops.gn_cluster_variant(16)), ("split", ops.GN_SPLIT)):
         y = ops.group_norm(xs[0], 32, wd, bd, 1e-6, variant=var)
         if y is None:
             continue
@@ -242,6 +243,48 @@ def per_shape(dev, peaks) -> dict:
                "rel_l2": err}
         out[f"cfg3_group_norm_bf16_{name}"] = rec
     del xs, ys
+    torch.cuda.empty_cache()
+
+    # cfg4b: long-filter depthwise conv1d fp16 [16,1024,16384] k2048 p1024 (FFT route)
+    from amd_tuned_torch import fftconv_ops
+    g = torch.Generator().manual_seed(44)
+    x = torch.randn(16, 1024, 16384, generator=g).half()
+    w = _kaiming((1024, 1, 2048), g).half()
+    b = _kaiming((1024, 2048), g)[:, 0].half()
+    xs = [x.to(dev) for _ in range(2)]
+    wd, bd = w.to(dev), b.to(dev)
+    y = fftconv_ops.fftconv1d(xs[0], wd, bd, 1024)
+    cs = [0, 511, 1023]
+    ref = torch.nn.functional.conv1d(x[:2, cs].float(), w[cs].float(), b[cs].float(),
+                                     padding=1024, groups=3)
+    err = _rel_l2(y[:2, cs].float().cpu(), ref)
+    ms = _events_time(lambda i: fftconv_ops.fftconv1d(xs[i % 2], wd, bd, 1024), 10, stream)
+    byt = 1077970944
+    out["cfg4b_fftconv1d_fp16"] = {"us_per_op": ms * 1e3, "bound": "hbm",
+                                   "achieved_gbs": byt / (ms * 1e-3) / 1e9,
+                                   "frac": byt / (ms * 1e-3) / 1e9 / hbm,
+                                   "rel_l2_slice": err, "nfft": fftconv_ops.fft_length(18432)}
+    del xs, y
+    torch.cuda.empty_cache()
+
+    # cfg4a: conv3d fp16 [2,64,16,64,64] x [64,64,15,15,15] p7 (FFT route)
+    g = torch.Generator().manual_seed(41)
+    x = torch.randn(2, 64, 16, 64, 64, generator=g).half()
+    w = _kaiming((64, 64, 15, 15, 15), g).half()
+    b = _kaiming((64, 64 * 3375), g)[:, 0].half()
+    xs = [x.to(dev) for _ in range(4)]
+    wd, bd = w.to(dev), b.to(dev)
+    y = fftconv_ops.fft_conv3d(xs[0], wd, bd, padding=7)
+    if y is not None:
+        ms = _events_time(lambda i: fftconv_ops.fft_conv3d(xs[i % 4], wd, bd, padding=7), 10,
+                          stream)
+        byt = 61202560
+        out["cfg4a_fftconv3d_fp16"] = {
+            "us_per_op": ms * 1e3, "bound": "hbm (compulsory I/O)",
+            "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
+            "effective_tflops": 3.624e12 / (ms * 1e-3) / 1e12,
+            "note": "weight spectrum cached (3.2 GB fp32) and streamed once per call"}
+    del xs, y
     torch.cuda.empty_cache()
     return out
 

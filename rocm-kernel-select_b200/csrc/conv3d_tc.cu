@@ -50,6 +50,7 @@ struct ConvParams {
   int BW, BH;
   int tiles_w, tiles_h, tiles_n, num_tiles;
   int cchunks, kblocks;
+  int rotate;
   void* y;
   const void* bias;
   int bias_dt;
@@ -129,9 +130,15 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       uint32_t phase = 0;
       bool ok = true;
       const int taps_hw = p.KH * p.KW;
+      // Each CTA starts its K walk at a different k-block: CTAs in lockstep
+      // would all fetch the same weight box at once (one L2 hot spot); the
+      // rotation spreads them over the taps.  The sum is order-independent.
+      const int rot = p.rotate ? static_cast<int>((blockIdx.x * 7u) % p.kblocks) : 0;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         const TileCoord tc = decode_tile(t, p, BN);
-        for (int kb = 0; kb < p.kblocks; ++kb) {
+        for (int kk = 0; kk < p.kblocks; ++kk) {
+          int kb = kk + rot;
+          if (kb >= p.kblocks) kb -= p.kblocks;
           const int tap = kb / p.cchunks, cc = kb - tap * p.cchunks;
           const int kd = tap / taps_hw, r = tap - kd * taps_hw;
           const int kh = r / p.KW, kw = r - kh * p.KW;
@@ -270,7 +277,63 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ wp, 
 }
 
 // ------------------------------------------------------ NCDHW -> N[S]C ---
-// 64 x 64 tiles of 16-bit elements through shared memory.
+// 16-bit elements, 64 channels x 64 positions per CTA: 16-byte loads along
+// the positions of a channel row, 16-byte stores along the channels of a
+// position.  Shared rows are 66 elements (33 words) so both the 32-bit
+// writes and the 8-channel column gathers spread over the banks.
+template <typename T>
+__global__ void __launch_bounds__(256)
+to_cl16_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t C, int64_t S) {
+  static_assert(sizeof(T) == 2, "16-bit elements");
+  __shared__ uint32_t tile[64 * 33];
+  const int64_t n = blockIdx.z;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 64;
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int v = threadIdx.x & 7;
+  const bool full = (c0 + 64 <= C) && (p0 + 64 <= S);
+  for (int r = threadIdx.x >> 3; r < 64; r += 32) {
+    const int64_t c = c0 + r;
+    uint4 q = make_uint4(0, 0, 0, 0);
+    const int64_t p = p0 + 8 * v;
+    const T* src = x + (n * C + c) * S + p;
+    if (full && (S & 7) == 0) {
+      q = ld_stream16(src);
+    } else if (c < C) {
+      uint16_t e[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        e[k] = (p + k < S) ? reinterpret_cast<const uint16_t*>(src)[k] : uint16_t(0);
+      q = make_uint4(e[0] | (uint32_t(e[1]) << 16), e[2] | (uint32_t(e[3]) << 16),
+                     e[4] | (uint32_t(e[5]) << 16), e[6] | (uint32_t(e[7]) << 16));
+    }
+    uint32_t* row = tile + r * 33 + 4 * v;
+    row[0] = q.x;
+    row[1] = q.y;
+    row[2] = q.z;
+    row[3] = q.w;
+  }
+  __syncthreads();
+  const uint16_t* t16 = reinterpret_cast<const uint16_t*>(tile);
+  for (int qp = threadIdx.x >> 3; qp < 64; qp += 32) {
+    const int64_t p = p0 + qp;
+    if (p >= S) continue;
+    uint16_t e[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) e[k] = t16[(8 * v + k) * 66 + qp];
+    T* dst = y + (n * S + p) * C + c0 + 8 * v;
+    if (full && (C & 7) == 0) {
+      *reinterpret_cast<uint4*>(dst) =
+          make_uint4(e[0] | (uint32_t(e[1]) << 16), e[2] | (uint32_t(e[3]) << 16),
+                     e[4] | (uint32_t(e[5]) << 16), e[6] | (uint32_t(e[7]) << 16));
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (c0 + 8 * v + k < C) reinterpret_cast<uint16_t*>(dst)[k] = e[k];
+    }
+  }
+}
+
+// Generic element type (fp32): 64 x 64 tile of scalars.
 template <typename T>
 __global__ void __launch_bounds__(256)
 to_cl_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t C, int64_t S) {
@@ -358,7 +421,10 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
               static_cast<unsigned>(N));
     if ((S + 63) / 64 > 0x7fffffffLL || (Cin + 63) / 64 > 65535)
       return fail_unsupported("transpose grid too large");
-    to_cl_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
+    if (aligned16(x) && aligned16(ws))
+      to_cl16_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
+    else
+      to_cl_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
     B200_LAUNCH_CHECK("to_cl_kernel");
     xcl = ws;
   }
@@ -426,6 +492,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   prm.num_tiles = (int)nt;
   prm.cchunks = (int)(Cin_pad / kBK);
   prm.kblocks = (int)(taps * prm.cchunks);
+  prm.rotate = ((variant >> 8) & 1) ? 0 : 1;   // variant bit 8 disables the k rotation
   prm.y = y;
   prm.bias = bias;
   prm.bias_dt = bias_dt;
@@ -507,10 +574,16 @@ int b200_to_channels_last(const void* x, void* y, int dtype, int64_t N, int64_t 
   dim3 grid(static_cast<unsigned>((S + 63) / 64), static_cast<unsigned>((C + 63) / 64),
             static_cast<unsigned>(N));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool al = aligned16(x) && aligned16(y);
   if (dtype == B200_DTYPE_F32)
     to_cl_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), static_cast<float*>(y), C, S);
+  else if (dtype == B200_DTYPE_F16 && al)
+    to_cl16_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y), C, S);
   else if (dtype == B200_DTYPE_F16)
     to_cl_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y), C, S);
+  else if (dtype == B200_DTYPE_BF16 && al)
+    to_cl16_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                      static_cast<__nv_bfloat16*>(y), C, S);
   else if (dtype == B200_DTYPE_BF16)
     to_cl_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                     static_cast<__nv_bfloat16*>(y), C, S);

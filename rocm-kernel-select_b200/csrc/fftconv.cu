@@ -193,22 +193,4 @@ int b200_fftconv1d_fwd(const void* x, const void* spectrum, const void* bias, vo
   return B200_OK;
 }
 
-// ------------------------------------------------------------ conv3d (TBD)
-size_t b200_fftconv3d_spectrum_bytes(int64_t Cout, int64_t Cin, int64_t fd, int64_t fh,
-                                     int64_t fw) {
-  return static_cast<size_t>(Cout * Cin * fd * fh * (fw / 2 + 1)) * sizeof(float2);
-}
-int b200_fftconv3d_prepare(const void*, void*, int, int64_t, int64_t, int64_t, int64_t, int64_t,
-                           int64_t, int64_t, int64_t, void*, size_t, void*) {
-  return fail_unsupported("fftconv3d not built");
-}
-size_t b200_fftconv3d_workspace_bytes(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t) {
-  return 0;
-}
-int b200_fftconv3d_fwd(const void*, const void*, const void*, void*, int, int, int64_t, int64_t,
-                       int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                       const int64_t*, int64_t, int64_t, int64_t, void*, size_t, void*) {
-  return fail_unsupported("fftconv3d not built");
-}
-
 }  // extern "C"

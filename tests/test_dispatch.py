@@ -1,0 +1,189 @@
+"""Dispatch logic on CPU with the native ops replaced by fakes (the reference
+does the same with MagicMock natives, tests/conftest.py:44-95 there): install
+set, routing, eligibility, the autograd wrappers and GroupNorm's backward math."""
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import amd_tuned_torch
+from amd_tuned_torch import _dispatch, conv1d_dispatch, kernel_select, ops
+
+STOCK = (F.conv1d, F.conv3d, F.group_norm)
+
+
+@pytest.fixture
+def patched():
+    amd_tuned_torch.enable()
+    yield
+    amd_tuned_torch.disable()
+
+
+@pytest.fixture
+def force_eligible(monkeypatch):
+    """CPU tensors reach the native branches; natives are recording fakes."""
+    calls = []
+    monkeypatch.setattr(_dispatch, "_usable", lambda *a, **k: True)
+    monkeypatch.setattr(_dispatch._lib, "available", lambda: True)
+    monkeypatch.setattr(kernel_select, "_ENABLED", False)
+
+    def fake_gn(x, G, w, b, eps, variant=0, out=None):
+        calls.append(("group_norm", variant))
+        return STOCK[2](x, G, w, b, eps)
+
+    def fake_conv3d(x, w, b, stride, padding, dilation, variant=0, x_channels_last=False,
+                    out_channels_last=False, out=None):
+        calls.append(("conv3d", x_channels_last))
+        if x_channels_last:
+            x = x.permute(0, 4, 1, 2, 3)
+        y = STOCK[1](x, w, b, stride, padding, dilation)
+        return y.permute(0, 2, 3, 4, 1).contiguous() if out_channels_last else y
+
+    monkeypatch.setattr(ops, "group_norm", fake_gn)
+    monkeypatch.setattr(ops, "conv3d", fake_conv3d)
+    return calls
+
+
+def test_enable_disable_install_set():
+    assert not amd_tuned_torch.is_enabled()
+    amd_tuned_torch.enable()
+    try:
+        assert amd_tuned_torch.is_enabled()
+        assert F.conv3d is _dispatch._patched_conv3d
+        assert F.group_norm is _dispatch._patched_group_norm
+        assert getattr(F.conv1d, "_amd_tuned_torch_wrapper", False)
+        amd_tuned_torch.enable()                    # idempotent
+        assert F.conv3d is _dispatch._patched_conv3d
+    finally:
+        amd_tuned_torch.disable()
+    assert (F.conv1d, F.conv3d, F.group_norm) == STOCK
+    assert not amd_tuned_torch.is_enabled()
+    amd_tuned_torch.disable()                       # idempotent
+
+
+def test_conv1d_fallback_toggle_is_independent():
+    conv1d_dispatch.enable_conv1d_fallback()
+    try:
+        assert conv1d_dispatch.is_conv1d_fallback_enabled()
+        amd_tuned_torch.enable()                    # does not double-wrap
+        amd_tuned_torch.disable()
+        assert conv1d_dispatch.is_conv1d_fallback_enabled()
+    finally:
+        conv1d_dispatch.disable_conv1d_fallback()
+    assert F.conv1d is STOCK[0]
+
+
+def test_cpu_tensors_go_to_stock(patched):
+    x = torch.randn(2, 8, 4, 4)
+    torch.testing.assert_close(F.group_norm(x, 4), STOCK[2](x, 4))
+    x3 = torch.randn(1, 4, 3, 5, 5)
+    w3 = torch.randn(2, 4, 3, 3, 3)
+    torch.testing.assert_close(F.conv3d(x3, w3, padding=1), STOCK[1](x3, w3, padding=1))
+    x1 = torch.randn(2, 4, 16)
+    w1 = torch.randn(4, 1, 3)
+    torch.testing.assert_close(F.conv1d(x1, w1, padding=1, groups=4),
+                               STOCK[0](x1, w1, padding=1, groups=4))
+
+
+def test_group_norm_routes_to_native(patched, force_eligible):
+    x = torch.randn(2, 8, 4, 4)
+    F.group_norm(x, 4, torch.ones(8), torch.zeros(8))
+    assert force_eligible[0][0] == "group_norm"
+
+
+def test_group_norm_non_contiguous_goes_to_stock(patched, force_eligible):
+    x = torch.randn(2, 4, 4, 8).permute(0, 3, 1, 2)
+    y = F.group_norm(x, 4)
+    assert not force_eligible
+    torch.testing.assert_close(y, STOCK[2](x, 4))
+
+
+def test_conv3d_routes_to_tensor_cores_and_channels_last(patched, force_eligible):
+    x = torch.randn(1, 8, 3, 4, 4)
+    w = torch.randn(8, 8, 3, 3, 3)
+    y = F.conv3d(x, w, None, 1, 1)
+    assert force_eligible == [("conv3d", False)]
+    xcl = x.contiguous(memory_format=torch.channels_last_3d)
+    y2 = F.conv3d(xcl, w, None, 1, 1)
+    assert force_eligible[-1] == ("conv3d", True)
+    assert y2.is_contiguous(memory_format=torch.channels_last_3d)
+    torch.testing.assert_close(y2, y)
+
+
+def test_grouped_conv3d_goes_to_stock(patched, force_eligible):
+    x = torch.randn(1, 8, 3, 4, 4)
+    w = torch.randn(8, 4, 3, 3, 3)
+    F.conv3d(x, w, None, 1, 1, 1, 2)
+    assert not force_eligible
+
+
+def test_conv3d_with_grad_uses_autograd_wrapper(patched, force_eligible):
+    x = torch.randn(1, 4, 3, 4, 4, requires_grad=True)
+    w = torch.randn(4, 4, 3, 3, 3, requires_grad=True)
+    y = F.conv3d(x, w, None, 1, 1)
+    assert y.grad_fn is not None and "Conv3dFn" in type(y.grad_fn).__name__
+    y.sum().backward()
+    x2 = x.detach().requires_grad_()
+    w2 = w.detach().requires_grad_()
+    STOCK[1](x2, w2, None, 1, 1).sum().backward()
+    torch.testing.assert_close(x.grad, x2.grad)
+    torch.testing.assert_close(w.grad, w2.grad)
+
+
+def test_tensor_subclass_is_not_plain():
+    class Sub(torch.Tensor):
+        pass
+    t = torch.zeros(2).as_subclass(Sub)
+    assert not _dispatch._is_plain_tensor(t)
+    assert _dispatch._is_plain_tensor(torch.zeros(2))
+    assert _dispatch._is_plain_tensor(torch.nn.Parameter(torch.zeros(2)))
+
+
+def test_grad_safe():
+    a = torch.zeros(2, requires_grad=True)
+    assert not _dispatch._grad_safe(a)
+    with torch.no_grad():
+        assert _dispatch._grad_safe(a)
+    with torch.inference_mode():
+        assert _dispatch._grad_safe(torch.zeros(2))
+
+
+def test_depthwise_eligibility():
+    elig = conv1d_dispatch._is_depthwise_conv1d_eligible
+    x = torch.randn(2, 8, 32)
+    w = torch.randn(8, 1, 4)
+    assert not elig(x, w, 1, 1, 8)     # CPU tensor
+    x.is_cuda  # noqa: B018
+    meta = torch.empty(2, 8, 32, device="meta")
+    assert not elig(meta, w, 1, 1, 8)
+
+
+# ---------------------------------------------------- GroupNorm backward math
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+@pytest.mark.parametrize("affine", [True, False])
+def test_group_norm_backward_matches_autograd(dtype, affine):
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(2, 8, 5, 3, generator=g, dtype=dtype, requires_grad=True)
+    w = (torch.rand(8, generator=g, dtype=dtype) + 0.5).requires_grad_() if affine else None
+    b = torch.randn(8, generator=g, dtype=dtype).requires_grad_() if affine else None
+    dy = torch.randn(2, 8, 5, 3, generator=g, dtype=dtype)
+    STOCK[2](x, 4, w, b, 1e-5).backward(dy)
+    gx, gw, gb = _dispatch._group_norm_backward(dy, x.detach(), 4,
+                                                w.detach() if affine else None, 1e-5,
+                                                (True, affine, affine))
+    tol = dict(rtol=1e-4, atol=1e-5) if dtype == torch.float32 else dict(rtol=1e-9, atol=1e-10)
+    torch.testing.assert_close(gx, x.grad, **tol)
+    if affine:
+        torch.testing.assert_close(gw, w.grad, **tol)
+        torch.testing.assert_close(gb, b.grad, **tol)
+
+
+def test_group_norm_backward_fp16_large_group_no_overflow():
+    """A large fp16 group must not overflow the reductions (fp32 accumulation)."""
+    x = torch.randn(1, 32, 64, 64).half() * 4
+    dy = torch.randn_like(x)
+    gx, gw, gb = _dispatch._group_norm_backward(dy, x, 1, torch.ones(32).half(), 1e-5,
+                                                (True, True, True))
+    assert torch.isfinite(gx.float()).all() and torch.isfinite(gw.float()).all()
+    assert torch.isfinite(gb.float()).all()

@@ -1,0 +1,248 @@
+"""kernel_select policy, hardware-free: timing is stubbed with a name -> ms
+table and candidates return sentinels, as in the reference's own
+tests/test_kernel_select.py (:44-236 policy, :239-370 verification, :372-414
+persistence, :416-590 out-of-memory handling).  CPU only."""
+from __future__ import annotations
+
+import json
+import os
+
+import pytest
+import torch
+
+from amd_tuned_torch import kernel_select
+
+
+@pytest.fixture(autouse=True)
+def _clean(monkeypatch, tmp_path):
+    monkeypatch.setattr(kernel_select, "_ENABLED", True)
+    monkeypatch.setattr(kernel_select, "_VERIFY_ENABLED", False)
+    monkeypatch.setattr(kernel_select, "_REFERENCE_COMPETES", True)
+    monkeypatch.setattr(kernel_select, "_CACHE_DIR", str(tmp_path))
+    kernel_select.reset()
+    yield
+    kernel_select.reset()
+
+
+@pytest.fixture
+def timings(monkeypatch):
+    calls: dict = {}
+
+    def install(table):
+        def fake_time(fn):
+            calls[fn._name] = calls.get(fn._name, 0) + 1
+            if fn() is None:
+                return None
+            return table.get(fn._name)
+        monkeypatch.setattr(kernel_select, "_time", fake_time)
+        return calls
+    return install
+
+
+def cands(names, declines=(), outputs=None):
+    out = []
+    for n in names:
+        def thunk(n=n):
+            if n in declines:
+                return None
+            return outputs[n] if outputs else f"out:{n}"
+        thunk._name = n
+        out.append((n, thunk))
+    return out
+
+
+def args():
+    return torch.zeros(1, 4, 8, 8, 8), torch.zeros(4, 4, 3, 3, 3), 1, 1, 1
+
+
+def test_fastest_wins_not_first(timings):
+    timings({"tcgen05": 5.0, "fftconv": 9.0, "stock": 1.0})
+    x, w, s, p, d = args()
+    assert kernel_select.pick("conv3d", x, w, s, p, d,
+                              cands(["tcgen05", "fftconv", "stock"])) == "out:stock"
+    assert kernel_select.cached("conv3d", x, w, s, p, d) == "stock"
+
+
+def test_winner_is_cached_per_shape(timings):
+    calls = timings({"a": 1.0, "stock": 2.0})
+    x, w, s, p, d = args()
+    for _ in range(3):
+        assert kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "stock"])) == "out:a"
+    assert calls == {"a": 1, "stock": 1}          # measured once
+    x2 = torch.zeros(2, 4, 8, 8, 8)
+    kernel_select.pick("conv3d", x2, w, s, p, d, cands(["a", "stock"]))
+    assert calls["a"] == 2                         # a new shape is measured again
+
+
+def test_declining_candidate_loses(timings):
+    timings({"a": 0.1, "b": 3.0, "stock": 5.0})
+    x, w, s, p, d = args()
+    out = kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "b", "stock"], declines={"a"}))
+    assert out == "out:b"
+
+
+def test_kill_switch(monkeypatch, timings):
+    monkeypatch.setattr(kernel_select, "_ENABLED", False)
+    x, w, s, p, d = args()
+    assert kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "stock"])) is None
+    assert kernel_select.pick_key("group_norm", ("k",), cands(["a", "stock"])) is None
+    assert kernel_select.cached("conv3d", x, w, s, p, d) is None
+
+
+def test_pick_key(timings):
+    timings({"native": 1.0, "stock": 2.0})
+    key = (torch.bfloat16, (4, 512, 128, 128), 32, False)
+    assert kernel_select.pick_key("group_norm", key, cands(["native", "stock"])) == "out:native"
+    assert kernel_select.cached_key("group_norm", key) == "native"
+
+
+def test_cached_winner_that_declines_is_evicted(timings):
+    calls = timings({"a": 1.0, "stock": 2.0})
+    x, w, s, p, d = args()
+    kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "stock"]))
+    out = kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "stock"], declines={"a"}))
+    assert out == "out:stock"
+    assert kernel_select.cached("conv3d", x, w, s, p, d) == "stock"
+    assert calls["stock"] == 2
+
+
+def test_reference_not_timed_by_default(monkeypatch, timings):
+    """B200 build: own kernels compete, stock only verifies / serves as fallback."""
+    monkeypatch.setattr(kernel_select, "_REFERENCE_COMPETES", False)
+    calls = timings({"a": 5.0, "b": 3.0, "stock": 0.001})
+    x, w, s, p, d = args()
+    assert kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "b", "stock"])) == "out:b"
+    assert "stock" not in calls
+    kernel_select.reset()
+    out = kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "stock"], declines={"a"}))
+    assert out == "out:stock"      # nothing of ours applies: the reference serves it
+    assert kernel_select.cached("conv3d", x, w, s, p, d) == "stock"
+
+
+# ------------------------------------------------------------ verification
+def test_wrong_fast_candidate_is_blacklisted(monkeypatch, timings):
+    monkeypatch.setattr(kernel_select, "_VERIFY_ENABLED", True)
+    good = torch.ones(64, 64)
+    outs = {"bad": good * 2, "good": good + 1e-6, "stock": good}
+    timings({"bad": 1.0, "good": 2.0, "stock": 3.0})
+    x, w, s, p, d = args()
+    with pytest.warns(UserWarning, match="disagrees"):
+        out = kernel_select.pick("conv3d", x, w, s, p, d,
+                                 cands(["bad", "good", "stock"], outputs=outs))
+    assert out is outs["good"]
+    key = kernel_select._key("conv3d", x, w, s, p, d)
+    assert kernel_select.debug_bad_candidates()[key] == {"bad"}
+
+
+def test_verification_bar_scales_with_output_rms():
+    ref = torch.full((1000,), 300.0)
+    ref[0] = 1e-3                     # one near-zero element
+    cand = ref.clone()
+    cand[0] = 2e-3                    # off by 1e-3: fails a plain atol of 1e-5
+    assert kernel_select._verify(cand, ref, tolerance=(1e-4, 1e-5)) is True
+    wrong = ref * 1.01
+    assert kernel_select._verify(wrong, ref, tolerance=(1e-4, 1e-5)) is False
+
+
+def test_verify_shape_mismatch_is_a_failure():
+    assert kernel_select._verify(torch.zeros(3), torch.zeros(4)) is False
+
+
+def test_all_candidates_wrong_falls_back_to_reference(monkeypatch, timings):
+    monkeypatch.setattr(kernel_select, "_VERIFY_ENABLED", True)
+    ref = torch.ones(8, 8)
+    outs = {"a": ref * 3, "b": ref * -1, "stock": ref}
+    timings({"a": 1.0, "b": 2.0, "stock": 3.0})
+    x, w, s, p, d = args()
+    with pytest.warns(UserWarning):
+        out = kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "b", "stock"], outputs=outs))
+    assert out is outs["stock"]
+    assert kernel_select.cached("conv3d", x, w, s, p, d) == "stock"
+
+
+# -------------------------------------------------------------- OOM handling
+def test_oom_during_deciding_run_is_a_decline(monkeypatch, timings):
+    timings({"a": 1.0, "stock": 2.0})
+
+    def oom():
+        raise torch.OutOfMemoryError("CUDA out of memory")
+    oom._name = "a"
+    x, w, s, p, d = args()
+    stock = ("stock", lambda: "out:stock")
+    stock[1]._name = "stock"
+    monkeypatch.setattr(kernel_select, "_time", lambda fn: {"a": 1.0, "stock": 2.0}[fn._name])
+    assert kernel_select.pick("conv3d", x, w, s, p, d, [("a", oom), stock]) == "out:stock"
+
+
+def test_non_oom_errors_propagate_in_the_deciding_run(monkeypatch):
+    def boom():
+        raise RuntimeError("kernel bug")
+    boom._name = "a"
+    ref = lambda: "out:stock"  # noqa: E731
+    ref._name = "stock"
+    monkeypatch.setattr(kernel_select, "_time", lambda fn: 1.0)
+    x, w, s, p, d = args()
+    with pytest.raises(RuntimeError, match="kernel bug"):
+        kernel_select.pick("conv3d", x, w, s, p, d, [("a", boom), ("stock", ref)])
+
+
+def test_oom_while_verifying_records_nothing(monkeypatch, timings):
+    monkeypatch.setattr(kernel_select, "_VERIFY_ENABLED", True)
+    monkeypatch.setattr(kernel_select, "_verify", lambda *a, **k: None)
+    timings({"a": 1.0, "stock": 2.0})
+    x, w, s, p, d = args()
+    with pytest.warns(UserWarning, match="out of memory"):
+        out = kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "stock"]))
+    assert out == "out:stock"
+    assert kernel_select.debug_winners() == {}
+    assert kernel_select.debug_bad_candidates() == {}
+
+
+# --------------------------------------------------------------- persistence
+def test_disk_cache_roundtrip_and_format(timings, monkeypatch):
+    timings({"tcgen05": 1.0, "stock": 2.0})
+    x, w, s, p, d = args()
+    kernel_select.pick("conv3d", x, w, s, p, d, cands(["tcgen05", "stock"]))
+    path = kernel_select._cache_path()
+    raw = json.load(open(path))
+    assert raw["verify_bar"] == kernel_select._VERIFY_BAR_VERSION
+    (k, v), = raw["winners"].items()
+    assert v == "tcgen05"
+    assert json.loads(k)[1] == {"__dtype__": "torch.float32"}
+    assert json.loads(k)[2] == {"__tuple__": [1, 4, 8, 8, 8]}
+    with kernel_select._lock:
+        kernel_select._winners.clear()
+    kernel_select._load_disk_cache()
+    assert kernel_select.cached("conv3d", x, w, s, p, d) == "tcgen05"
+
+
+def test_stale_verify_bar_drops_blacklist_and_its_winners(tmp_path):
+    key_a = kernel_select._key_to_str(("conv3d", torch.float16, (1,), (2,), (1,), (1,), (1,), False))
+    key_b = kernel_select._key_to_str(("group_norm", torch.bfloat16, (4,), 32, False))
+    raw = {"verify_bar": 1, "winners": {key_a: "x", key_b: "y"}, "bad": {key_a: ["z"]}}
+    with open(kernel_select._cache_path(), "w") as f:
+        json.dump(raw, f)
+    kernel_select._load_disk_cache()
+    winners = kernel_select.debug_winners()
+    assert list(winners.values()) == ["y"]
+    assert kernel_select.debug_bad_candidates() == {}
+
+
+def test_flat_legacy_file_and_corrupt_file(tmp_path):
+    key = kernel_select._key_to_str(("conv1d", torch.float32, (1,), (1,), (1,), (1,), (1,), False))
+    with open(kernel_select._cache_path(), "w") as f:
+        json.dump({key: "depthwise"}, f)
+    kernel_select._load_disk_cache()
+    assert "depthwise" in kernel_select.debug_winners().values()
+    with open(kernel_select._cache_path(), "w") as f:
+        f.write("{not json")
+    kernel_select._load_disk_cache()   # must not raise
+
+
+def test_reset_removes_the_file(timings):
+    timings({"a": 1.0, "stock": 2.0})
+    x, w, s, p, d = args()
+    kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "stock"]))
+    assert os.path.exists(kernel_select._cache_path())
+    kernel_select.reset()
+    assert not os.path.exists(kernel_select._cache_path())
