@@ -67,6 +67,19 @@ int b200_gn_fwd(const void* x, const void* gamma, const void* beta, void* y, int
                 int affine_dtype, int64_t N, int64_t C, int64_t S, int64_t G, float eps,
                 int variant, void* workspace, size_t workspace_bytes, void* stream);
 
+/* GroupNorm forward that allocates nothing: same result as b200_gn_fwd's
+ * split variant, with its scratch in a fixed 256 KiB device array inside the
+ * library instead of a caller workspace.  For callers that cannot allocate
+ * device memory (their device memory belongs to their own pool or arena, or
+ * they run in a loop where an allocation is not acceptable).  Limit:
+ * 3 * N * G * (ceil(C/G * S / 65536) + 1) floats <= 65536, else B200_ERR_ARG.
+ * Calls share the array: calls that may overlap on the GPU race.  The first
+ * call on a device resolves the array's address (make it before any stream
+ * capture).  No counterpart in the reference. */
+int b200_gn_fwd_static_scratch(const void* x, const void* gamma, const void* beta, void* y,
+                               int dtype, int affine_dtype, int64_t N, int64_t C, int64_t S,
+                               int64_t G, float eps, void* stream);
+
 /* GroupNorm statistics only: per (n, g) mean and rstd (fp32, [N*G] each).
  * Used by the fused GroupNorm->SiLU->conv3d producer and by the T-sharded
  * stack, which merges per-rank partial statistics.  Partial form: writes

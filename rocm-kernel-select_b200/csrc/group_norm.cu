@@ -23,6 +23,8 @@
 //    the T-sharded stack (partials are (count, mean, M2) triples).
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace cg = cooperative_groups;
@@ -605,3 +607,108 @@ int b200_gn_apply(const void* x, const float* stats, const void* gamma, const vo
 }
 
 }  // extern "C"
+
+// ---------------------------------------------- allocation-free variant ---
+// GroupNorm forward for callers that cannot allocate device memory: an
+// application whose device memory is owned entirely by its own pool or
+// arena (a serving engine's memory planner, a plugin host that forbids
+// third-party allocations), or a latency-critical loop where an allocation
+// and the synchronisation it can imply are not acceptable.  The per-chunk
+// partial statistics and the merged per-group statistics of the split path
+// live in the file-scope device array below instead of a caller workspace.
+//
+// Limits and sharing rules:
+//  * kStaticScratchFloats floats (256 KiB) per device, held by every GPU that
+//    loads this library until the process exits.  The split path needs
+//    3 * N * G * (chunks + 1) floats, chunks = ceil(Cg * S / 65536); calls
+//    that need more are rejected with B200_ERR_ARG and a message.
+//  * Every call uses the same array.  Each slot a call reads was written
+//    earlier by that same call (partials by the statistics kernel, merged
+//    statistics by the merge kernel), so nothing has to start at zero and
+//    a previous call's leftovers are never read.  Calls whose kernels can
+//    overlap on the GPU (different streams without ordering between them)
+//    race on the array and must not be issued.
+//  * The first call on each device resolves the array's device address
+//    with cudaGetSymbolAddress while that device is current; make that
+//    first call before any stream capture begins.
+namespace b200 {
+namespace {
+constexpr int64_t kStaticScratchFloats = 65536;
+}  // namespace
+}  // namespace b200
+
+static __device__ __align__(256) float g_gn_static_scratch[b200::kStaticScratchFloats];
+
+namespace b200 {
+namespace {
+
+// Device address of g_gn_static_scratch on the current device (host code
+// cannot use the symbol itself as a device pointer).  nullptr on failure.
+float* static_scratch_address(cudaError_t* err) {
+  static std::mutex mu;
+  static float* addr[64] = {nullptr};
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    *err = cudaGetSymbolAddress(&p, g_gn_static_scratch);
+    if (*err != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<float*>(p);
+  }
+  return addr[dev];
+}
+
+template <typename T>
+int gn_static_typed(const void* xv, const void* gamma, const void* beta, void* yv, int affine_dt,
+                    const GnShape& sh, float eps, float* scratch, cudaStream_t stream) {
+  const T* x = static_cast<const T*>(xv);
+  T* y = static_cast<T*>(yv);
+  const int64_t stats_floats = sh.groups * 3;
+  const int64_t stats_pad = (stats_floats + 3) / 4 * 4;   // keep partials 16-byte aligned
+  const size_t part_bytes =
+      static_cast<size_t>(kStaticScratchFloats - stats_pad) * sizeof(float);
+  const int rc = launch_stats<T>(x, scratch, sh, scratch + stats_pad, part_bytes, stream);
+  if (rc != B200_OK) return rc;
+  return launch_apply<T>(x, scratch, gamma, beta, y, affine_dt, sh, eps, false, false, stream);
+}
+
+}  // namespace
+}  // namespace b200
+
+extern "C" int b200_gn_fwd_static_scratch(const void* x, const void* gamma, const void* beta,
+                                          void* y, int dtype, int affine_dtype, int64_t N,
+                                          int64_t C, int64_t S, int64_t G, float eps,
+                                          void* stream) {
+  using namespace b200;
+  if (!x || !y) return fail_arg("x/y is NULL");
+  if (!dtype_ok(dtype) || ((gamma || beta) && !dtype_ok(affine_dtype)))
+    return fail_arg("bad dtype");
+  GnShape sh;
+  int rc = check_shape(N, C, S, G, &sh);
+  if (rc != B200_OK) return rc;
+  // Scratch demand of the split path (scalar chunking is the larger case).
+  const int64_t chunk = split_chunk(sh, 1);
+  const int64_t chunks = (sh.M + chunk - 1) / chunk;
+  const int64_t need = (sh.groups * 3 + 3) / 4 * 4 + sh.groups * chunks * 3;
+  if (need > kStaticScratchFloats) {
+    set_last_error("b200_gn_fwd_static_scratch: needs " + std::to_string(need) +
+                   " scratch floats (N*G*(chunks+1)*3), the static array holds " +
+                   std::to_string(kStaticScratchFloats));
+    return B200_ERR_ARG;
+  }
+  cudaError_t err = cudaSuccess;
+  float* scratch = static_scratch_address(&err);
+  if (scratch == nullptr) return fail_cuda(err, "cudaGetSymbolAddress(g_gn_static_scratch)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B200_DTYPE_F32)
+    return gn_static_typed<float>(x, gamma, beta, y, affine_dtype, sh, eps, scratch, s);
+  if (dtype == B200_DTYPE_F16)
+    return gn_static_typed<__half>(x, gamma, beta, y, affine_dtype, sh, eps, scratch, s);
+  return gn_static_typed<__nv_bfloat16>(x, gamma, beta, y, affine_dtype, sh, eps, scratch, s);
+}
