@@ -72,6 +72,18 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
+// fp32 -> bit pattern of a 16-bit float (register-only, no address taken).
+template <typename T>
+__device__ __forceinline__ uint16_t f32_to_bits16(float v);
+template <>
+__device__ __forceinline__ uint16_t f32_to_bits16<__half>(float v) {
+  return __half_as_ushort(__float2half_rn(v));
+}
+template <>
+__device__ __forceinline__ uint16_t f32_to_bits16<__nv_bfloat16>(float v) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
 // Loads one parameter (gamma/beta/bias/weight) of runtime dtype `dt` as fp32.
 __device__ __forceinline__ float load_param(const void* p, int dt, int64_t i) {
   if (dt == B200_DTYPE_F32) return __ldg(reinterpret_cast<const float*>(p) + i);

@@ -30,6 +30,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -41,7 +42,7 @@ namespace {
 constexpr int kConvThreads = 192;  // 6 warps
 constexpr int kBM = 128;
 constexpr int kBK = 64;            // channels per k-block (one 128-byte swizzle row)
-constexpr int kABytes = kBM * kBK * 2;
+constexpr int kMaxStages = 8;
 
 struct ConvParams {
   int Do, Ho, Wo, Cout;
@@ -50,11 +51,14 @@ struct ConvParams {
   int BW, BH;
   int tiles_w, tiles_h, tiles_n, num_tiles;
   int cchunks, kblocks;
+  int khg, khb;                 // kh taps per k-block (1 or KH), kh blocks = KH / khg
+  int a_bytes, stage_bytes, stages;
   int rotate;
   void* y;
   const void* bias;
   int bias_dt;
   int y_cl;
+  int out_tma;
   int* flags;
 };
 
@@ -78,23 +82,26 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const ConvParams& p, int
   return c;
 }
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
-                 const ConvParams p) {
-  constexpr int kBBytes = BN * kBK * 2;
-  constexpr int kStage = kABytes + kBBytes;
+                 const __grid_constant__ CUtensorMap tmy, const ConvParams p) {
+  constexpr int kBTap = BN * kBK * 2;      // one tap's weight box
+  constexpr int kOutBytes = kBM * BN * 2;
   constexpr uint32_t kIdesc = umma_idesc_f16(sizeof(T) == 2 && std::is_same<T, __half>::value ? 0 : 1, kBM, BN);
   constexpr uint32_t kTmemCols = 2 * BN;
+  const int STAGES = p.stages;
 
+  // Stage s = [A box: a_bytes][B boxes: khg * kBTap], every piece 1024-byte
+  // aligned (the 128-byte swizzle atom), then the output staging tile.
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStage);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;  // [2]
+  uint8_t* sOut = smem + STAGES * p.stage_bytes;                   // [BN][128] staging
+  float* sBias = reinterpret_cast<float*>(sOut + kOutBytes);       // [BN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sBias + BN);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* tfull = empty + kMaxStages;  // [2]
   uint64_t* tempty = tfull + 2;      // [2]
   uint64_t* drain = tempty + 2;      // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -105,7 +112,8 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmx);
     prefetch_tmap(&tmw);
-    for (int s = 0; s < STAGES; ++s) {
+    if (p.out_tma) prefetch_tmap(&tmy);
+    for (int s = 0; s < kMaxStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -125,47 +133,62 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    // The whole warp walks the loop (waits included) so it stays converged;
+    // one lane issues the copies.
+    {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      const int taps_hw = p.KH * p.KW;
-      // Each CTA starts its K walk at a different k-block: CTAs in lockstep
-      // would all fetch the same weight box at once (one L2 hot spot); the
-      // rotation spreads them over the taps.  The sum is order-independent.
+      // k-block = (kd, kh block, kw, 64-channel chunk).  One A box of
+      // BH + (khg - 1) * dh input rows serves the khg kh-taps of the block
+      // (tap j reads the rows starting j * dh rows down); one weight box per
+      // tap.  Each CTA starts its K walk at a different k-block: CTAs in
+      // lockstep would all fetch the same weight box at once (an L2 hot
+      // spot); the sum is order-independent.
       const int rot = p.rotate ? static_cast<int>((blockIdx.x * 7u) % p.kblocks) : 0;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         const TileCoord tc = decode_tile(t, p, BN);
         for (int kk = 0; kk < p.kblocks; ++kk) {
           int kb = kk + rot;
           if (kb >= p.kblocks) kb -= p.kblocks;
-          const int tap = kb / p.cchunks, cc = kb - tap * p.cchunks;
-          const int kd = tap / taps_hw, r = tap - kd * taps_hw;
-          const int kh = r / p.KW, kw = r - kh * p.KW;
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, p.flags, 1)) {
+          const int cc = kb % p.cchunks;
+          int r = kb / p.cchunks;
+          const int kw = r % p.KW;
+          r /= p.KW;
+          const int hb = r % p.khb, kd = r / p.khb;
+          const bool got = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, p.flags, 1);
+          if (!__all_sync(0xffffffffu, got)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&full[stage], kStage);
-          tma_load_5d(sA + stage * kABytes, &tmx, &full[stage], cc * kBK,
-                      tc.ow0 - p.pw + kw * p.dw, tc.oh0 - p.ph + kh * p.dh,
-                      tc.od - p.pd + kd * p.dd, tc.n);
-          tma_load_3d(sB + stage * kBBytes, &tmw, &full[stage], cc * kBK, tc.n0, tap);
+          if (lane == 0) {
+            uint8_t* st = smem + stage * p.stage_bytes;
+            mbar_expect_tx(&full[stage], p.stage_bytes);
+            tma_load_5d(st, &tmx, &full[stage], cc * kBK, tc.ow0 - p.pw + kw * p.dw,
+                        tc.oh0 - p.ph + hb * p.khg * p.dh, tc.od - p.pd + kd * p.dd, tc.n);
+            for (int j = 0; j < p.khg; ++j) {
+              const int tap = (kd * p.KH + hb * p.khg + j) * p.KW + kw;
+              tma_load_3d(st + p.a_bytes + j * kBTap, &tmw, &full[stage], cc * kBK, tc.n0, tap);
+            }
+          }
+          __syncwarp();
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         // Let the loads already issued land before shared memory goes away.
         const int last = (stage + STAGES - 1) % STAGES;
         mbar_wait_bounded(&full[last], (stage == 0 ? phase ^ 1u : phase), nullptr, nullptr, 0);
       }
+      __syncwarp();
     }
   } else if (warp == 1) {
     // -------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // Converged warp; lane 0 issues the MMAs and commits.
+    {
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -173,53 +196,82 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++it) {
         const int acc = it & 1;
         const uint32_t aphase = static_cast<uint32_t>(it >> 1) & 1u;
-        if (!mbar_wait_bounded(&tempty[acc], aphase ^ 1u, abort, p.flags, 1)) {
+        const bool free_acc = mbar_wait_bounded(&tempty[acc], aphase ^ 1u, abort, p.flags, 1);
+        if (!__all_sync(0xffffffffu, free_acc)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, abort, p.flags, 1)) {
+          const bool got = mbar_wait_bounded(&full[stage], phase, abort, p.flags, 1);
+          if (!__all_sync(0xffffffffu, got)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * kABytes));
-          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * kBBytes));
+          if (lane == 0) {
+            const uint8_t* st = smem + stage * p.stage_bytes;
+            const uint32_t a_row_step = static_cast<uint32_t>(p.dh * p.BW * kBK * 2);
+            for (int j = 0; j < p.khg; ++j) {
+              // Tap j: A rows start j * dh input rows down (a multiple of 8
+              // rows, so the swizzle atoms stay aligned); its own B box.
+              const uint64_t adesc = umma_desc_sw128(smem_u32(st) + j * a_row_step);
+              const uint64_t bdesc = umma_desc_sw128(smem_u32(st + p.a_bytes + j * kBTap));
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            // +32 bytes along K inside the swizzled 128-byte row = +2 in the
-            // descriptor's address field.
-            umma_f16_ss(d_tmem, adesc + static_cast<uint64_t>(2 * k),
-                        bdesc + static_cast<uint64_t>(2 * k), kIdesc,
-                        (kb > 0 || k > 0) ? 1u : 0u);
+              for (int k = 0; k < kBK / 16; ++k) {
+                // +32 bytes along K inside the swizzled 128-byte row = +2 in
+                // the descriptor's address field.
+                umma_f16_ss(d_tmem, adesc + static_cast<uint64_t>(2 * k),
+                            bdesc + static_cast<uint64_t>(2 * k), kIdesc,
+                            (kb > 0 || j > 0 || k > 0) ? 1u : 0u);
+              }
+            }
+            umma_commit(&empty[stage]);
           }
-          umma_commit(&empty[stage]);
+          __syncwarp();
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (ok) umma_commit(&tfull[acc]);
+        if (ok && lane == 0) umma_commit(&tfull[acc]);
+        __syncwarp();
       }
       // Drain: every MMA issued above has completed once `drain` flips.
-      umma_commit(drain);
+      if (lane == 0) umma_commit(drain);
+      __syncwarp();
       mbar_wait_bounded(drain, 0, nullptr, nullptr, 0);
+      __syncwarp();
     }
   } else {
     // ---------------------------------------------------------- epilogue
+    // TMEM -> registers (+ bias) -> either a shared staging tile written by
+    // one TMA tensor store (NCDHW output whose rows TMA can address), or
+    // direct global stores.  Warps 2-5 synchronise on named barrier 1.
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
+    const int etid = threadIdx.x - 64;
     int it = 0;
     T* y = static_cast<T*>(p.y);
+    uint16_t* stage16 = reinterpret_cast<uint16_t*>(sOut);
     const int64_t plane = static_cast<int64_t>(p.Ho) * p.Wo;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t aphase = static_cast<uint32_t>(it >> 1) & 1u;
-      if (!mbar_wait_bounded(&tfull[acc], aphase, abort, p.flags, 1)) break;
+      // All 128 threads leave together or not at all (a named barrier
+      // follows); the vote also orders this tile after the previous tile's
+      // readers of sBias / staging.
+      const bool got = mbar_wait_bounded(&tfull[acc], aphase, abort, p.flags, 1);
+      if (!epi_bar_and(got)) break;
       tc_fence_after();
       const TileCoord tc = decode_tile(t, p, BN);
+      for (int j = etid; j < BN; j += 128) {
+        const int co = tc.n0 + j;
+        sBias[j] = (p.bias && co < p.Cout) ? load_param(p.bias, p.bias_dt, co) : 0.f;
+      }
+      if (p.out_tma && etid == 0) bulk_wait_read0();  // staging free again
+      epi_bar();
       const int oh = tc.oh0 + row / p.BW, ow = tc.ow0 + row % p.BW;
       const bool valid = oh < p.Ho && ow < p.Wo;
       const uint32_t taddr =
@@ -227,30 +279,53 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       const int64_t pos = (static_cast<int64_t>(tc.od) * p.Ho + oh) * p.Wo + ow;
 #pragma unroll 1
       for (int j0 = 0; j0 < BN; j0 += 32) {
-        float v0[16], v1[16];
+        float v0[16], v1[16], v[32];
         tmem_ld16(taddr + j0, v0);
         tmem_ld16(taddr + j0 + 16, v1);
         tmem_ld_wait();
-        if (valid) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = (j < 16 ? v0[j] : v1[j - 16]) + sBias[j0 + j];
+        if (p.out_tma) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) stage16[(j0 + j) * kBM + row] = f32_to_bits16<T>(v[j]);
+        } else if (valid && p.y_cl) {
+          T* dst = y + (static_cast<int64_t>(tc.n) * p.Do * plane + pos) * p.Cout + tc.n0 + j0;
+          const bool vec = tc.n0 + j0 + 32 <= p.Cout && (p.Cout & 7) == 0;
+          if (vec) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = v[8 * q + e];
+              *reinterpret_cast<uint4*>(dst + 8 * q) = pack16<T>(f);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (tc.n0 + j0 + j < p.Cout) dst[j] = from_f32<T>(v[j]);
+          }
+        } else if (valid) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int co = tc.n0 + j0 + j;
-            if (co < p.Cout) {
-              float v = j < 16 ? v0[j] : v1[j - 16];
-              if (p.bias) v += load_param(p.bias, p.bias_dt, co);
-              int64_t off;
-              if (p.y_cl)
-                off = (static_cast<int64_t>(tc.n) * p.Do * plane + pos) * p.Cout + co;
-              else
-                off = ((static_cast<int64_t>(tc.n) * p.Cout + co) * p.Do) * plane + pos;
-              y[off] = from_f32<T>(v);
-            }
+            if (co < p.Cout)
+              y[((static_cast<int64_t>(tc.n) * p.Cout + co) * p.Do) * plane + pos] =
+                  from_f32<T>(v[j]);
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      mbar_arrive(&tempty[acc]);  // accumulator drained: the MMA warp may reuse it
+      if (p.out_tma) {
+        fence_proxy_async();        // staging writes -> visible to the TMA engine
+        epi_bar();
+        if (etid == 0) {
+          tma_store_5d(&tmy, sOut, tc.ow0, tc.oh0, tc.od, tc.n0, tc.n);
+          bulk_commit();
+        }
+      }
     }
+    if (p.out_tma && etid == 0) bulk_wait_all0();
   }
 
   tc_fence_before();
@@ -368,16 +443,23 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-template <typename T, int BN, int STAGES>
-int launch_conv(const CUtensorMap& tmx, const CUtensorMap& tmw, const ConvParams& prm,
-                cudaStream_t stream) {
-  constexpr int kStage = kABytes + BN * kBK * 2;
-  constexpr size_t smem = static_cast<size_t>(STAGES) * kStage + 1024 + 256;
-  auto kern = conv3d_tc_kernel<T, BN, STAGES>;
+// Shared memory besides the stages: output staging, bias, barriers, and the
+// slack for aligning the dynamic base to 1024 bytes.
+constexpr size_t fixed_smem(int BN) {
+  return static_cast<size_t>(kBM) * BN * 2 + BN * 4 + (2 * kMaxStages + 5) * 8 + 8 + 1024;
+}
+constexpr size_t kSmemBudget = 232448;  // sm_100 opt-in maximum per CTA
+
+template <typename T, int BN>
+int launch_conv(const CUtensorMap& tmx, const CUtensorMap& tmw, const CUtensorMap& tmy,
+                const ConvParams& prm, cudaStream_t stream) {
+  const size_t smem = static_cast<size_t>(prm.stages) * prm.stage_bytes + fixed_smem(BN);
+  if (smem > kSmemBudget) return fail_unsupported("conv3d stage geometry exceeds shared memory");
+  auto kern = conv3d_tc_kernel<T, BN>;
   B200_CUDA_CHECK(
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int grid = std::min(prm.num_tiles, sm_count());
-  kern<<<grid, kConvThreads, smem, stream>>>(tmx, tmw, prm);
+  kern<<<grid, kConvThreads, smem, stream>>>(tmx, tmw, tmy, prm);
   B200_LAUNCH_CHECK("conv3d_tc_kernel");
   return B200_OK;
 }
@@ -440,9 +522,34 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     BW = 8;
     while (BW < Wo && BW < 128) BW *= 2;
   }
+  if (BW < 8) return fail_arg("conv3d tile width must be >= 8");
   const int BH = kBM / BW;
   const int64_t Cin_pad = (Cin + kBK - 1) / kBK * kBK;
   const int64_t taps = KD * KH * KW;
+
+  // kh grouping: one A box of BH + (KH - 1) * dh rows serves all KH taps of a
+  // (kd, kw) pair -- half the input traffic and a third of the pipeline
+  // hand-offs of one box per tap -- when it still leaves >= 3 stages.
+  // Variant bits 10-11: 1 = one tap per k-block, 2 = grouped whenever it fits.
+  const int kgmode = (variant >> 10) & 3;
+  const size_t btap = static_cast<size_t>(BN) * kBK * 2;
+  const size_t budget = kSmemBudget - fixed_smem(BN);
+  auto geom = [&](int khg, int* stages, int* a_bytes, int* stage_bytes) {
+    const int64_t rows = BH + (khg - 1) * dh;
+    if (rows > 256) return false;
+    *a_bytes = static_cast<int>(rows * BW * kBK * 2);
+    *stage_bytes = *a_bytes + khg * static_cast<int>(btap);
+    *stages = static_cast<int>(std::min<size_t>(kMaxStages, budget / *stage_bytes));
+    return *stages >= 2;
+  };
+  int khg = 1, stages = 0, a_bytes = 0, stage_bytes = 0;
+  if (kgmode != 1 && KH > 1 && geom(static_cast<int>(KH), &stages, &a_bytes, &stage_bytes) &&
+      (stages >= 3 || kgmode == 2)) {
+    khg = static_cast<int>(KH);
+  } else if (!geom(1, &stages, &a_bytes, &stage_bytes)) {
+    return fail_unsupported("conv3d tile does not fit in shared memory");
+  }
+  const int a_rows_h = BH + (khg - 1) * static_cast<int>(dh);
 
   CUtensorMap tmx, tmw;
   const CUtensorMapDataType dt =
@@ -451,7 +558,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     cuuint64_t dims[5] = {(cuuint64_t)Cin, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)N};
     cuuint64_t strides[4] = {(cuuint64_t)(Cin * 2), (cuuint64_t)(W * Cin * 2),
                              (cuuint64_t)(H * W * Cin * 2), (cuuint64_t)(D * H * W * Cin * 2)};
-    cuuint32_t box[5] = {(cuuint32_t)kBK, (cuuint32_t)BW, (cuuint32_t)BH, 1, 1};
+    cuuint32_t box[5] = {(cuuint32_t)kBK, (cuuint32_t)BW, (cuuint32_t)a_rows_h, 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = encode(&tmx, dt, 5, const_cast<void*>(xcl), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -491,16 +598,41 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   if (nt > 0x7fffffffLL) return fail_unsupported("too many tiles");
   prm.num_tiles = (int)nt;
   prm.cchunks = (int)(Cin_pad / kBK);
-  prm.kblocks = (int)(taps * prm.cchunks);
+  prm.khg = khg;
+  prm.khb = static_cast<int>(KH) / khg;
+  prm.a_bytes = a_bytes;
+  prm.stage_bytes = stage_bytes;
+  prm.stages = stages;
+  prm.kblocks = static_cast<int>(KD * prm.khb * KW * prm.cchunks);
+  (void)taps;
   prm.rotate = ((variant >> 8) & 1) ? 0 : 1;   // variant bit 8 disables the k rotation
   prm.y = y;
   prm.bias = bias;
   prm.bias_dt = bias_dt;
   prm.y_cl = y_cl;
   prm.flags = device_flags_ptr();
-  if (BN == 64) return launch_conv<T, 64, 8>(tmx, tmw, prm, stream);
-  if (BN == 128) return launch_conv<T, 128, 6>(tmx, tmw, prm, stream);
-  return launch_conv<T, 256, 4>(tmx, tmw, prm, stream);
+
+  // NCDHW output through one TMA store per tile when TMA can address it:
+  // 16-byte aligned base, rows of Wo elements a multiple of 16 bytes.  The
+  // store clips positions and channels outside the output.
+  CUtensorMap tmy;
+  std::memset(&tmy, 0, sizeof(tmy));
+  prm.out_tma = 0;
+  if (!y_cl && aligned16(y) && (Wo % 8) == 0 && ((variant >> 9) & 1) == 0) {
+    cuuint64_t dims[5] = {(cuuint64_t)Wo, (cuuint64_t)Ho, (cuuint64_t)Do, (cuuint64_t)Cout,
+                          (cuuint64_t)N};
+    cuuint64_t strides[4] = {(cuuint64_t)(Wo * 2), (cuuint64_t)(Ho * Wo * 2),
+                             (cuuint64_t)(Do * Ho * Wo * 2), (cuuint64_t)(Cout * Do * Ho * Wo * 2)};
+    cuuint32_t box[5] = {(cuuint32_t)BW, (cuuint32_t)BH, 1, (cuuint32_t)BN, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = encode(&tmy, dt, 5, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    prm.out_tma = (r == CUDA_SUCCESS) ? 1 : 0;
+  }
+  if (BN == 64) return launch_conv<T, 64>(tmx, tmw, tmy, prm, stream);
+  if (BN == 128) return launch_conv<T, 128>(tmx, tmw, tmy, prm, stream);
+  return launch_conv<T, 256>(tmx, tmw, tmy, prm, stream);
 }
 
 }  // namespace
