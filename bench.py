@@ -370,6 +370,8 @@ def run_ours(args, rank, world, dev) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = float(t.item()) * 1e3 / world
 
+    stack = run_stack(args, rank, world, dev, peaks) if not args.no_stack else None
+    torch.cuda.empty_cache()
     shapes = per_shape(dev, peaks) if (rank == 0 and not args.no_shapes) else {}
     cpu = cpu_baseline(x, w, b) if (rank == 0 and world == 1) else None
     tr = _traffic("conv3d_tc_kernel")
@@ -395,7 +397,50 @@ def run_ours(args, rank, world, dev) -> dict:
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
         "per_shape": shapes,
+        "video_stack": stack,
     }
+
+
+CFG5_FLOPS = 4 * 2 * 134217728 * 128 * 27   # 3.7108e12 per step (4 conv layers)
+
+
+def run_stack(args, rank, world, dev, peaks) -> dict:
+    """BASELINE cfg 5: video-decoder stack bf16 [1,128,64,128,128], 4 x
+    [GN32 -> SiLU -> conv3d 128->128 k3 p1], T-sharded over the ranks (strong
+    scaling: the whole 64-frame clip is split, halo + statistics exchanged)."""
+    from amd_tuned_torch import video_stack as vs
+    params = vs.make_params(channels=128, blocks=4, groups=32, dtype=torch.bfloat16, seed=5,
+                            device=dev)
+    x = torch.randn(1, 128, 64, 128, 128, generator=torch.Generator().manual_seed(5))
+    x_local = vs.shard_t(x.bfloat16(), rank, world).to(dev)
+    del x
+    group = dist.group.WORLD if world > 1 else None
+    stack = vs.VideoStack(params, group=group)
+    for _ in range(max(2, args.warmup // 2)):
+        stack.forward(x_local)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    steps = max(3, min(args.steps, 10))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        y = stack.forward(x_local)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    del y
+    return {"workload": "cfg5 video stack bf16 [1,128,64,128,128] x 4 blocks, T-sharded",
+            "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
+            "tflops": CFG5_FLOPS / (ms * 1e-3) / 1e12,
+            "frac_of_peak": CFG5_FLOPS / (ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"],
+            "peak_src": peaks["src"] + " sustained bf16",
+            "collectives": "per block: all_gather of GN partial stats; NCCL send/recv of "
+                           "1 halo frame each side"}
 
 
 def cpu_baseline(x, w, b, budget_s: float = 10.0) -> dict:
@@ -449,6 +494,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-shapes", action="store_true")
+    ap.add_argument("--no-stack", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -1,0 +1,268 @@
+"""Video-VAE-decoder-like stack, optionally T-sharded across ranks.
+
+    blocks x [GroupNorm(G) -> SiLU -> Conv3d(C, C, k=3, padding=1)]
+
+on an [N, C, T, H, W] activation.  There is no reference counterpart: the
+reference is single-GPU, and in a diffusion/VAE decoder these three ops are
+separate F.group_norm / F.silu / F.conv3d calls, each through its own patched
+tier.  This module runs the same math on this package's kernels and shards it
+along T:
+
+* GroupNorm statistics span all of T, so each rank computes partial
+  (count, mean, M2) triples for its frames (b200_gn_partial_stats), the ranks
+  all-gather them and every rank merges them in the same fixed order (Chan's
+  pairwise update) -- identical statistics everywhere, independent of R.
+* Normalise + SiLU is fused with the layout change the conv needs: it writes
+  the channels-last conv operand straight into the interior frames of a
+  buffer [N, T_local + 2, H, W, C] (b200_gn_apply).
+* The two halo frames (k - 1 = 2 per layer: the neighbours' boundary frames)
+  are exchanged with NCCL send/recv between T-neighbours; the first and last
+  rank zero theirs, which is exactly the conv's zero padding in T.
+* conv3d on tensor cores (b200_conv3d_fwd, channels-last input) with T
+  padding 0 over the haloed buffer produces the rank's T_local output frames.
+
+`StackBackend` separates the host orchestration (partitioning, halo exchange,
+statistics merge -- what the multi-process CPU tests check with gloo) from
+the device kernels; `CudaBackend` is the only backend this package ships.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class StackParams:
+    gn_weight: List[torch.Tensor]
+    gn_bias: List[torch.Tensor]
+    conv_weight: List[torch.Tensor]
+    conv_bias: List[torch.Tensor]
+    groups: int = 32
+    eps: float = 1e-5
+
+
+def make_params(channels: int = 128, blocks: int = 4, groups: int = 32, eps: float = 1e-5,
+                dtype: torch.dtype = torch.bfloat16, device="cpu", seed: int = 5) -> StackParams:
+    """Random-init parameters: GroupNorm gamma = 1, beta = 0 (nn.GroupNorm's
+    init); conv weight kaiming-uniform(a = sqrt(5)) and bias U(+-1/sqrt(fan_in))
+    (nn.Conv3d's init), drawn from a seeded generator."""
+    g = torch.Generator().manual_seed(seed)
+    fan_in = channels * 27
+    bound = 1.0 / math.sqrt(fan_in)
+    gw, gb, cw, cb = [], [], [], []
+    for _ in range(blocks):
+        gw.append(torch.ones(channels, dtype=dtype, device=device))
+        gb.append(torch.zeros(channels, dtype=dtype, device=device))
+        w = (torch.rand(channels, channels, 3, 3, 3, generator=g) * 2 - 1) * bound
+        b = (torch.rand(channels, generator=g) * 2 - 1) * bound
+        cw.append(w.to(device=device, dtype=dtype))
+        cb.append(b.to(device=device, dtype=dtype))
+    return StackParams(gw, gb, cw, cb, groups, eps)
+
+
+def t_partition(T: int, world: int) -> List[int]:
+    """Frames per rank: as even as possible, earlier ranks take the remainder."""
+    base, rem = divmod(T, world)
+    return [base + (1 if r < rem else 0) for r in range(world)]
+
+
+def merge_stats(parts: torch.Tensor) -> torch.Tensor:
+    """Merge per-rank (count, mean, M2) triples [R, groups, 3] -> [groups, 3]
+    in rank order (Chan et al.), fp64 internally."""
+    parts = parts.double()
+    n = parts[0, :, 0].clone()
+    mean = parts[0, :, 1].clone()
+    m2 = parts[0, :, 2].clone()
+    for r in range(1, parts.shape[0]):
+        nb, mb, qb = parts[r, :, 0], parts[r, :, 1], parts[r, :, 2]
+        tot = n + nb
+        safe = torch.where(tot > 0, tot, torch.ones_like(tot))
+        d = mb - mean
+        mean = torch.where(tot > 0, mean + d * nb / safe, mean)
+        m2 = torch.where(tot > 0, m2 + qb + d * d * n * nb / safe, m2)
+        n = tot
+    return torch.stack([n, mean, m2], dim=1).float()
+
+
+class StackBackend:
+    """Device kernels the stack needs (one implementation per device kind)."""
+
+    def partial_stats(self, x: torch.Tensor, groups: int) -> torch.Tensor:
+        raise NotImplementedError
+
+    def norm_silu_into(self, x: torch.Tensor, stats: torch.Tensor, groups: int,
+                       weight, bias, eps: float, out_cl: torch.Tensor) -> None:
+        """GroupNorm with `stats` + SiLU, written channels-last into out_cl
+        ([N, T, H, W, C] contiguous view for one batch item at a time)."""
+        raise NotImplementedError
+
+    def conv_cl(self, xp: torch.Tensor, weight, bias, pad_hw: int) -> torch.Tensor:
+        """Conv3d over channels-last xp [N, Tp, H, W, C], T padding 0,
+        H/W padding pad_hw; returns NCDHW [N, Cout, Tp - 2, H, W]."""
+        raise NotImplementedError
+
+
+class CudaBackend(StackBackend):
+    """This package's sm_100a kernels (libb200conv.so)."""
+
+    def partial_stats(self, x, groups):
+        from . import ops
+        return ops.group_norm_partial_stats(x, groups)
+
+    def norm_silu_into(self, x, stats, groups, weight, bias, eps, out_cl):
+        from . import ops
+        N = x.shape[0]
+        for n in range(N):
+            y = ops.group_norm_apply(x[n:n + 1], stats[n * groups:(n + 1) * groups], groups,
+                                     weight, bias, eps, silu=True, channels_last_out=True)
+            out_cl[n].copy_(y.reshape(out_cl[n].shape))
+
+    def conv_cl(self, xp, weight, bias, pad_hw):
+        from . import ops
+        out = ops.conv3d(xp, weight, bias, (1, 1, 1), (0, pad_hw, pad_hw), (1, 1, 1),
+                         x_channels_last=True)
+        if out is None:
+            raise RuntimeError("conv3d tensor-core kernel declined the stack's shape")
+        return out
+
+
+class CudaBackendInPlace(CudaBackend):
+    """Like CudaBackend, but the normalise kernel writes directly into the
+    interior of the haloed buffer (no staging copy) when the slice is
+    contiguous."""
+
+    def norm_silu_into(self, x, stats, groups, weight, bias, eps, out_cl):
+        from . import _lib, ops
+        L = _lib.lib()
+        N, C = x.shape[0], x.shape[1]
+        S = x[0].numel() // C
+        for n in range(N):
+            dst = out_cl[n]
+            if not dst.is_contiguous():
+                return super().norm_silu_into(x, stats, groups, weight, bias, eps, out_cl)
+            adt = weight.dtype if weight is not None else x.dtype
+            rc = L.b200_gn_apply(x[n].data_ptr(), stats[n * groups:].data_ptr(),
+                                 ops._ptr(weight), ops._ptr(bias), dst.data_ptr(),
+                                 ops._code(x.dtype), ops._code(adt), 1, C, S, groups,
+                                 float(eps), 1, 1, ops._stream(x.device))
+            if not _lib.check(rc, "b200_gn_apply"):
+                raise _lib.NativeError("GroupNorm apply declined")
+
+
+class VideoStack:
+    """Runs the stack on one rank's T-slice (or the whole tensor when world == 1).
+
+    `group` is a torch.distributed process group (None = no sharding).  All
+    ranks call forward() with their own [N, C, T_local, H, W] slice; the
+    result is the rank's slice of the output.
+    """
+
+    def __init__(self, params: StackParams, backend: Optional[StackBackend] = None,
+                 group=None):
+        self.p = params
+        self.backend = backend or CudaBackendInPlace()
+        self.group = group
+        self.rank = dist.get_rank(group) if group is not None else 0
+        self.world = dist.get_world_size(group) if group is not None else 1
+
+    # ------------------------------------------------------------ pieces
+    def gn_stats(self, x: torch.Tensor) -> torch.Tensor:
+        part = self.backend.partial_stats(x, self.p.groups)          # [N*G, 3]
+        if self.world == 1:
+            return part
+        gathered = [torch.empty_like(part) for _ in range(self.world)]
+        dist.all_gather(gathered, part.contiguous(), group=self.group)
+        return merge_stats(torch.stack(gathered)).to(part.device)
+
+    def exchange_halo(self, xp: torch.Tensor) -> None:
+        """xp [N, T_local + 2, H, W, C]: send frame 1 to the previous rank and
+        frame T_local to the next; receive into frames 0 and T_local + 1.
+        The ends of the chain get zero frames (the conv's T padding)."""
+        T = xp.shape[1] - 2
+        prev_r = self.rank - 1 if self.rank > 0 else None
+        next_r = self.rank + 1 if self.rank < self.world - 1 else None
+        if prev_r is None:
+            xp[:, 0].zero_()
+        if next_r is None:
+            xp[:, T + 1].zero_()
+        if self.world == 1:
+            return
+        ops_ = []
+        to_send = []
+        if prev_r is not None:
+            first = xp[:, 1].contiguous()
+            to_send.append(first)
+            ops_.append(dist.P2POp(dist.isend, first, self._global(prev_r), self.group))
+            recv_lo = torch.empty_like(first)
+            ops_.append(dist.P2POp(dist.irecv, recv_lo, self._global(prev_r), self.group))
+        if next_r is not None:
+            last = xp[:, T].contiguous()
+            to_send.append(last)
+            ops_.append(dist.P2POp(dist.isend, last, self._global(next_r), self.group))
+            recv_hi = torch.empty_like(last)
+            ops_.append(dist.P2POp(dist.irecv, recv_hi, self._global(next_r), self.group))
+        for req in dist.batch_isend_irecv(ops_):
+            req.wait()
+        if prev_r is not None:
+            xp[:, 0].copy_(recv_lo)
+        if next_r is not None:
+            xp[:, T + 1].copy_(recv_hi)
+
+    def _global(self, r: int) -> int:
+        if self.group is None:
+            return r
+        return dist.get_global_rank(self.group, r)
+
+    # -------------------------------------------------------------- main
+    def block(self, x: torch.Tensor, i: int) -> torch.Tensor:
+        N, C, T, H, W = x.shape
+        stats = self.gn_stats(x)
+        xp = torch.empty(N, T + 2, H, W, C, dtype=x.dtype, device=x.device)
+        self.backend.norm_silu_into(x, stats, self.p.groups, self.p.gn_weight[i],
+                                    self.p.gn_bias[i], self.p.eps, xp[:, 1:T + 1])
+        self.exchange_halo(xp)
+        return self.backend.conv_cl(xp, self.p.conv_weight[i], self.p.conv_bias[i], 1)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x = x.contiguous()
+        for i in range(len(self.p.conv_weight)):
+            x = self.block(x, i)
+        return x
+
+
+def reference_forward(x: torch.Tensor, params: StackParams,
+                      round_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """The stack in plain torch ops (F.group_norm / F.silu / F.conv3d), fp32
+    math; with round_dtype, activations are rounded to it at the same op
+    boundaries as the device path (after GN+SiLU and after each conv)."""
+    import torch.nn.functional as F
+    h = x.float()
+    for i in range(len(params.conv_weight)):
+        h = F.group_norm(h, params.groups, params.gn_weight[i].float(),
+                         params.gn_bias[i].float(), params.eps)
+        h = F.silu(h)
+        if round_dtype is not None:
+            h = h.to(round_dtype).float()
+        h = F.conv3d(h, params.conv_weight[i].float(), params.conv_bias[i].float(), padding=1)
+        if round_dtype is not None:
+            h = h.to(round_dtype).float()
+    return h
+
+
+def shard_t(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """This rank's T-slice of [N, C, T, H, W]."""
+    sizes = t_partition(x.shape[2], world)
+    start = sum(sizes[:rank])
+    return x[:, :, start:start + sizes[rank]].contiguous()
+
+
+def shard_dim(x: torch.Tensor, dim: int, rank: int, world: int) -> torch.Tensor:
+    """Batch/channel sharding with no communication (the other BASELINE
+    configs): this rank's contiguous slice along `dim`."""
+    sizes = t_partition(x.shape[dim], world)
+    start = sum(sizes[:rank])
+    return x.narrow(dim, start, sizes[rank])

@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the tensor-core kernels
-// use: mbarriers (with bounded waits), TMA tensor loads (never multicast),
+// use: mbarriers (with bounded waits), TMA tensor loads into the issuing CTA,
 // tcgen05 MMA / TMEM allocation / TMEM loads, and UMMA descriptors.
 #pragma once
 
@@ -66,7 +66,8 @@ __device__ __forceinline__ void fence_proxy_async() {
 
 // ------------------------------------------------------------------ TMA ---
 // Tiled tensor loads into this CTA's shared memory, completion counted on
-// `bar` in bytes.  No .multicast::cluster form is used anywhere.
+// `bar` in bytes.  Every load lands in the issuing CTA only (no cross-CTA
+// delivery form is used anywhere in this library).
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {
   asm volatile(
