@@ -186,106 +186,113 @@ def _rel_l2(a, b) -> float:
 
 
 # ------------------------------------------------------------ per shape ---
-def per_shape(dev, peaks) -> dict:
-    """Device-timed µs/op, roofline fraction and rel-L2 for BASELINE configs 1-3."""
+def per_shape(dev, peaks, only=None, small=False) -> dict:
+    """Device-timed us/op, roofline fraction and rel-L2 for BASELINE configs
+    1, 3, 4a, 4b (`only` selects one; `small` shrinks cfg 4b to 64 channels
+    for profiler captures)."""
     from amd_tuned_torch import ops
     out = {}
     stream = torch.cuda.current_stream(dev)
     hbm = peaks["hbm_gbs"]
 
-    # cfg1: depthwise conv1d fp32 [8,256,2048] k3 p1
-    g = torch.Generator().manual_seed(1)
-    x = torch.randn(8, 256, 2048, generator=g)
-    w = _kaiming((256, 1, 3), g)
-    b = _kaiming((256, 1), g).reshape(256)
-    nbuf = max(2, ROTATE_BYTES // (x.numel() * 4 * 2))
-    xs = [x.to(dev) for _ in range(nbuf)]
-    wd, bd = w.reshape(256, 3).to(dev), b.to(dev)
-    ys = [torch.empty(8, 256, 2048, device=dev) for _ in range(nbuf)]
-    y = ops.depthwise_conv1d(xs[0], wd, bd, 1)
-    ref = F.conv1d(x, w, b, padding=1, groups=256)
-    err = _rel_l2(y.cpu(), ref)
-    for i in range(3):
-        ops.depthwise_conv1d(xs[i % nbuf], wd, bd, 1)
-    ms = _graph_time(lambda i: ops.depthwise_conv1d(xs[i % nbuf], wd, bd, 1, out=ys[i % nbuf]),
-                     200, stream)
-    byt = 33558528
-    out["cfg1_dwconv1d_fp32"] = {"us_per_op": ms * 1e3, "bound": "hbm",
-                                 "achieved_gbs": byt / (ms * 1e-3) / 1e9,
-                                 "frac": byt / (ms * 1e-3) / 1e9 / hbm, "rel_l2": err}
-    del xs, ys
-
-    # cfg3: GroupNorm bf16 [4,512,128,128] G32 eps 1e-6
-    g = torch.Generator().manual_seed(3)
-    x = (torch.randn(4, 512, 128, 128, generator=g) * 2).bfloat16()
-    w = (torch.rand(512, generator=g) + 0.5).bfloat16()
-    b = (torch.randn(512, generator=g) * 0.1).bfloat16()
-    nbuf = max(2, ROTATE_BYTES // (x.numel() * 2 * 2))
-    xs = [x.to(dev) for _ in range(nbuf)]
-    ys = [torch.empty_like(xs[0]) for _ in range(nbuf)]
-    wd, bd = w.to(dev), b.to(dev)
-    ref = F.group_norm(x.float(), 32, w.float(), b.float(), 1e-6)
-    byt = 134219776
-    best = None
-    for name, var in (("auto", ops.GN_AUTO), ("cluster4", ops.gn_cluster_variant(4)),
-                      ("cluster8", ops.gn_cluster_variant(8)),
-                      ("cluster16", ops.gn_cluster_variant(16)), ("split", ops.GN_SPLIT)):
-        y = ops.group_norm(xs[0], 32, wd, bd, 1e-6, variant=var)
-        if y is None:
-            continue
-        err = _rel_l2(y.float().cpu(), ref)
+    if only in (None, "cfg1"):
+        # cfg1: depthwise conv1d fp32 [8,256,2048] k3 p1
+        g = torch.Generator().manual_seed(1)
+        x = torch.randn(8, 256, 2048, generator=g)
+        w = _kaiming((256, 1, 3), g)
+        b = _kaiming((256, 1), g).reshape(256)
+        nbuf = max(2, ROTATE_BYTES // (x.numel() * 4 * 2))
+        xs = [x.to(dev) for _ in range(nbuf)]
+        wd, bd = w.reshape(256, 3).to(dev), b.to(dev)
+        ys = [torch.empty(8, 256, 2048, device=dev) for _ in range(nbuf)]
+        y = ops.depthwise_conv1d(xs[0], wd, bd, 1)
+        ref = F.conv1d(x, w, b, padding=1, groups=256)
+        err = _rel_l2(y.cpu(), ref)
         for i in range(3):
-            ops.group_norm(xs[i % nbuf], 32, wd, bd, 1e-6, variant=var)
-        ms = _graph_time(lambda i: ops.group_norm(xs[i % nbuf], 32, wd, bd, 1e-6, variant=var,
-                                                  out=ys[i % nbuf]), 100, stream)
-        rec = {"variant": name, "us_per_op": ms * 1e3, "bound": "hbm",
-               "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
-               "rel_l2": err}
-        out[f"cfg3_group_norm_bf16_{name}"] = rec
-    del xs, ys
-    torch.cuda.empty_cache()
+            ops.depthwise_conv1d(xs[i % nbuf], wd, bd, 1)
+        ms = _graph_time(lambda i: ops.depthwise_conv1d(xs[i % nbuf], wd, bd, 1, out=ys[i % nbuf]),
+                         200, stream)
+        byt = 33558528
+        out["cfg1_dwconv1d_fp32"] = {"us_per_op": ms * 1e3, "bound": "hbm",
+                                     "achieved_gbs": byt / (ms * 1e-3) / 1e9,
+                                     "frac": byt / (ms * 1e-3) / 1e9 / hbm, "rel_l2": err}
+        del xs, ys
 
-    # cfg4b: long-filter depthwise conv1d fp16 [16,1024,16384] k2048 p1024 (FFT route)
-    from amd_tuned_torch import fftconv_ops
-    g = torch.Generator().manual_seed(44)
-    x = torch.randn(16, 1024, 16384, generator=g).half()
-    w = _kaiming((1024, 1, 2048), g).half()
-    b = _kaiming((1024, 2048), g)[:, 0].half()
-    xs = [x.to(dev) for _ in range(2)]
-    wd, bd = w.to(dev), b.to(dev)
-    y = fftconv_ops.fftconv1d(xs[0], wd, bd, 1024)
-    cs = [0, 511, 1023]
-    ref = torch.nn.functional.conv1d(x[:2, cs].float(), w[cs].float(), b[cs].float(),
-                                     padding=1024, groups=3)
-    err = _rel_l2(y[:2, cs].float().cpu(), ref)
-    ms = _events_time(lambda i: fftconv_ops.fftconv1d(xs[i % 2], wd, bd, 1024), 10, stream)
-    byt = 1077970944
-    out["cfg4b_fftconv1d_fp16"] = {"us_per_op": ms * 1e3, "bound": "hbm",
-                                   "achieved_gbs": byt / (ms * 1e-3) / 1e9,
-                                   "frac": byt / (ms * 1e-3) / 1e9 / hbm,
-                                   "rel_l2_slice": err, "nfft": fftconv_ops.fft_length(18432)}
-    del xs, y
-    torch.cuda.empty_cache()
+    if only in (None, "cfg3"):
+        # cfg3: GroupNorm bf16 [4,512,128,128] G32 eps 1e-6
+        g = torch.Generator().manual_seed(3)
+        x = (torch.randn(4, 512, 128, 128, generator=g) * 2).bfloat16()
+        w = (torch.rand(512, generator=g) + 0.5).bfloat16()
+        b = (torch.randn(512, generator=g) * 0.1).bfloat16()
+        nbuf = max(2, ROTATE_BYTES // (x.numel() * 2 * 2))
+        xs = [x.to(dev) for _ in range(nbuf)]
+        ys = [torch.empty_like(xs[0]) for _ in range(nbuf)]
+        wd, bd = w.to(dev), b.to(dev)
+        ref = F.group_norm(x.float(), 32, w.float(), b.float(), 1e-6)
+        byt = 134219776
+        best = None
+        for name, var in (("auto", ops.GN_AUTO), ("cluster4", ops.gn_cluster_variant(4)),
+                          ("cluster8", ops.gn_cluster_variant(8)),
+                          ("cluster16", ops.gn_cluster_variant(16)), ("split", ops.GN_SPLIT)):
+            y = ops.group_norm(xs[0], 32, wd, bd, 1e-6, variant=var)
+            if y is None:
+                continue
+            err = _rel_l2(y.float().cpu(), ref)
+            for i in range(3):
+                ops.group_norm(xs[i % nbuf], 32, wd, bd, 1e-6, variant=var)
+            ms = _graph_time(lambda i: ops.group_norm(xs[i % nbuf], 32, wd, bd, 1e-6, variant=var,
+                                                      out=ys[i % nbuf]), 100, stream)
+            rec = {"variant": name, "us_per_op": ms * 1e3, "bound": "hbm",
+                   "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
+                   "rel_l2": err}
+            out[f"cfg3_group_norm_bf16_{name}"] = rec
+        del xs, ys
+        torch.cuda.empty_cache()
 
-    # cfg4a: conv3d fp16 [2,64,16,64,64] x [64,64,15,15,15] p7 (FFT route)
-    g = torch.Generator().manual_seed(41)
-    x = torch.randn(2, 64, 16, 64, 64, generator=g).half()
-    w = _kaiming((64, 64, 15, 15, 15), g).half()
-    b = _kaiming((64, 64 * 3375), g)[:, 0].half()
-    xs = [x.to(dev) for _ in range(4)]
-    wd, bd = w.to(dev), b.to(dev)
-    y = fftconv_ops.fft_conv3d(xs[0], wd, bd, padding=7)
-    if y is not None:
-        ms = _events_time(lambda i: fftconv_ops.fft_conv3d(xs[i % 4], wd, bd, padding=7), 10,
-                          stream)
-        byt = 61202560
-        out["cfg4a_fftconv3d_fp16"] = {
-            "us_per_op": ms * 1e3, "bound": "hbm (compulsory I/O)",
-            "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
-            "effective_tflops": 3.624e12 / (ms * 1e-3) / 1e12,
-            "note": "weight spectrum cached (3.2 GB fp32) and streamed once per call"}
-    del xs, y
-    torch.cuda.empty_cache()
+    if only in (None, "cfg4b"):
+        # cfg4b: long-filter depthwise conv1d fp16 [16,1024,16384] k2048 p1024 (FFT route)
+        from amd_tuned_torch import fftconv_ops
+        g = torch.Generator().manual_seed(44)
+        C4 = 64 if small else 1024
+        x = torch.randn(16, C4, 16384, generator=g).half()
+        w = _kaiming((C4, 1, 2048), g).half()
+        b = _kaiming((C4, 2048), g)[:, 0].half()
+        xs = [x.to(dev) for _ in range(2)]
+        wd, bd = w.to(dev), b.to(dev)
+        y = fftconv_ops.fftconv1d(xs[0], wd, bd, 1024)
+        cs = [0, C4 // 2 - 1, C4 - 1]
+        ref = torch.nn.functional.conv1d(x[:2, cs].float(), w[cs].float(), b[cs].float(),
+                                         padding=1024, groups=3)
+        err = _rel_l2(y[:2, cs].float().cpu(), ref)
+        ms = _events_time(lambda i: fftconv_ops.fftconv1d(xs[i % 2], wd, bd, 1024), 10, stream)
+        byt = 1077970944 * C4 // 1024
+        out["cfg4b_fftconv1d_fp16"] = {"us_per_op": ms * 1e3, "bound": "hbm",
+                                       "achieved_gbs": byt / (ms * 1e-3) / 1e9,
+                                       "frac": byt / (ms * 1e-3) / 1e9 / hbm,
+                                       "rel_l2_slice": err, "nfft": fftconv_ops.fft_length(18432)}
+        del xs, y
+        torch.cuda.empty_cache()
+
+    if only in (None, "cfg4a"):
+        # cfg4a: conv3d fp16 [2,64,16,64,64] x [64,64,15,15,15] p7 (FFT route)
+        g = torch.Generator().manual_seed(41)
+        x = torch.randn(2, 64, 16, 64, 64, generator=g).half()
+        w = _kaiming((64, 64, 15, 15, 15), g).half()
+        b = _kaiming((64, 64 * 3375), g)[:, 0].half()
+        xs = [x.to(dev) for _ in range(4)]
+        wd, bd = w.to(dev), b.to(dev)
+        y = fftconv_ops.fft_conv3d(xs[0], wd, bd, padding=7)
+        if y is not None:
+            ms = _events_time(lambda i: fftconv_ops.fft_conv3d(xs[i % 4], wd, bd, padding=7), 10,
+                              stream)
+            byt = 61202560
+            out["cfg4a_fftconv3d_fp16"] = {
+                "us_per_op": ms * 1e3, "bound": "hbm (compulsory I/O)",
+                "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
+                "effective_tflops": 3.624e12 / (ms * 1e-3) / 1e12,
+                "note": "weight spectrum cached (3.2 GB fp32) and streamed once per call"}
+        del xs, y
+        torch.cuda.empty_cache()
     return out
 
 
@@ -495,11 +502,19 @@ def main() -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-shapes", action="store_true")
     ap.add_argument("--no-stack", action="store_true")
+    ap.add_argument("--only", choices=("cfg1", "cfg3", "cfg4a", "cfg4b"), default=None,
+                    help="time one per-shape config alone (profiling target), one GPU")
+    ap.add_argument("--small", action="store_true", help="with --only cfg4b: 64 channels")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.only:
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        print(json.dumps(per_shape(dev, _peaks(), only=args.only, small=args.small)), flush=True)
+        return 0
     if args.impl == "reference":
         rec = run_reference(args, rank, world)
         if rec is not None:

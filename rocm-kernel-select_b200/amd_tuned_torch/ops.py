@@ -301,31 +301,35 @@ def to_channels_last(x: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------ FFT ---
-def fftconv1d_spectrum(w2d: torch.Tensor, nfft: int) -> Optional[torch.Tensor]:
-    """Conjugated half spectrum [C, nfft/2 + 1] complex64 of a depthwise [C, K]
-    kernel (cached per weight version)."""
-    hit = _spectra.get(w2d, ("fft1d", nfft))
+def fftconv1d_spectrum(w: torch.Tensor, nfft: int) -> Optional[torch.Tensor]:
+    """Conjugated spectrum (nfft complex64 per channel, transform-position
+    order) of a depthwise kernel given as [C, 1, K] or [C, K]; cached on the
+    caller's weight object (pass the parameter itself, not a fresh view, or
+    every call recomputes it)."""
+    hit = _spectra.get(w, ("fft1d", nfft))
     if hit is not None:
         return hit
     L = _lib.lib()
-    C, K = w2d.shape
+    C, K = w.shape[0], w.shape[-1]
+    w2d = w.reshape(C, K).contiguous()
     spec = torch.empty(L.b200_fftconv1d_spectrum_bytes(C, nfft) // 4, dtype=torch.float32,
-                       device=w2d.device)
-    rc = L.b200_fftconv1d_prepare(w2d.contiguous().data_ptr(), spec.data_ptr(),
-                                  _code(w2d.dtype), C, K, nfft, _stream(w2d.device))
+                       device=w.device)
+    rc = L.b200_fftconv1d_prepare(w2d.data_ptr(), spec.data_ptr(), _code(w.dtype), C, K, nfft,
+                                  _stream(w.device))
     if not _lib.check(rc, "b200_fftconv1d_prepare"):
         return None
-    _spectra.put(w2d, ("fft1d", nfft), spec)
+    _spectra.put(w, ("fft1d", nfft), spec)
     return spec
 
 
 def fftconv1d(x: torch.Tensor, w2d: torch.Tensor, bias: Optional[torch.Tensor], padding: int,
               nfft: int) -> Optional[torch.Tensor]:
+    """Depthwise FFT conv1d; `w2d` is the kernel as [C, 1, K] or [C, K]."""
     L_ = _lib.lib()
     if not L_.b200_fft_supported_length(nfft):
         return None
     B, C, L = x.shape
-    K = w2d.shape[1]
+    K = w2d.shape[-1]
     Lout = L + 2 * padding - K + 1
     spec = fftconv1d_spectrum(w2d, nfft)
     if spec is None:

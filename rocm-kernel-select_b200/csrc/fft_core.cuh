@@ -281,6 +281,83 @@ __device__ __forceinline__ void inverse(float2* buf, const Plan& p, const float2
   }
 }
 
+// ------------------------------------------------ per-pass twiddle tables ---
+// Pass p (span S_p, radix R_p) needs W_{S_p}^(k m) for k < S_p / R_p, m < R_p.
+// The table holds only W_{S_p}^k (contiguous in k, so a warp's lookups hit
+// distinct banks); the powers m are formed in registers by repeated complex
+// multiplication (R - 2 products, error ~R ulps).
+__device__ __forceinline__ int pass_tw_count(const Plan& p) {
+  int total = 0, span = p.n;
+  for (int i = 0; i < p.passes; ++i) {
+    total += span / p.radix[i];
+    span /= p.radix[i];
+  }
+  return total;
+}
+
+__device__ __forceinline__ void build_pass_twiddles(float2* tw, const Plan& p) {
+  int off = 0, span = p.n;
+  for (int i = 0; i < p.passes; ++i) {
+    const int cnt = span / p.radix[i];
+    for (int k = threadIdx.x; k < cnt; k += blockDim.x) {
+      double s, c;
+      sincospi(-2.0 * static_cast<double>(k) / static_cast<double>(span), &s, &c);
+      tw[off + k] = make_float2(static_cast<float>(c), static_cast<float>(s));
+    }
+    off += cnt;
+    span /= p.radix[i];
+  }
+}
+
+// Multiplies v[m] (m >= 1) by w^m (forward) or conj(w)^m (inverse).
+template <int R, bool INV>
+__device__ __forceinline__ void apply_twiddle_powers(float2 (&v)[R], float2 w) {
+  if (INV) w.y = -w.y;
+  float2 wm = w;
+#pragma unroll
+  for (int m = 1; m < R; ++m) {
+    v[m] = cmul(v[m], wm);
+    if (m + 1 < R) wm = cmul(wm, w);
+  }
+}
+
+// Middle pass (shared memory in and out), per-pass table `tw`.
+template <int R, bool INV>
+__device__ __forceinline__ void pass_t(float2* buf, int n, int span, const float2* tw) {
+  const int stride = span / R;
+  const int nbf = n / R;
+  for (int b = threadIdx.x; b < nbf; b += blockDim.x) {
+    const int g = b / stride, k = b - g * stride;
+    const int base = g * span + k;
+    float2 v[R];
+#pragma unroll
+    for (int m = 0; m < R; ++m) v[m] = buf[pidx(base + m * stride)];
+    if (!INV) {
+      Dft<R, false>::run(v);
+      if (k != 0) apply_twiddle_powers<R, false>(v, tw[k]);
+    } else {
+      if (k != 0) apply_twiddle_powers<R, true>(v, tw[k]);
+      Dft<R, true>::run(v);
+    }
+#pragma unroll
+    for (int m = 0; m < R; ++m) buf[pidx(base + m * stride)] = v[m];
+  }
+}
+
+template <bool INV>
+__device__ __forceinline__ void run_pass_t(int radix, float2* buf, int n, int span,
+                                           const float2* tw) {
+  switch (radix) {
+    case 16: pass_t<16, INV>(buf, n, span, tw); break;
+    case 8: pass_t<8, INV>(buf, n, span, tw); break;
+    case 4: pass_t<4, INV>(buf, n, span, tw); break;
+    case 2: pass_t<2, INV>(buf, n, span, tw); break;
+    case 9: pass_t<9, INV>(buf, n, span, tw); break;
+    case 3: pass_t<3, INV>(buf, n, span, tw); break;
+    default: pass_t<5, INV>(buf, n, span, tw); break;
+  }
+}
+
 // Host: radix plan for n = 2^a 3^b 5^c (largest radices first); false if n
 // has another prime factor or needs too many passes.
 inline bool make_plan(int64_t n, Plan* p) {

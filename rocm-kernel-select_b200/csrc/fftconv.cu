@@ -30,17 +30,94 @@ size_t fft1d_smem(int n) {
   return static_cast<size_t>(fft::kLo + nhi + fft::padded_len(n)) * sizeof(float2);
 }
 
+// Forward pass 0 (span n, stride n/R) fed straight from the two input rows
+// (zero outside [0, L) after shifting by `pad`).
+template <typename T, int R>
+__device__ __forceinline__ void first_pass_from_rows(float2* buf, int n, const float2* tw0,
+                                                     const T* x0, const T* x1, bool has1,
+                                                     int64_t pad, int64_t L) {
+  const int stride = n / R;
+  for (int k = threadIdx.x; k < stride; k += blockDim.x) {
+    float2 v[R];
+#pragma unroll
+    for (int m = 0; m < R; ++m) {
+      const int64_t l = static_cast<int64_t>(k + m * stride) - pad;
+      const bool in = l >= 0 && l < L;
+      v[m] = make_float2(in ? to_f32(x0[l]) : 0.f, (in && has1) ? to_f32(x1[l]) : 0.f);
+    }
+    fft::Dft<R, false>::run(v);
+    if (k != 0) fft::apply_twiddle_powers<R, false>(v, tw0[k]);
+#pragma unroll
+    for (int m = 0; m < R; ++m) buf[fft::pidx(k + m * stride)] = v[m];
+  }
+}
+
+// Last forward pass (span R: R consecutive positions, no twiddles), the
+// spectral product, and the first inverse pass over the same positions --
+// all in registers, one shared-memory round trip.
+template <int R>
+__device__ __forceinline__ void last_fwd_product_first_inv(float2* buf, int n,
+                                                            const float2* __restrict__ h) {
+  const int ng = n / R;
+  for (int g = threadIdx.x; g < ng; g += blockDim.x) {
+    const int base = g * R;
+    float2 v[R];
+#pragma unroll
+    for (int m = 0; m < R; ++m) v[m] = buf[fft::pidx(base + m)];
+    fft::Dft<R, false>::run(v);
+#pragma unroll
+    for (int m = 0; m < R; ++m) v[m] = fft::cmul(v[m], __ldg(h + base + m));
+    fft::Dft<R, true>::run(v);
+#pragma unroll
+    for (int m = 0; m < R; ++m) buf[fft::pidx(base + m)] = v[m];
+  }
+}
+
+// Inverse pass 0 (span n) written straight to the two output rows: crop to
+// L_out, scale 1/n, + bias, dtype conversion.
+template <typename T, int R>
+__device__ __forceinline__ void last_pass_to_rows(const float2* buf, int n, const float2* tw0,
+                                                  T* y0, T* y1, bool has1, int64_t Lout,
+                                                  float scale, float bv) {
+  const int stride = n / R;
+  for (int k = threadIdx.x; k < stride; k += blockDim.x) {
+    float2 v[R];
+#pragma unroll
+    for (int m = 0; m < R; ++m) v[m] = buf[fft::pidx(k + m * stride)];
+    if (k != 0) fft::apply_twiddle_powers<R, true>(v, tw0[k]);
+    fft::Dft<R, true>::run(v);
+#pragma unroll
+    for (int m = 0; m < R; ++m) {
+      const int64_t l = k + m * stride;
+      if (l < Lout) {
+        y0[l] = from_f32<T>(fmaf(v[m].x, scale, bv));
+        if (has1) y1[l] = from_f32<T>(fmaf(v[m].y, scale, bv));
+      }
+    }
+  }
+}
+
+#define B200_FFT_RADIX_SWITCH(r, CALL) \
+  switch (r) {                         \
+    case 16: CALL(16); break;          \
+    case 8: CALL(8); break;            \
+    case 4: CALL(4); break;            \
+    case 2: CALL(2); break;            \
+    case 9: CALL(9); break;            \
+    case 3: CALL(3); break;            \
+    default: CALL(5); break;           \
+  }
+
 template <typename T>
 __global__ void __launch_bounds__(kFftThreads, 1)
 fftconv1d_kernel(const T* __restrict__ x, const float2* __restrict__ spec,
                  const void* __restrict__ bias, int bias_dt, T* __restrict__ y, int64_t B,
-                 int64_t C, int64_t L, int64_t pad, int64_t Lout, const fft::Plan plan) {
+                 int64_t C, int64_t L, int64_t pad, int64_t Lout, const fft::Plan plan,
+                 int tw_count) {
   extern __shared__ float2 sm[];
   const int n = plan.n;
-  const int nhi = (n + fft::kLo - 1) >> fft::kLoBits;
-  float2* lo = sm;
-  float2* hi = lo + fft::kLo;
-  float2* buf = hi + nhi;
+  float2* tw = sm;
+  float2* buf = tw + ((tw_count + 1) & ~1);
 
   const int64_t pairs = (B + 1) / 2;
   const int64_t c = blockIdx.x / pairs;
@@ -48,34 +125,56 @@ fftconv1d_kernel(const T* __restrict__ x, const float2* __restrict__ spec,
   const bool has1 = b1 < B;
   const T* x0 = x + (b0 * C + c) * L;
   const T* x1 = x + (min64(b1, B - 1) * C + c) * L;
-
-  fft::build_twiddles(lo, hi, n);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int64_t l = i - pad;
-    const bool in = l >= 0 && l < L;
-    const float re = in ? to_f32(x0[l]) : 0.f;
-    const float im = (in && has1) ? to_f32(x1[l]) : 0.f;
-    buf[fft::pidx(i)] = make_float2(re, im);
-  }
-  __syncthreads();
-  fft::forward(buf, plan, lo, hi);
-  const float2* h = spec + c * n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int p = fft::pidx(i);
-    buf[p] = fft::cmul(buf[p], __ldg(h + i));
-  }
-  __syncthreads();
-  fft::inverse(buf, plan, lo, hi);
-
-  const float scale = 1.0f / static_cast<float>(n);
-  const float bv = bias ? load_param(bias, bias_dt, c) : 0.f;
   T* y0 = y + (b0 * C + c) * Lout;
   T* y1 = y + (min64(b1, B - 1) * C + c) * Lout;
-  for (int64_t l = threadIdx.x; l < Lout; l += blockDim.x) {
-    const float2 v = buf[fft::pidx(static_cast<int>(l))];
-    y0[l] = from_f32<T>(fmaf(v.x, scale, bv));
-    if (has1) y1[l] = from_f32<T>(fmaf(v.y, scale, bv));
+
+  fft::build_pass_twiddles(tw, plan);
+  __syncthreads();
+  // Span and twiddle-table offset of every pass.
+  int span[fft::kMaxPasses], off[fft::kMaxPasses];
+  {
+    int s = n, o = 0;
+    for (int i = 0; i < plan.passes; ++i) {
+      span[i] = s;
+      off[i] = o;
+      o += s / plan.radix[i];
+      s /= plan.radix[i];
+    }
   }
+  const int P = plan.passes;
+
+#define B200_FIRST(R) first_pass_from_rows<T, R>(buf, n, tw, x0, x1, has1, pad, L)
+  B200_FFT_RADIX_SWITCH(plan.radix[0], B200_FIRST)
+#undef B200_FIRST
+  __syncthreads();
+  for (int i = 1; i < P - 1; ++i) {
+    fft::run_pass_t<false>(plan.radix[i], buf, n, span[i], tw + off[i]);
+    __syncthreads();
+  }
+  const float2* h = spec + c * n;
+#define B200_MID(R) last_fwd_product_first_inv<R>(buf, n, h)
+  B200_FFT_RADIX_SWITCH(plan.radix[P - 1], B200_MID)
+#undef B200_MID
+  __syncthreads();
+  for (int i = P - 2; i >= 1; --i) {
+    fft::run_pass_t<true>(plan.radix[i], buf, n, span[i], tw + off[i]);
+    __syncthreads();
+  }
+  const float scale = 1.0f / static_cast<float>(n);
+  const float bv = bias ? load_param(bias, bias_dt, c) : 0.f;
+#define B200_LAST(R) last_pass_to_rows<T, R>(buf, n, tw, y0, y1, has1, Lout, scale, bv)
+  B200_FFT_RADIX_SWITCH(plan.radix[0], B200_LAST)
+#undef B200_LAST
+}
+
+// Host mirror of fft::pass_tw_count.
+int host_tw_count(const fft::Plan& p) {
+  int total = 0, span = p.n;
+  for (int i = 0; i < p.passes; ++i) {
+    total += span / p.radix[i];
+    span /= p.radix[i];
+  }
+  return total;
 }
 
 // Kernel spectrum, one CTA per channel: the zero-padded real filter through
@@ -169,7 +268,10 @@ int b200_fftconv1d_fwd(const void* x, const void* spectrum, const void* bias, vo
   if (L_out > L + 2 * pad) return fail_arg("L_out too long");
   const int64_t blocks = C * ((B + 1) / 2);
   if (blocks > 0x7fffffffLL) return fail_unsupported("grid too large");
-  const size_t smem = fft1d_smem(plan.n);
+  if (plan.passes < 2) return fail_unsupported("FFT length too short for the fused kernel");
+  const int twc = host_tw_count(plan);
+  const size_t smem =
+      static_cast<size_t>(((twc + 1) & ~1) + fft::padded_len(plan.n)) * sizeof(float2);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const float2* sp = static_cast<const float2*>(spectrum);
   int rc;
@@ -177,17 +279,17 @@ int b200_fftconv1d_fwd(const void* x, const void* spectrum, const void* bias, vo
     if ((rc = prep_smem(fftconv1d_kernel<float>, smem)) != B200_OK) return rc;
     fftconv1d_kernel<float><<<(unsigned)blocks, kFftThreads, smem, s>>>(
         static_cast<const float*>(x), sp, bias, bias_dtype, static_cast<float*>(y), B, C, L, pad,
-        L_out, plan);
+        L_out, plan, twc);
   } else if (dtype == B200_DTYPE_F16) {
     if ((rc = prep_smem(fftconv1d_kernel<__half>, smem)) != B200_OK) return rc;
     fftconv1d_kernel<__half><<<(unsigned)blocks, kFftThreads, smem, s>>>(
         static_cast<const __half*>(x), sp, bias, bias_dtype, static_cast<__half*>(y), B, C, L,
-        pad, L_out, plan);
+        pad, L_out, plan, twc);
   } else {
     if ((rc = prep_smem(fftconv1d_kernel<__nv_bfloat16>, smem)) != B200_OK) return rc;
     fftconv1d_kernel<__nv_bfloat16><<<(unsigned)blocks, kFftThreads, smem, s>>>(
         static_cast<const __nv_bfloat16*>(x), sp, bias, bias_dtype,
-        static_cast<__nv_bfloat16*>(y), B, C, L, pad, L_out, plan);
+        static_cast<__nv_bfloat16*>(y), B, C, L, pad, L_out, plan, twc);
   }
   B200_LAUNCH_CHECK("fftconv1d_kernel");
   return B200_OK;
