@@ -141,11 +141,18 @@ def test_dwconv1d_cfg1_full_size(cuda):
 
 
 @pytest.mark.parametrize("K,pad,L", [(3, 1, 4099), (31, 15, 5000), (2, 0, 17), (64, 40, 100),
-                                     (11, 0, 2048)])
+                                     (11, 0, 2048),
+                                     # register path: 16-byte rows, halo <= one vector,
+                                     # same / valid / causal padding, partial last tile
+                                     (5, 2, 4096), (7, 3, 1024), (9, 4, 2048), (3, 1, 1000),
+                                     (3, 1, 8), (9, 0, 4096), (1, 0, 64), (5, 4, 4096),
+                                     (9, 8, 2040),
+                                     # near misses that take the shared-memory kernel
+                                     (8, 4, 2048), (2, 1, 512), (4, 3, 8192)])
 def test_dwconv1d_shapes(cuda, K, pad, L):
     from amd_tuned_torch import ops
     g = torch.Generator().manual_seed(K)
-    for dt in ("f32", "bf16"):
+    for dt in ("f32", "bf16", "f16"):
         x = torch.randn(2, 5, L, generator=g).to(torch_dtype(dt))
         w = _kaiming((5, 1, K), g).to(torch_dtype(dt))
         b = torch.randn(5, generator=g).to(torch_dtype(dt))
