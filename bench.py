@@ -249,6 +249,35 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         del xs, ys
         torch.cuda.empty_cache()
 
+    if only in (None, "cfg5conv"):
+        # The video stack's conv3d alone (cfg 5, one GPU): bf16 channels-last
+        # x[1, 66, 128, 128, 128] (64 frames + 2 halo frames) x w[128,128,3,3,3],
+        # padding (0, 1, 1) -> NCDHW y[1, 128, 64, 128, 128]; inputs > L2.
+        g = torch.Generator().manual_seed(5)
+        w = _kaiming((128, 128, 3, 3, 3), g).bfloat16().to(dev)
+        b = (torch.randn(128, generator=g) * 0.1).bfloat16().to(dev)
+        xs = [torch.randn(1, 66, 128, 128, 128, generator=g, dtype=torch.float32).bfloat16().to(dev)
+              for _ in range(2)]
+        ys = [torch.empty(1, 128, 64, 128, 128, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+
+        def conv(i):
+            return ops.conv3d(xs[i % 2], w, b, (1, 1, 1), (0, 1, 1), (1, 1, 1),
+                              x_channels_last=True, out=ys[i % 2])
+        y = conv(0)
+        # parity on a slice: output frames 0-1 from input frames 0-3
+        xs_ref = xs[0][:, :4].permute(0, 4, 1, 2, 3).float().cpu()
+        ref = F.conv3d(xs_ref, w.float().cpu(), b.float().cpu(), padding=(0, 1, 1))
+        err = _rel_l2(y[:, :, :2].float().cpu(), ref)
+        for i in range(3):
+            conv(i)
+        ms = _graph_time(conv, 10, stream)
+        flop = 2.0 * 64 * 128 * 128 * 128 * 128 * 27
+        tf = flop / (ms * 1e-3) / 1e12
+        out["cfg5_conv3d_bf16"] = {"us_per_op": ms * 1e3, "bound": "tensor", "tflops": tf,
+                                   "frac": tf / peaks["bf16_tflops"], "rel_l2_slice": err}
+        del xs, ys, y
+        torch.cuda.empty_cache()
+
     if only in (None, "cfg4b"):
         # cfg4b: long-filter depthwise conv1d fp16 [16,1024,16384] k2048 p1024 (FFT route)
         from amd_tuned_torch import fftconv_ops
@@ -502,7 +531,7 @@ def main() -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-shapes", action="store_true")
     ap.add_argument("--no-stack", action="store_true")
-    ap.add_argument("--only", choices=("cfg1", "cfg3", "cfg4a", "cfg4b"), default=None,
+    ap.add_argument("--only", choices=("cfg1", "cfg3", "cfg4a", "cfg4b", "cfg5conv"), default=None,
                     help="time one per-shape config alone (profiling target), one GPU")
     ap.add_argument("--small", action="store_true", help="with --only cfg4b: 64 channels")
     args = ap.parse_args()

@@ -41,7 +41,7 @@ namespace {
 
 constexpr int kConvThreads = 192;  // 6 warps
 constexpr int kBM = 128;
-constexpr int kBK = 64;            // channels per k-block (one 128-byte swizzle row)
+constexpr int kBK = 64;            // weight packing granule: Cin is padded to a multiple of 64
 constexpr int kMaxStages = 8;
 
 struct ConvParams {
@@ -49,6 +49,7 @@ struct ConvParams {
   int KH, KW;
   int pd, ph, pw, dd, dh, dw;
   int BW, BH;
+  int MT;                       // M tiles (of 128 positions) per CTA tile, stacked along H
   int tiles_w, tiles_h, tiles_n, num_tiles;
   int cchunks, kblocks;
   int khg, khb;                 // kh taps per k-block (1 or KH), kh blocks = KH / khg
@@ -76,29 +77,37 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const ConvParams& p, int
   t /= p.tiles_h;
   c.od = t % p.Do;
   c.n = t / p.Do;
-  c.oh0 = th * p.BH;
+  c.oh0 = th * p.BH * p.MT;
   c.ow0 = tw * p.BW;
   c.n0 = nt * BN;
   return c;
 }
 
-template <typename T, int BN>
+// MT: M tiles per CTA tile (1, 2 or 4); they share every weight box and the
+// A rows of neighbouring taps.  KB: channels per k-block -- 64 (128-byte
+// K-major rows, SWIZZLE_128B) or 32 (64-byte rows, SWIZZLE_64B, half the
+// stage size so that MT = 4 still leaves three stages).
+template <typename T, int BN, int MT, int KB>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                  const __grid_constant__ CUtensorMap tmy, const ConvParams p) {
-  constexpr int kBTap = BN * kBK * 2;      // one tap's weight box
-  constexpr int kOutBytes = kBM * BN * 2;
+  static_assert(KB == 64 || KB == 32, "k-block of 32 or 64 channels");
+  constexpr int kRow = KB * 2;               // bytes per K-major operand row
+  constexpr int kBTap = BN * kRow;           // one tap's weight box
+  constexpr int kAcc = MT * BN;              // TMEM columns of one tile's accumulators
+  constexpr int kBufs = (2 * kAcc <= 512) ? 2 : 1;
+  constexpr uint32_t kTmemCols = kBufs * kAcc < 32 ? 32u : static_cast<uint32_t>(kBufs * kAcc);
+  static_assert(kBufs * kAcc <= 512 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM columns");
   constexpr uint32_t kIdesc = umma_idesc_f16(sizeof(T) == 2 && std::is_same<T, __half>::value ? 0 : 1, kBM, BN);
-  constexpr uint32_t kTmemCols = 2 * BN;
   const int STAGES = p.stages;
 
   // Stage s = [A box: a_bytes][B boxes: khg * kBTap], every piece 1024-byte
-  // aligned (the 128-byte swizzle atom), then the output staging tile.
+  // aligned, then the output staging tile (present when out_tma is set).
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sOut = smem + STAGES * p.stage_bytes;                   // [BN][128] staging
-  float* sBias = reinterpret_cast<float*>(sOut + kOutBytes);       // [BN]
+  float* sBias = reinterpret_cast<float*>(sOut + (p.out_tma ? kBM * BN * 2 : 0));  // [BN]
   uint64_t* full = reinterpret_cast<uint64_t*>(sBias + BN);
   uint64_t* empty = full + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;  // [2]
@@ -164,11 +173,11 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
           if (lane == 0) {
             uint8_t* st = smem + stage * p.stage_bytes;
             mbar_expect_tx(&full[stage], p.stage_bytes);
-            tma_load_5d(st, &tmx, &full[stage], cc * kBK, tc.ow0 - p.pw + kw * p.dw,
+            tma_load_5d(st, &tmx, &full[stage], cc * KB, tc.ow0 - p.pw + kw * p.dw,
                         tc.oh0 - p.ph + hb * p.khg * p.dh, tc.od - p.pd + kd * p.dd, tc.n);
             for (int j = 0; j < p.khg; ++j) {
               const int tap = (kd * p.KH + hb * p.khg + j) * p.KW + kw;
-              tma_load_3d(st + p.a_bytes + j * kBTap, &tmw, &full[stage], cc * kBK, tc.n0, tap);
+              tma_load_3d(st + p.a_bytes + j * kBTap, &tmw, &full[stage], cc * KB, tc.n0, tap);
             }
           }
           __syncwarp();
@@ -194,15 +203,15 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++it) {
-        const int acc = it & 1;
-        const uint32_t aphase = static_cast<uint32_t>(it >> 1) & 1u;
+        const int acc = kBufs == 2 ? (it & 1) : 0;
+        const uint32_t aphase = static_cast<uint32_t>(kBufs == 2 ? (it >> 1) : it) & 1u;
         const bool free_acc = mbar_wait_bounded(&tempty[acc], aphase ^ 1u, abort, p.flags, 1);
         if (!__all_sync(0xffffffffu, free_acc)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kAcc);
         for (int kb = 0; kb < p.kblocks; ++kb) {
           const bool got = mbar_wait_bounded(&full[stage], phase, abort, p.flags, 1);
           if (!__all_sync(0xffffffffu, got)) {
@@ -212,19 +221,28 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
           tc_fence_after();
           if (lane == 0) {
             const uint8_t* st = smem + stage * p.stage_bytes;
-            const uint32_t a_row_step = static_cast<uint32_t>(p.dh * p.BW * kBK * 2);
+            // One input row of the box = BW positions x kRow bytes.
+            const uint32_t row_bytes = static_cast<uint32_t>(p.BW * kRow);
             for (int j = 0; j < p.khg; ++j) {
-              // Tap j: A rows start j * dh input rows down (a multiple of 8
-              // rows, so the swizzle atoms stay aligned); its own B box.
-              const uint64_t adesc = umma_desc_sw128(smem_u32(st) + j * a_row_step);
-              const uint64_t bdesc = umma_desc_sw128(smem_u32(st + p.a_bytes + j * kBTap));
+              const uint32_t b_addr = smem_u32(st + p.a_bytes + j * kBTap);
+              const uint64_t bdesc = KB == 64 ? umma_desc_sw128(b_addr) : umma_desc_sw64(b_addr);
 #pragma unroll
-              for (int k = 0; k < kBK / 16; ++k) {
-                // +32 bytes along K inside the swizzled 128-byte row = +2 in
-                // the descriptor's address field.
-                umma_f16_ss(d_tmem, adesc + static_cast<uint64_t>(2 * k),
-                            bdesc + static_cast<uint64_t>(2 * k), kIdesc,
-                            (kb > 0 || j > 0 || k > 0) ? 1u : 0u);
+              for (int i = 0; i < MT; ++i) {
+                // M tile i of tap j: its A rows start i * BH + j * dh input
+                // rows down (BW >= 8, so a whole number of 8-row swizzle
+                // atoms); the weight box is shared by the MT tiles.
+                const uint32_t a_addr =
+                    smem_u32(st) + static_cast<uint32_t>(i * p.BH + j * p.dh) * row_bytes;
+                const uint64_t adesc = KB == 64 ? umma_desc_sw128(a_addr) : umma_desc_sw64(a_addr);
+#pragma unroll
+                for (int k = 0; k < KB / 16; ++k) {
+                  // +32 bytes along K inside the swizzled row = +2 in the
+                  // descriptor's address field.
+                  umma_f16_ss(d_tmem + static_cast<uint32_t>(i * BN),
+                              adesc + static_cast<uint64_t>(2 * k),
+                              bdesc + static_cast<uint64_t>(2 * k), kIdesc,
+                              (kb > 0 || j > 0 || k > 0) ? 1u : 0u);
+                }
               }
             }
             umma_commit(&empty[stage]);
@@ -257,8 +275,8 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
     uint16_t* stage16 = reinterpret_cast<uint16_t*>(sOut);
     const int64_t plane = static_cast<int64_t>(p.Ho) * p.Wo;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
-      const int acc = it & 1;
-      const uint32_t aphase = static_cast<uint32_t>(it >> 1) & 1u;
+      const int acc = kBufs == 2 ? (it & 1) : 0;
+      const uint32_t aphase = static_cast<uint32_t>(kBufs == 2 ? (it >> 1) : it) & 1u;
       // All 128 threads leave together or not at all (a named barrier
       // follows); the vote also orders this tile after the previous tile's
       // readers of sBias / staging.
@@ -272,56 +290,66 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       }
       if (p.out_tma && etid == 0) bulk_wait_read0();  // staging free again
       epi_bar();
-      const int oh = tc.oh0 + row / p.BW, ow = tc.ow0 + row % p.BW;
-      const bool valid = oh < p.Ho && ow < p.Wo;
-      const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const int64_t pos = (static_cast<int64_t>(tc.od) * p.Ho + oh) * p.Wo + ow;
 #pragma unroll 1
-      for (int j0 = 0; j0 < BN; j0 += 32) {
-        float v0[16], v1[16], v[32];
-        tmem_ld16(taddr + j0, v0);
-        tmem_ld16(taddr + j0 + 16, v1);
-        tmem_ld_wait();
+      for (int i = 0; i < MT; ++i) {
+        if (i > 0 && p.out_tma) {
+          if (etid == 0) bulk_wait_read0();
+          epi_bar();
+        }
+        const int oh0 = tc.oh0 + i * p.BH;
+        const int oh = oh0 + row / p.BW, ow = tc.ow0 + row % p.BW;
+        const bool valid = oh < p.Ho && ow < p.Wo;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(acc * kAcc + i * BN);
+        const int64_t pos = (static_cast<int64_t>(tc.od) * p.Ho + oh) * p.Wo + ow;
+#pragma unroll 1
+        for (int j0 = 0; j0 < BN; j0 += 32) {
+          float v0[16], v1[16], v[32];
+          tmem_ld16(taddr + j0, v0);
+          tmem_ld16(taddr + j0 + 16, v1);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = (j < 16 ? v0[j] : v1[j - 16]) + sBias[j0 + j];
-        if (p.out_tma) {
+          for (int j = 0; j < 32; ++j) v[j] = (j < 16 ? v0[j] : v1[j - 16]) + sBias[j0 + j];
+          if (p.out_tma) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) stage16[(j0 + j) * kBM + row] = f32_to_bits16<T>(v[j]);
-        } else if (valid && p.y_cl) {
-          T* dst = y + (static_cast<int64_t>(tc.n) * p.Do * plane + pos) * p.Cout + tc.n0 + j0;
-          const bool vec = tc.n0 + j0 + 32 <= p.Cout && (p.Cout & 7) == 0;
-          if (vec) {
+            for (int j = 0; j < 32; ++j) stage16[(j0 + j) * kBM + row] = f32_to_bits16<T>(v[j]);
+          } else if (valid && p.y_cl) {
+            T* dst = y + (static_cast<int64_t>(tc.n) * p.Do * plane + pos) * p.Cout + tc.n0 + j0;
+            const bool vec = tc.n0 + j0 + 32 <= p.Cout && (p.Cout & 7) == 0;
+            if (vec) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float f[8];
+              for (int q = 0; q < 4; ++q) {
+                float f[8];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) f[e] = v[8 * q + e];
-              *reinterpret_cast<uint4*>(dst + 8 * q) = pack16<T>(f);
+                for (int e = 0; e < 8; ++e) f[e] = v[8 * q + e];
+                *reinterpret_cast<uint4*>(dst + 8 * q) = pack16<T>(f);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (tc.n0 + j0 + j < p.Cout) dst[j] = from_f32<T>(v[j]);
             }
-          } else {
+          } else if (valid) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (tc.n0 + j0 + j < p.Cout) dst[j] = from_f32<T>(v[j]);
-          }
-        } else if (valid) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int co = tc.n0 + j0 + j;
-            if (co < p.Cout)
-              y[((static_cast<int64_t>(tc.n) * p.Cout + co) * p.Do) * plane + pos] =
-                  from_f32<T>(v[j]);
+            for (int j = 0; j < 32; ++j) {
+              const int co = tc.n0 + j0 + j;
+              if (co < p.Cout)
+                y[((static_cast<int64_t>(tc.n) * p.Cout + co) * p.Do) * plane + pos] =
+                    from_f32<T>(v[j]);
+            }
           }
         }
-      }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);  // accumulator drained: the MMA warp may reuse it
-      if (p.out_tma) {
-        fence_proxy_async();        // staging writes -> visible to the TMA engine
-        epi_bar();
-        if (etid == 0) {
-          tma_store_5d(&tmy, sOut, tc.ow0, tc.oh0, tc.od, tc.n0, tc.n);
-          bulk_commit();
+        if (i == MT - 1) {
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);  // accumulators drained: the MMA warp may reuse them
+        }
+        if (p.out_tma) {
+          fence_proxy_async();        // staging writes -> visible to the TMA engine
+          epi_bar();
+          if (etid == 0) {
+            tma_store_5d(&tmy, sOut, tc.ow0, oh0, tc.od, tc.n0, tc.n);
+            bulk_commit();
+          }
         }
       }
     }
@@ -443,19 +471,22 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// Shared memory besides the stages: output staging, bias, barriers, and the
-// slack for aligning the dynamic base to 1024 bytes.
-constexpr size_t fixed_smem(int BN) {
-  return static_cast<size_t>(kBM) * BN * 2 + BN * 4 + (2 * kMaxStages + 5) * 8 + 8 + 1024;
+// Shared memory besides the stages: output staging (when the output goes out
+// through TMA stores), bias, barriers, and the slack for aligning the dynamic
+// base to 1024 bytes.
+constexpr size_t fixed_smem(int BN, bool staging) {
+  return (staging ? static_cast<size_t>(kBM) * BN * 2 : 0) + BN * 4 + (2 * kMaxStages + 5) * 8 +
+         8 + 1024;
 }
 constexpr size_t kSmemBudget = 232448;  // sm_100 opt-in maximum per CTA
 
-template <typename T, int BN>
+template <typename T, int BN, int MT, int KB>
 int launch_conv(const CUtensorMap& tmx, const CUtensorMap& tmw, const CUtensorMap& tmy,
-                const ConvParams& prm, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(prm.stages) * prm.stage_bytes + fixed_smem(BN);
+                const ConvParams& prm, bool staging, cudaStream_t stream) {
+  const size_t smem = static_cast<size_t>(prm.stages) * prm.stage_bytes + fixed_smem(BN, staging);
   if (smem > kSmemBudget) return fail_unsupported("conv3d stage geometry exceeds shared memory");
-  auto kern = conv3d_tc_kernel<T, BN>;
+  if (prm.out_tma && !staging) return fail_arg("conv3d TMA output without staging");
+  auto kern = conv3d_tc_kernel<T, BN, MT, KB>;
   B200_CUDA_CHECK(
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int grid = std::min(prm.num_tiles, sm_count());
@@ -524,54 +555,107 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   }
   if (BW < 8) return fail_arg("conv3d tile width must be >= 8");
   const int BH = kBM / BW;
-  const int64_t Cin_pad = (Cin + kBK - 1) / kBK * kBK;
   const int64_t taps = KD * KH * KW;
-
-  // kh grouping: one A box of BH + (KH - 1) * dh rows serves all KH taps of a
-  // (kd, kw) pair -- half the input traffic and a third of the pipeline
-  // hand-offs of one box per tap -- when it still leaves >= 3 stages.
-  // Variant bits 10-11: 1 = one tap per k-block, 2 = grouped whenever it fits.
-  const int kgmode = (variant >> 10) & 3;
-  const size_t btap = static_cast<size_t>(BN) * kBK * 2;
-  const size_t budget = kSmemBudget - fixed_smem(BN);
-  auto geom = [&](int khg, int* stages, int* a_bytes, int* stage_bytes) {
-    const int64_t rows = BH + (khg - 1) * dh;
-    if (rows > 256) return false;
-    *a_bytes = static_cast<int>(rows * BW * kBK * 2);
-    *stage_bytes = *a_bytes + khg * static_cast<int>(btap);
-    *stages = static_cast<int>(std::min<size_t>(kMaxStages, budget / *stage_bytes));
-    return *stages >= 2;
+  const int64_t Cin_pad = (Cin + kBK - 1) / kBK * kBK;   // packed weight row length
+  const int64_t tiles_w = (Wo + BW - 1) / BW, tiles_n = (Cout + BN - 1) / BN;
+  auto tiles_for = [&](int mt) {
+    return N * Do * ((Ho + BH * mt - 1) / (BH * mt)) * tiles_w * tiles_n;
   };
-  int khg = 1, stages = 0, a_bytes = 0, stage_bytes = 0;
-  if (kgmode != 1 && KH > 1 && geom(static_cast<int>(KH), &stages, &a_bytes, &stage_bytes) &&
-      (stages >= 3 || kgmode == 2)) {
-    khg = static_cast<int>(KH);
-  } else if (!geom(1, &stages, &a_bytes, &stage_bytes)) {
-    return fail_unsupported("conv3d tile does not fit in shared memory");
+  // NCDHW output through TMA stores when TMA can address it: 16-byte aligned
+  // base, rows of Wo elements a multiple of 16 bytes (variant bit 9 disables).
+  const bool tma_out_ok = !y_cl && aligned16(y) && (Wo % 8) == 0 && ((variant >> 9) & 1) == 0;
+
+  // Tile geometry.  MT M tiles per CTA tile share each weight box: per MMA
+  // clock the CTA then streams ~1/MT of the weight bytes; with MT > 1 the
+  // k-block is 32 channels so that three stages still fit.  kh grouping: one
+  // A box of MT * BH + (KH - 1) * dh rows serves all KH taps of a (kd, kw)
+  // pair.  Variant bits 10-11: 1 = one tap per k-block, 2 = grouped whenever
+  // it fits; bits 12-13: 1/2/3 force MT = 1/2/4 (0 = choose).
+  struct Geo {
+    int mt = 1, kb = kBK, khg = 1, stages = 0, a_bytes = 0, stage_bytes = 0;
+    bool staging = false;
+  };
+  auto geom = [&](int mt, int kb, int khg, bool staging, Geo* g) {
+    const int64_t rows = static_cast<int64_t>(mt) * BH + (khg - 1) * dh;
+    if (rows > 256) return false;
+    const size_t budget = kSmemBudget - fixed_smem(BN, staging);
+    g->mt = mt;
+    g->kb = kb;
+    g->khg = khg;
+    g->staging = staging;
+    g->a_bytes = static_cast<int>(rows * BW * kb * 2);
+    g->stage_bytes = g->a_bytes + khg * BN * kb * 2;
+    g->stages = static_cast<int>(std::min<size_t>(kMaxStages, budget / g->stage_bytes));
+    return g->stages >= 2;
+  };
+  const int kgmode = (variant >> 10) & 3;
+  const int mt_code = (variant >> 12) & 3;
+  // Geometry for a given MT: kh-grouped when that leaves >= 3 stages (any
+  // number >= 2 when forced), else one tap per k-block; the output staging
+  // tile only when three stages remain beside it.
+  auto plan = [&](int mt, Geo* g) {
+    const int kb = mt == 1 ? kBK : 32;
+    const bool group = kgmode != 1 && KH > 1;
+    const int nopt = group ? 2 : 1;
+    for (int o = 0; o < nopt; ++o) {
+      const int khg = (group && o == 0) ? static_cast<int>(KH) : 1;
+      const bool last = o == nopt - 1;
+      const int need = (last || kgmode == 2) ? 2 : 3;
+      if (tma_out_ok && geom(mt, kb, khg, true, g) && g->stages >= std::max(need, 3)) return true;
+      if (geom(mt, kb, khg, false, g) && g->stages >= need) return true;
+    }
+    return false;
+  };
+  Geo g;
+  bool planned = false;
+  if (mt_code != 0) {
+    const int mt = mt_code == 1 ? 1 : (mt_code == 2 ? 2 : 4);
+    if (mt > 1 && BN > 128) return fail_unsupported("conv3d: MT > 1 needs Cout tiles <= 128");
+    planned = plan(mt, &g);
+  } else {
+    // Several M tiles per CTA when there are still >= 2 tiles per SM and the
+    // accumulators stay double-buffered in TMEM (2 * MT * BN <= 512 columns,
+    // so the epilogue of one tile overlaps the MMAs of the next): MT = 4 for
+    // BN = 64, MT = 2 for BN = 128.  (MT = 4 at BN = 128 single-buffers and
+    // measured slower than MT = 2 on the video stack's conv.)
+    const int64_t want = 2LL * sm_count();
+    for (int mt : {4, 2}) {
+      if (planned || BN > 128 || 2 * mt * BN > 512 || tiles_for(mt) < want) continue;
+      Geo c;
+      if (plan(mt, &c) && c.stages >= 3) {
+        g = c;
+        planned = true;
+      }
+    }
+    if (!planned) planned = plan(1, &g);
   }
-  const int a_rows_h = BH + (khg - 1) * static_cast<int>(dh);
+  if (!planned) return fail_unsupported("conv3d tile does not fit in shared memory");
+  const int khg = g.khg, stages = g.stages, a_bytes = g.a_bytes, stage_bytes = g.stage_bytes;
+  const int KB = g.kb, MT = g.mt;
+  const int a_rows_h = MT * BH + (khg - 1) * static_cast<int>(dh);
 
   CUtensorMap tmx, tmw;
+  const CUtensorMapSwizzle swz = KB == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUtensorMapDataType dt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   {
     cuuint64_t dims[5] = {(cuuint64_t)Cin, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)N};
     cuuint64_t strides[4] = {(cuuint64_t)(Cin * 2), (cuuint64_t)(W * Cin * 2),
                              (cuuint64_t)(H * W * Cin * 2), (cuuint64_t)(D * H * W * Cin * 2)};
-    cuuint32_t box[5] = {(cuuint32_t)kBK, (cuuint32_t)BW, (cuuint32_t)a_rows_h, 1, 1};
+    cuuint32_t box[5] = {(cuuint32_t)KB, (cuuint32_t)BW, (cuuint32_t)a_rows_h, 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = encode(&tmx, dt, 5, const_cast<void*>(xcl), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail_unsupported("input tensor map rejected");
   }
   {
     cuuint64_t dims[3] = {(cuuint64_t)Cin_pad, (cuuint64_t)Cout, (cuuint64_t)taps};
     cuuint64_t strides[2] = {(cuuint64_t)(Cin_pad * 2), (cuuint64_t)(Cout * Cin_pad * 2)};
-    cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)BN, 1};
+    cuuint32_t box[3] = {(cuuint32_t)KB, (cuuint32_t)BN, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = encode(&tmw, dt, 3, const_cast<void*>(wp), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail_unsupported("weight tensor map rejected");
   }
@@ -591,13 +675,14 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   prm.dw = (int)dw;
   prm.BW = BW;
   prm.BH = BH;
-  prm.tiles_w = (int)((Wo + BW - 1) / BW);
-  prm.tiles_h = (int)((Ho + BH - 1) / BH);
-  prm.tiles_n = (int)((Cout + BN - 1) / BN);
-  const int64_t nt = N * Do * prm.tiles_h * prm.tiles_w * prm.tiles_n;
+  prm.MT = MT;
+  prm.tiles_w = (int)tiles_w;
+  prm.tiles_h = (int)((Ho + BH * MT - 1) / (BH * MT));
+  prm.tiles_n = (int)tiles_n;
+  const int64_t nt = tiles_for(MT);
   if (nt > 0x7fffffffLL) return fail_unsupported("too many tiles");
   prm.num_tiles = (int)nt;
-  prm.cchunks = (int)(Cin_pad / kBK);
+  prm.cchunks = (int)((Cin + KB - 1) / KB);
   prm.khg = khg;
   prm.khb = static_cast<int>(KH) / khg;
   prm.a_bytes = a_bytes;
@@ -618,7 +703,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   CUtensorMap tmy;
   std::memset(&tmy, 0, sizeof(tmy));
   prm.out_tma = 0;
-  if (!y_cl && aligned16(y) && (Wo % 8) == 0 && ((variant >> 9) & 1) == 0) {
+  if (tma_out_ok && g.staging) {
     cuuint64_t dims[5] = {(cuuint64_t)Wo, (cuuint64_t)Ho, (cuuint64_t)Do, (cuuint64_t)Cout,
                           (cuuint64_t)N};
     cuuint64_t strides[4] = {(cuuint64_t)(Wo * 2), (cuuint64_t)(Ho * Wo * 2),
@@ -630,9 +715,18 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     prm.out_tma = (r == CUDA_SUCCESS) ? 1 : 0;
   }
-  if (BN == 64) return launch_conv<T, 64>(tmx, tmw, tmy, prm, stream);
-  if (BN == 128) return launch_conv<T, 128>(tmx, tmw, tmy, prm, stream);
-  return launch_conv<T, 256>(tmx, tmw, tmy, prm, stream);
+  const bool stg = g.staging;
+  if (MT == 1) {
+    if (BN == 64) return launch_conv<T, 64, 1, 64>(tmx, tmw, tmy, prm, stg, stream);
+    if (BN == 128) return launch_conv<T, 128, 1, 64>(tmx, tmw, tmy, prm, stg, stream);
+    return launch_conv<T, 256, 1, 64>(tmx, tmw, tmy, prm, stg, stream);
+  }
+  if (MT == 2) {
+    if (BN == 64) return launch_conv<T, 64, 2, 32>(tmx, tmw, tmy, prm, stg, stream);
+    return launch_conv<T, 128, 2, 32>(tmx, tmw, tmy, prm, stg, stream);
+  }
+  if (BN == 64) return launch_conv<T, 64, 4, 32>(tmx, tmw, tmy, prm, stg, stream);
+  return launch_conv<T, 128, 4, 32>(tmx, tmw, tmy, prm, stg, stream);
 }
 
 }  // namespace

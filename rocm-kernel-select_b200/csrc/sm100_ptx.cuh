@@ -191,6 +191,14 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
          (static_cast<uint64_t>(2) << 61);
 }
 
+// K-major operand with 64-byte rows (32 16-bit elements) in the SWIZZLE_64B
+// layout TMA writes: 8-row atoms of 512 bytes (SBO), layout type 4.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(512 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(4) << 61);
+}
+
 // Instruction descriptor, kind::f16: fp32 accumulator, A/B both `fmt`
 // (0 = f16, 1 = bf16), both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int fmt, int M, int N) {

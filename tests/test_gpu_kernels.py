@@ -212,6 +212,54 @@ def test_conv3d_shapes(cuda, dt, N, Cin, D, H, W, Cout, k, p):
     assert oracle.rel_l2(_np(y), ref) <= TOL[dt]
 
 
+# Several M tiles per CTA (variant bits 12-13: 2 -> MT 2, 3 -> MT 4; 32-channel
+# k-blocks), with ragged H, partial channel chunks and Cout tiles, dilation,
+# KH = 1, direct stores (bit 9) and channels-last input/output.
+_MT2, _MT4, _NO_TMA_OUT = 2 << 12, 3 << 12, 1 << 9
+
+
+@pytest.mark.parametrize("dt,N,Cin,D,H,W,Cout,k,p,dil,variant,cl", [
+    ("f16", 1, 128, 4, 12, 128, 128, (3, 3, 3), (1, 1, 1), (1, 1, 1), _MT4, False),
+    ("bf16", 1, 128, 4, 12, 128, 128, (3, 3, 3), (1, 1, 1), (1, 1, 1), _MT2, False),
+    ("f16", 2, 40, 3, 7, 32, 48, (3, 3, 3), (1, 1, 1), (1, 1, 1), _MT4, False),
+    ("bf16", 1, 64, 5, 10, 64, 64, (3, 3, 3), (2, 2, 2), (2, 2, 2), _MT2, False),
+    ("f16", 1, 64, 3, 8, 64, 64, (3, 1, 3), (1, 0, 1), (1, 1, 1), _MT4, False),
+    ("bf16", 1, 96, 3, 9, 32, 128, (3, 3, 3), (1, 1, 1), (1, 1, 1), _MT2 | _NO_TMA_OUT, False),
+    ("f16", 1, 64, 4, 8, 64, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), _MT4, True),
+    ("bf16", 1, 32, 3, 6, 16, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), _MT2, True),
+])
+def test_conv3d_multi_mtile(cuda, dt, N, Cin, D, H, W, Cout, k, p, dil, variant, cl):
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(Cin * 7 + Cout + variant)
+    x = torch.randn(N, Cin, D, H, W, generator=g).to(torch_dtype(dt))
+    w = _kaiming((Cout, Cin) + k, g).to(torch_dtype(dt))
+    b = torch.randn(Cout, generator=g).to(torch_dtype(dt)) * 0.1
+    ref = torch.nn.functional.conv3d(x.float(), w.float(), b.float(), padding=p, dilation=dil)
+    xin = x.permute(0, 2, 3, 4, 1).contiguous() if cl else x
+    y = ops.conv3d(xin.to(cuda), w.to(cuda), b.to(cuda), (1, 1, 1), p, dil, variant=variant,
+                   x_channels_last=cl, out_channels_last=cl)
+    assert y is not None
+    if cl:
+        y = y.permute(0, 4, 1, 2, 3)
+    assert tuple(y.shape) == tuple(ref.shape)
+    assert oracle.rel_l2(_np(y), ref.numpy()) <= TOL[dt]
+    _no_fault()
+
+
+def test_conv3d_auto_multi_mtile_large(cuda):
+    """Large enough for the automatic choice of 4 M tiles per CTA (>= 2 tiles
+    per SM): Cin = Cout = 64, 24 x 64 x 128, k3 p1, fp16."""
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(77)
+    x = torch.randn(1, 64, 24, 64, 128, generator=g).half()
+    w = _kaiming((64, 64, 3, 3, 3), g).half()
+    b = torch.randn(64, generator=g).half() * 0.1
+    y = ops.conv3d(x.to(cuda), w.to(cuda), b.to(cuda), (1, 1, 1), (1, 1, 1), (1, 1, 1))
+    ref = torch.nn.functional.conv3d(x.float(), w.float(), b.float(), padding=1)
+    assert oracle.rel_l2(_np(y), ref.numpy()) <= 2e-3
+    _no_fault()
+
+
 def test_conv3d_channels_last_io(cuda):
     from amd_tuned_torch import ops
     g = torch.Generator().manual_seed(9)
