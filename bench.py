@@ -46,6 +46,12 @@ L2_BYTES = 126 * 1024 * 1024
 ROTATE_BYTES = 3 * L2_BYTES   # inputs rotated over > L2 so every step reads HBM
 
 
+def _nbuf(bytes_per_op: int, least: int = 3) -> int:
+    """Buffers to rotate so that the input + output bytes touched between two
+    uses of the same buffer exceed 3 x L2."""
+    return max(least, -(-ROTATE_BYTES // bytes_per_op))
+
+
 def _peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -201,7 +207,7 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         x = torch.randn(8, 256, 2048, generator=g)
         w = _kaiming((256, 1, 3), g)
         b = _kaiming((256, 1), g).reshape(256)
-        nbuf = max(2, ROTATE_BYTES // (x.numel() * 4 * 2))
+        nbuf = _nbuf(x.numel() * 4 * 2)
         xs = [x.to(dev) for _ in range(nbuf)]
         wd, bd = w.reshape(256, 3).to(dev), b.to(dev)
         ys = [torch.empty(8, 256, 2048, device=dev) for _ in range(nbuf)]
@@ -224,7 +230,7 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         x = (torch.randn(4, 512, 128, 128, generator=g) * 2).bfloat16()
         w = (torch.rand(512, generator=g) + 0.5).bfloat16()
         b = (torch.randn(512, generator=g) * 0.1).bfloat16()
-        nbuf = max(2, ROTATE_BYTES // (x.numel() * 2 * 2))
+        nbuf = _nbuf(x.numel() * 2 * 2)
         xs = [x.to(dev) for _ in range(nbuf)]
         ys = [torch.empty_like(xs[0]) for _ in range(nbuf)]
         wd, bd = w.to(dev), b.to(dev)
@@ -233,7 +239,8 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         best = None
         for name, var in (("auto", ops.GN_AUTO), ("cluster4", ops.gn_cluster_variant(4)),
                           ("cluster8", ops.gn_cluster_variant(8)),
-                          ("cluster16", ops.gn_cluster_variant(16)), ("split", ops.GN_SPLIT)):
+                          ("cluster16", ops.gn_cluster_variant(16)), ("split", ops.GN_SPLIT),
+                          ("l2", ops.GN_L2)):
             y = ops.group_norm(xs[0], 32, wd, bd, 1e-6, variant=var)
             if y is None:
                 continue
@@ -333,7 +340,7 @@ def run_ours(args, rank, world, dev) -> dict:
     stream = torch.cuda.current_stream(dev)
     x, w, b = make_cfg2()
     xd, wd, bd = x.to(dev), w.to(dev), b.to(dev)
-    nbuf = max(4, ROTATE_BYTES // (x.numel() * 2 * 2))
+    nbuf = _nbuf(x.numel() * 2 * 2, 4)
     xs = [xd.clone() for _ in range(nbuf)]
     ys = [torch.empty_like(xd) for _ in range(nbuf)]
 

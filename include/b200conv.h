@@ -59,6 +59,8 @@ int b200_sm_count(void);
  * (src/cuda/group_norm.cu:40-104).  x, y: contiguous [N, C, S] with
  * S = product of spatial dims; gamma/beta: [C] of `affine_dtype` or NULL.
  * variant: 0 auto, 1 split (stats + apply, uses workspace),
+ *          2 two-pass: statistics pass, then a normalise pass that re-reads
+ *            x (from L2 when the tensor fits), both 16-byte vectorised,
  *          16 + k: single-read cluster kernel with k CTAs per group
  *          (k in {1, 2, 4, 8, 16}; group slice held in shared memory). */
 size_t b200_gn_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int dtype,

@@ -267,6 +267,7 @@ def _group_norm_candidates(input, num_groups, weight, bias, eps):
                                                     ops.gn_cluster_variant(k))))
         cands.append(("native_split", _gn_thunk(input, num_groups, weight, bias, eps,
                                                 ops.GN_SPLIT)))
+        cands.append(("native_l2", _gn_thunk(input, num_groups, weight, bias, eps, ops.GN_L2)))
     cands.append(("stock", lambda: orig(input, num_groups, weight, bias, eps)))
     return cands
 

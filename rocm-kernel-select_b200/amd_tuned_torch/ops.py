@@ -129,7 +129,7 @@ def clear_caches() -> None:
 
 
 # ------------------------------------------------------------ GroupNorm ---
-GN_AUTO, GN_SPLIT = 0, 1
+GN_AUTO, GN_SPLIT, GN_L2 = 0, 1, 2   # auto; stats+apply; two-pass L2-resident
 
 
 def gn_cluster_variant(k: int) -> int:

@@ -166,6 +166,15 @@ __device__ __forceinline__ void st_stream16(void* p, const uint4& r) {
                : "memory");
 }
 
+// Programmatic dependent launch.  launch_dependents lets the next grid in the
+// stream (launched with the programmatic-serialization attribute) start its
+// prologue early; wait blocks until every grid this one depends on has
+// completed and its memory is visible.  Both are no-ops without PDL.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

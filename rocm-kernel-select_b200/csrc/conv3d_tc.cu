@@ -139,6 +139,10 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialisation: everything above (barrier
+  // set-up, TMEM allocation, descriptor prefetch) overlaps the previous
+  // kernel; no global memory is touched before it has completed.
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -389,6 +393,7 @@ __global__ void __launch_bounds__(256)
 to_cl16_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t C, int64_t S) {
   static_assert(sizeof(T) == 2, "16-bit elements");
   __shared__ uint32_t tile[64 * 33];
+  pdl_launch_dependents();  // the conv kernel's prologue may overlap this copy
   const int64_t n = blockIdx.z;
   const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 64;
   const int64_t p0 = static_cast<int64_t>(blockIdx.x) * 64;
@@ -441,6 +446,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 to_cl_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t C, int64_t S) {
   __shared__ T tile[64][66];
+  pdl_launch_dependents();
   const int64_t n = blockIdx.z;
   const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 64;
   const int64_t p0 = static_cast<int64_t>(blockIdx.x) * 64;
@@ -490,8 +496,17 @@ int launch_conv(const CUtensorMap& tmx, const CUtensorMap& tmw, const CUtensorMa
   B200_CUDA_CHECK(
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int grid = std::min(prm.num_tiles, sm_count());
-  kern<<<grid, kConvThreads, smem, stream>>>(tmx, tmw, tmy, prm);
-  B200_LAUNCH_CHECK("conv3d_tc_kernel");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kConvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tmx, tmw, tmy, prm));
   return B200_OK;
 }
 

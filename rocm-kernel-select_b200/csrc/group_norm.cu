@@ -306,6 +306,7 @@ gn_apply_cl_kernel(const T* __restrict__ x, const float* __restrict__ stats,
                    T* __restrict__ y, int affine_dt, int64_t C, int64_t S, int G, int Cg,
                    float eps) {
   __shared__ float tile[32][65];
+  pdl_launch_dependents();  // the consuming conv kernel's prologue may overlap
   const int64_t n = blockIdx.z;
   const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 32;
   const int64_t p0 = static_cast<int64_t>(blockIdx.x) * 64;
@@ -331,6 +332,189 @@ gn_apply_cl_kernel(const T* __restrict__ x, const float* __restrict__ stats,
   for (int pp = lp; pp < 64; pp += 8) {
     const int64_t p = p0 + pp, c = c0 + lc;
     if (p < S && c < C) y[(n * S + p) * C + c] = from_f32<T>(tile[lc][pp]);
+  }
+}
+
+// -------------------------------------------- two-pass, L2-resident ----
+// For tensors that fit in L2 (126 MB): pass 1 reads x from HBM once, marking
+// the lines evict_last, and writes per-chunk shifted sums; pass 2 re-reads x
+// (now from L2), merges its group's partial sums in fp64, and streams y out.
+// HBM traffic stays at one read and one write of the tensor, and no cluster
+// lock-step is needed.  Each thread moves kL2Vec 16-byte vectors per pass,
+// all loads issued before the first use.
+constexpr int kL2Threads = 256;
+constexpr int kL2Vec = 8;
+constexpr int kL2MaxCh = 1024;   // channels of one chunk staged in shared memory
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last(float fraction) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, %1;" : "=l"(pol) : "f"(fraction));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint4 ld16_hint(const void* p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ void st16_hint(void* p, const uint4& r, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;"
+               ::"l"(p), "r"(r.x), "r"(r.y), "r"(r.z), "r"(r.w), "l"(pol)
+               : "memory");
+}
+
+// Pass 1: one CTA per (group, chunk of kL2Threads * kL2Vec vectors).  Sums
+// are shifted by the group's first element (the same shift for every chunk
+// of a group, so the merge is a plain fp64 sum).
+template <typename T>
+__global__ void __launch_bounds__(kL2Threads)
+gn_l2_stats_kernel(const T* __restrict__ x, float2* __restrict__ part, int64_t M, int chunks,
+                   float keep_fraction) {
+  constexpr int V = Vec16<T>::N;
+  constexpr int64_t kChunk = static_cast<int64_t>(kL2Threads) * kL2Vec * V;
+  __shared__ float scratch[33];
+  const int64_t ng = blockIdx.x / chunks;
+  const int ch = blockIdx.x % chunks;
+  const T* grp = x + ng * M;
+  const int64_t beg = static_cast<int64_t>(ch) * kChunk;
+  const uint64_t pol = l2_policy_evict_last(keep_fraction);
+  uint4 r[kL2Vec];
+#pragma unroll
+  for (int u = 0; u < kL2Vec; ++u) {
+    const int64_t e = beg + (static_cast<int64_t>(u) * kL2Threads + threadIdx.x) * V;
+    if (e < M) r[u] = ld16_hint(grp + e, pol);
+  }
+  const float shift = to_f32(grp[0]);
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int u = 0; u < kL2Vec; ++u) {
+    const int64_t e = beg + (static_cast<int64_t>(u) * kL2Threads + threadIdx.x) * V;
+    if (e < M) {
+      float v[V];
+      unpack16<T>(r[u], v);
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const float d = v[k] - shift;
+        s1 += d;
+        s2 = fmaf(d, d, s2);
+      }
+    }
+  }
+  s1 = block_sum<kL2Threads>(s1, scratch);
+  s2 = block_sum<kL2Threads>(s2, scratch);
+  if (threadIdx.x == 0) part[ng * chunks + ch] = make_float2(s1, s2);
+  pdl_launch_dependents();
+}
+
+// Pass 2: same chunking, walked in reverse (the chunks pass 1 read last are
+// the likeliest still in L2).  The x loads are issued before waiting on pass 1
+// (x is not written by it), so they overlap pass 1's tail.  The channels the
+// chunk spans get their gamma / beta staged in shared memory once.
+template <typename T, bool SILU>
+__global__ void __launch_bounds__(kL2Threads)
+gn_l2_apply_kernel(const T* __restrict__ x, const float2* __restrict__ part,
+                   const void* __restrict__ gamma, const void* __restrict__ beta,
+                   T* __restrict__ y, int affine_dt, int64_t S, int G, int Cg, int64_t M,
+                   int chunks, float eps) {
+  constexpr int V = Vec16<T>::N;
+  constexpr int64_t kChunk = static_cast<int64_t>(kL2Threads) * kL2Vec * V;
+  __shared__ float stat[2];
+  __shared__ float sG[kL2MaxCh], sB[kL2MaxCh];
+  const int64_t t = static_cast<int64_t>(gridDim.x) - 1 - blockIdx.x;
+  const int64_t ng = t / chunks;
+  const int ch = static_cast<int>(t % chunks);
+  const T* grp = x + ng * M;
+  T* out = y + ng * M;
+  const int64_t beg = static_cast<int64_t>(ch) * kChunk;
+  const uint64_t pol = l2_policy_evict_first();
+  uint4 r[kL2Vec];
+#pragma unroll
+  for (int u = 0; u < kL2Vec; ++u) {
+    const int64_t e = beg + (static_cast<int64_t>(u) * kL2Threads + threadIdx.x) * V;
+    if (e < M) r[u] = ld16_hint(grp + e, pol);
+  }
+  // Channels [c_lo, c_hi] of the group hold this chunk.
+  const int64_t last = min64(M, beg + kChunk) - 1;
+  const int c_lo = static_cast<int>(beg / S);
+  const int nch = static_cast<int>(last / S) - c_lo + 1;
+  const bool staged = nch <= kL2MaxCh;
+  const int c0 = static_cast<int>(ng % G) * Cg;
+  if (staged) {
+    for (int c = threadIdx.x; c < nch; c += kL2Threads) {
+      sG[c] = gamma ? load_param(gamma, affine_dt, c0 + c_lo + c) : 1.f;
+      sB[c] = beta ? load_param(beta, affine_dt, c0 + c_lo + c) : 0.f;
+    }
+  }
+  pdl_wait();
+  if (threadIdx.x < 32) {
+    // Fixed-order fp64 merge of the group's partial sums (lane-strided, then
+    // a butterfly): every CTA of the group computes identical statistics.
+    double a = 0.0, b = 0.0;
+    for (int c = threadIdx.x; c < chunks; c += 32) {
+      const float2 q = part[ng * chunks + c];
+      a += q.x;
+      b += q.y;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    if (threadIdx.x == 0) {
+      const double n = static_cast<double>(M);
+      const double mean_d = a / n;
+      const double var = fmax(b / n - mean_d * mean_d, 0.0);
+      stat[0] = static_cast<float>(mean_d + static_cast<double>(to_f32(grp[0])));
+      stat[1] = 1.0f / sqrtf(static_cast<float>(var) + eps);
+    }
+  }
+  __syncthreads();
+  const float mean = stat[0], rstd = stat[1];
+  // Channel of this thread's first vector; later vectors are kL2Threads * V
+  // elements further on.
+  const int64_t e0 = beg + static_cast<int64_t>(threadIdx.x) * V;
+  int64_t q = e0 / S, rem = e0 - q * S;
+  constexpr int64_t kStep = static_cast<int64_t>(kL2Threads) * V;
+#pragma unroll
+  for (int u = 0; u < kL2Vec; ++u) {
+    const int64_t e = e0 + u * kStep;
+    if (u > 0) {
+      rem += kStep;
+      if (rem >= S) {
+        if (rem < 2 * S) {
+          rem -= S;
+          q += 1;
+        } else {
+          q += rem / S;
+          rem %= S;
+        }
+      }
+    }
+    if (e < M) {
+      const int c = static_cast<int>(q);
+      float a, b;
+      if (staged) {
+        a = rstd * sG[c - c_lo];
+        b = sB[c - c_lo];
+      } else {
+        a = gamma ? rstd * load_param(gamma, affine_dt, c0 + c) : rstd;
+        b = beta ? load_param(beta, affine_dt, c0 + c) : 0.f;
+      }
+      float v[V];
+      unpack16<T>(r[u], v);
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        v[k] = fmaf(v[k] - mean, a, b);
+        if (SILU) v[k] = silu(v[k]);
+      }
+      st16_hint(out + e, pack16<T>(v), pol);
+    }
   }
 }
 
@@ -472,6 +656,58 @@ int launch_apply(const T* x, const float* stats, const void* gamma, const void* 
   return B200_OK;
 }
 
+// Two-pass L2-resident path (variant 2).  Declines (> 0) unless x/y are
+// 16-byte aligned with S a multiple of the vector width.
+constexpr double kL2KeepBytes = 80e6;  // evict_last budget, well inside the 126 MB L2
+
+int64_t l2_chunks(const GnShape& sh, size_t esize) {
+  const int64_t chunk = static_cast<int64_t>(kL2Threads) * kL2Vec * (16 / static_cast<int64_t>(esize));
+  return (sh.M + chunk - 1) / chunk;
+}
+
+size_t l2_ws_bytes(const GnShape& sh, size_t esize) {
+  return static_cast<size_t>(sh.groups * l2_chunks(sh, esize)) * sizeof(float2);
+}
+
+// Whole tensor within the L2 keep budget: the re-read of pass 2 hits L2.
+bool l2_fits(const GnShape& sh, size_t esize) {
+  return static_cast<double>(sh.N) * sh.C * sh.S * esize <= kL2KeepBytes;
+}
+
+template <typename T>
+int launch_l2(const T* x, const void* gamma, const void* beta, T* y, int affine_dt,
+              const GnShape& sh, float eps, bool silu, void* ws, size_t ws_bytes,
+              cudaStream_t stream) {
+  if (!vec_ok<T>(x, y, sh)) return fail_unsupported("two-pass GroupNorm needs 16-byte rows");
+  const int64_t chunks = l2_chunks(sh, sizeof(T));
+  const int64_t blocks = sh.groups * chunks;
+  if (blocks > 0x7fffffffLL) return fail_unsupported("grid too large");
+  if (ws == nullptr || ws_bytes < l2_ws_bytes(sh, sizeof(T)))
+    return fail_arg("GroupNorm workspace too small");
+  float2* part = static_cast<float2*>(ws);
+  const double bytes = static_cast<double>(sh.N) * sh.C * sh.S * sizeof(T);
+  const float keep = static_cast<float>(std::min(1.0, kL2KeepBytes / bytes));
+  const unsigned grid = static_cast<unsigned>(blocks);
+  gn_l2_stats_kernel<T><<<grid, kL2Threads, 0, stream>>>(x, part, sh.M, (int)chunks, keep);
+  B200_LAUNCH_CHECK("gn_l2_stats_kernel");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kL2Threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto kern = silu ? gn_l2_apply_kernel<T, true> : gn_l2_apply_kernel<T, false>;
+  const float2* cpart = part;
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, x, cpart, gamma, beta, y, affine_dt, sh.S,
+                                     static_cast<int>(sh.G), static_cast<int>(sh.Cg), sh.M,
+                                     static_cast<int>(chunks), eps));
+  return B200_OK;
+}
+
 // Smallest power-of-two cluster whose per-CTA slice fits `target` bytes.
 int auto_cluster(const GnShape& sh, size_t esize) {
   const int64_t bytes = sh.M * static_cast<int64_t>(esize);
@@ -488,6 +724,8 @@ int gn_fwd_typed(const void* xv, const void* gamma, const void* beta, void* yv, 
                  cudaStream_t stream) {
   const T* x = static_cast<const T*>(xv);
   T* y = static_cast<T*>(yv);
+  if (variant == 0 && l2_fits(sh, sizeof(T)) && vec_ok<T>(x, y, sh)) variant = 2;
+  if (variant == 2) return launch_l2<T>(x, gamma, beta, y, affine_dt, sh, eps, false, ws, ws_bytes, stream);
   if (variant == 0) {
     const int k = auto_cluster(sh, sizeof(T));
     if (k > 0) {
@@ -535,7 +773,9 @@ size_t b200_gn_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int d
     // fallback's scratch available.
   }
   const size_t stats_bytes = ((static_cast<size_t>(sh.groups * 3) * sizeof(float) + 15) / 16) * 16;
-  return stats_bytes + stats_ws_bytes(sh, dtype);
+  const size_t split = stats_bytes + stats_ws_bytes(sh, dtype);
+  const size_t l2 = l2_ws_bytes(sh, dtype_size(dtype));
+  return split > l2 ? split : l2;
 }
 
 int b200_gn_fwd(const void* x, const void* gamma, const void* beta, void* y, int dtype,
