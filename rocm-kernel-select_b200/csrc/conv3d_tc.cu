@@ -39,7 +39,8 @@
 namespace b200 {
 namespace {
 
-constexpr int kConvThreads = 192;  // 6 warps
+constexpr int kConvThreads = 192;       // 6 warps
+constexpr int kConvThreadsFused = 320;  // + 4 transposer warps
 constexpr int kBM = 128;
 constexpr int kBK = 64;            // weight packing granule: Cin is padded to a multiple of 64
 constexpr int kMaxStages = 8;
@@ -61,6 +62,9 @@ struct ConvParams {
   int y_cl;
   int out_tma;
   int* flags;
+  // Fused NCDHW input (FUSE kernels): one raw box {raw_w, khg rows, 1, 64, 1}
+  // per (kd, channel chunk), starting at column ow0 - wpad8 (a multiple of 8).
+  int raw_w, raw_bytes, raw_tx, wpad8, lbw;
 };
 
 struct TileCoord {
@@ -87,11 +91,20 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const ConvParams& p, int
 // A rows of neighbouring taps.  KB: channels per k-block -- 64 (128-byte
 // K-major rows, SWIZZLE_128B) or 32 (64-byte rows, SWIZZLE_64B, half the
 // stage size so that MT = 4 still leaves three stages).
-template <typename T, int BN, int MT, int KB>
-__global__ void __launch_bounds__(kConvThreads, 1)
+//
+// FUSE: x is NCDHW.  Instead of a channels-last copy, the producer loads ONE
+// raw box {W span, rows, 1, 64 channels, 1} per (kd, channel chunk) -- its
+// innermost coordinate rounded down to a multiple of 8 elements, the rest
+// of the W span covered by a wider box -- and warps 6-9 write the K-major,
+// 128-byte-swizzled A tile of each kw shift from it into the pipeline stage
+// (generic stores, then a proxy fence before the stage is handed to the
+// MMA warp).  One global read of the input serves all KW shifts.
+template <typename T, int BN, int MT, int KB, bool FUSE>
+__global__ void __launch_bounds__(FUSE ? kConvThreadsFused : kConvThreads, 1)
 conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                  const __grid_constant__ CUtensorMap tmy, const ConvParams p) {
   static_assert(KB == 64 || KB == 32, "k-block of 32 or 64 channels");
+  static_assert(!FUSE || (MT == 1 && KB == 64), "fused NCDHW input: one M tile, 64-channel k-blocks");
   constexpr int kRow = KB * 2;               // bytes per K-major operand row
   constexpr int kBTap = BN * kRow;           // one tap's weight box
   constexpr int kAcc = MT * BN;              // TMEM columns of one tile's accumulators
@@ -106,14 +119,17 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sOut = smem + STAGES * p.stage_bytes;                   // [BN][128] staging
+  uint8_t* sRaw = smem + STAGES * p.stage_bytes;                   // FUSE: 2 raw boxes
+  uint8_t* sOut = sRaw + (FUSE ? 2 * p.raw_bytes : 0);             // [BN][128] staging
   float* sBias = reinterpret_cast<float*>(sOut + (p.out_tma ? kBM * BN * 2 : 0));  // [BN]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sBias + BN);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sBias + BN + 4);   // + 16-byte scratch
   uint64_t* empty = full + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;  // [2]
   uint64_t* tempty = tfull + 2;      // [2]
   uint64_t* drain = tempty + 2;      // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* rfull = drain + 1;       // [2] FUSE: raw box landed
+  uint64_t* rempty = rfull + 2;      // [2] FUSE: raw box consumed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + 2);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -123,8 +139,14 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
     prefetch_tmap(&tmw);
     if (p.out_tma) prefetch_tmap(&tmy);
     for (int s = 0; s < kMaxStages; ++s) {
-      mbar_init(&full[s], 1);
+      // FUSE: a stage is full once its weight boxes landed AND the
+      // transposer warps handed over its A tile.
+      mbar_init(&full[s], FUSE ? 2 : 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int r = 0; r < 2; ++r) {
+      mbar_init(&rfull[r], 1);
+      mbar_init(&rempty[r], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
@@ -144,7 +166,68 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
   // kernel; no global memory is touched before it has completed.
   pdl_wait();
 
-  if (warp == 0) {
+  if (warp == 0 && FUSE) {
+    // --------------------------------------- TMA producer, fused NCDHW input
+    // Unit u = (kd, channel chunk): one raw box, then KW k-blocks (one per kw
+    // shift) whose weight boxes go into the stages the transposer fills.
+    int stage = 0;
+    uint32_t phase = 0;
+    int ru = 0;
+    bool ok = true;
+    const int units = p.kblocks / p.KW;
+    const int rot = p.rotate ? static_cast<int>((blockIdx.x * 7u) % units) : 0;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      const TileCoord tc = decode_tile(t, p, BN);
+      for (int uu = 0; uu < units && ok; ++uu, ++ru) {
+        int u = uu + rot;
+        if (u >= units) u -= units;
+        const int cc = u % p.cchunks, kd = u / p.cchunks;
+        const int r = ru & 1;
+        const uint32_t rph = static_cast<uint32_t>(ru >> 1) & 1u;
+        bool got = mbar_wait_bounded(&rempty[r], rph ^ 1u, abort, p.flags, 1);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_expect_tx(&rfull[r], static_cast<uint32_t>(p.raw_tx));
+          tma_load_5d(sRaw + r * p.raw_bytes, &tmx, &rfull[r], tc.ow0 - p.wpad8, tc.oh0 - p.ph,
+                      tc.od - p.pd + kd * p.dd, cc * KB, tc.n);
+        }
+        __syncwarp();
+        for (int kw = 0; kw < p.KW; ++kw) {
+          got = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, p.flags, 1);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            uint8_t* st = smem + stage * p.stage_bytes;
+            mbar_expect_tx(&full[stage], static_cast<uint32_t>(p.khg * kBTap));
+            for (int j = 0; j < p.khg; ++j) {
+              const int tap = (kd * p.KH + j) * p.KW + kw;
+              tma_load_3d(st + p.a_bytes + j * kBTap, &tmw, &full[stage], cc * KB, tc.n0, tap);
+            }
+          }
+          __syncwarp();
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      // Let the copies already issued land before shared memory goes away.
+      const int last = (stage + STAGES - 1) % STAGES;
+      mbar_wait_bounded(&full[last], (stage == 0 ? phase ^ 1u : phase), nullptr, nullptr, 0);
+      if (ru > 0) {
+        const int lr = (ru - 1) & 1;
+        mbar_wait_bounded(&rfull[lr], static_cast<uint32_t>((ru - 1) >> 1) & 1u, nullptr, nullptr, 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     // The whole warp walks the loop (waits included) so it stays converged;
     // one lane issues the copies.
@@ -265,6 +348,75 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       __syncwarp();
       mbar_wait_bounded(drain, 0, nullptr, nullptr, 0);
       __syncwarp();
+    }
+  } else if (FUSE && warp >= 6) {
+    // ------------------------------------------------ transposer (FUSE only)
+    // Raw box [64 channels][rows][raw_w] (16-bit) -> A tile of each kw shift:
+    // position q = row * BW + w is a 128-byte K-major row whose channel group
+    // cg (8 channels, 16 bytes) sits at chunk cg ^ (q & 7) (SWIZZLE_128B).
+    // Work item = (row, block of 8 raw columns, 32 channels): ldmatrix.trans
+    // turns four [8 channels x 8 columns] blocks into per-column channel rows
+    // and stmatrix writes each column's row to the A row of the output
+    // position that column feeds for this kw (rows outside the tile go to a
+    // scratch slot).  The unaligned kw shift only moves store addresses.
+    const int tt = threadIdx.x - 192;
+    const int twarp = tt >> 5;
+    const int rows = p.BH + (p.khg - 1) * p.dh;
+    const int plane = rows * p.raw_w;   // elements between two channels of the raw box
+    const int BWm = p.BW;
+    const uint32_t dummy = smem_u32(sBias + BN);   // 16 scratch bytes past the bias (see fixed_smem)
+    const int m = lane >> 3, i = lane & 7;      // this lane's matrix and row
+    int stage = 0;
+    uint32_t phase = 0;
+    int ru = 0;
+    bool ok = true;
+    const int units = p.kblocks / p.KW;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int uu = 0; uu < units && ok; ++uu, ++ru) {
+        const int r = ru & 1;
+        const uint32_t rph = static_cast<uint32_t>(ru >> 1) & 1u;
+        bool got = mbar_wait_bounded(&rfull[r], rph, abort, p.flags, 1);
+        if (!tp_bar_and(got)) {
+          ok = false;
+          break;
+        }
+        const uint32_t raw = smem_u32(sRaw + r * p.raw_bytes);
+        for (int kw = 0; kw < p.KW; ++kw) {
+          got = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, p.flags, 1);
+          if (!tp_bar_and(got)) {
+            ok = false;
+            break;
+          }
+          const uint32_t A = smem_u32(smem + stage * p.stage_bytes);
+          const int xs = p.wpad8 - p.pw + kw * p.dw;   // raw column feeding output w = 0
+          const int j0 = xs >> 3, j1 = (xs + BWm - 1) >> 3;
+          const int nblk = j1 - j0 + 1;
+          const int items = rows * nblk * 2;           // (row, column block, 32-channel half)
+          for (int it = twarp; it < items; it += 4) {
+            const int half = it & 1;
+            const int rb = it >> 1;
+            const int rr = rb / nblk, j = j0 + rb % nblk;
+            const int c = half * 32 + m * 8 + i;       // channel of this lane's source row
+            uint32_t v[4];
+            ldsm_x4_trans(raw + static_cast<uint32_t>(((c * rows + rr) * p.raw_w + 8 * j) * 2), v);
+            const int w = 8 * j + i - xs;              // output position fed by raw column 8j + i
+            const int q = rr * BWm + w;
+            const int cg = half * 4 + m;
+            const uint32_t dst = (w >= 0 && w < BWm)
+                                     ? A + static_cast<uint32_t>(q * 128 + ((cg ^ (q & 7)) << 4))
+                                     : dummy;
+            stsm_x4(dst, v);
+          }
+          fence_proxy_async();   // generic stores -> visible to the tensor-core reads
+          tp_bar();
+          if (tt == 0) mbar_arrive(&full[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok && tt == 0) mbar_arrive(&rempty[r]);   // every read of this raw box is done
+      }
     }
   } else {
     // ---------------------------------------------------------- epilogue
@@ -481,24 +633,25 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 // through TMA stores), bias, barriers, and the slack for aligning the dynamic
 // base to 1024 bytes.
 constexpr size_t fixed_smem(int BN, bool staging) {
-  return (staging ? static_cast<size_t>(kBM) * BN * 2 : 0) + BN * 4 + (2 * kMaxStages + 5) * 8 +
+  return (staging ? static_cast<size_t>(kBM) * BN * 2 : 0) + BN * 4 + 16 + (2 * kMaxStages + 9) * 8 +
          8 + 1024;
 }
 constexpr size_t kSmemBudget = 232448;  // sm_100 opt-in maximum per CTA
 
-template <typename T, int BN, int MT, int KB>
+template <typename T, int BN, int MT, int KB, bool FUSE = false>
 int launch_conv(const CUtensorMap& tmx, const CUtensorMap& tmw, const CUtensorMap& tmy,
                 const ConvParams& prm, bool staging, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(prm.stages) * prm.stage_bytes + fixed_smem(BN, staging);
+  const size_t smem = static_cast<size_t>(prm.stages) * prm.stage_bytes + fixed_smem(BN, staging) +
+                      (FUSE ? 2 * static_cast<size_t>(prm.raw_bytes) : 0);
   if (smem > kSmemBudget) return fail_unsupported("conv3d stage geometry exceeds shared memory");
   if (prm.out_tma && !staging) return fail_arg("conv3d TMA output without staging");
-  auto kern = conv3d_tc_kernel<T, BN, MT, KB>;
+  auto kern = conv3d_tc_kernel<T, BN, MT, KB, FUSE>;
   B200_CUDA_CHECK(
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int grid = std::min(prm.num_tiles, sm_count());
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kConvThreads);
+  cfg.blockDim = dim3(FUSE ? kConvThreadsFused : kConvThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -540,23 +693,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   auto encode = get_encode_fn();
   if (!encode) return fail_unsupported("cuTensorMapEncodeTiled unavailable");
 
-  const void* xcl = x;
-  if (!x_cl) {
-    const size_t need = static_cast<size_t>(N * D * H * W * Cin) * sizeof(T);
-    if (ws == nullptr || ws_bytes < need) return fail_arg("conv3d workspace too small");
-    const int64_t S = D * H * W;
-    dim3 grid(static_cast<unsigned>((S + 63) / 64), static_cast<unsigned>((Cin + 63) / 64),
-              static_cast<unsigned>(N));
-    if ((S + 63) / 64 > 0x7fffffffLL || (Cin + 63) / 64 > 65535)
-      return fail_unsupported("transpose grid too large");
-    if (aligned16(x) && aligned16(ws))
-      to_cl16_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
-    else
-      to_cl_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
-    B200_LAUNCH_CHECK("to_cl_kernel");
-    xcl = ws;
-  }
-  if (!aligned16(xcl) || !aligned16(wp)) return fail_unsupported("operands not 16-byte aligned");
+  if (!aligned16(wp)) return fail_unsupported("operands not 16-byte aligned");
 
   const int BN = pick_bn(Cout, variant & 0xF);
   int BW;
@@ -645,6 +782,59 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     if (!planned) planned = plan(1, &g);
   }
   if (!planned) return fail_unsupported("conv3d tile does not fit in shared memory");
+
+  // NCDHW input: by default transpose into the workspace first (a separate
+  // bandwidth-bound kernel).  Variant bit 14 instead fuses the transposition
+  // into the conv kernel (one M tile, kh-grouped, two raw boxes in shared
+  // memory) when TMA can address x (16-byte aligned, rows of W elements a
+  // multiple of 16 bytes).  Measured on the cfg2 shape the fused kernel is
+  // slower (21 us vs 13 us for transpose + conv): the raw boxes leave room
+  // for only two pipeline stages.  It stays selectable for other shapes.
+  bool fuse = false;
+  int raw_w = 0, raw_tx = 0, raw_bytes = 0, wpad8 = 0;
+  if (!x_cl && ((variant >> 14) & 1) == 1 && aligned16(x) && (W % 8) == 0 && g.mt == 1 &&
+      kgmode != 1) {
+    wpad8 = static_cast<int>((pw + 7) / 8 * 8);
+    const int64_t rw = ((wpad8 - pw) + BW + (KW - 1) * dw + 7) / 8 * 8;
+    const int64_t rows = BH + (KH - 1) * dh;
+    if (rw <= 256 && rows <= 256) {
+      raw_w = static_cast<int>(rw);
+      raw_tx = static_cast<int>(kBK * rows * rw * 2);
+      raw_bytes = (raw_tx + 1023) / 1024 * 1024;
+      Geo f;
+      f.mt = 1;
+      f.kb = kBK;
+      f.khg = static_cast<int>(KH);
+      f.a_bytes = static_cast<int>(rows * BW * kBK * 2);
+      f.stage_bytes = f.a_bytes + f.khg * BN * kBK * 2;
+      for (int pass = 0; pass < 2 && !fuse; ++pass) {
+        f.staging = tma_out_ok && pass == 0;
+        if (pass == 0 && !tma_out_ok) continue;
+        const size_t fixed = fixed_smem(BN, f.staging) + 2 * static_cast<size_t>(raw_bytes);
+        if (fixed >= kSmemBudget) continue;
+        f.stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemBudget - fixed) / f.stage_bytes));
+        if (f.stages >= 2) fuse = true;
+      }
+      if (fuse) g = f;
+    }
+  }
+  const void* xcl = x;
+  if (!x_cl && !fuse) {
+    const size_t need = static_cast<size_t>(N * D * H * W * Cin) * sizeof(T);
+    if (ws == nullptr || ws_bytes < need) return fail_arg("conv3d workspace too small");
+    const int64_t S = D * H * W;
+    dim3 grid(static_cast<unsigned>((S + 63) / 64), static_cast<unsigned>((Cin + 63) / 64),
+              static_cast<unsigned>(N));
+    if ((S + 63) / 64 > 0x7fffffffLL || (Cin + 63) / 64 > 65535)
+      return fail_unsupported("transpose grid too large");
+    if (aligned16(x) && aligned16(ws))
+      to_cl16_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
+    else
+      to_cl_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
+    B200_LAUNCH_CHECK("to_cl_kernel");
+    xcl = ws;
+  }
+  if (!aligned16(xcl)) return fail_unsupported("operands not 16-byte aligned");
   const int khg = g.khg, stages = g.stages, a_bytes = g.a_bytes, stage_bytes = g.stage_bytes;
   const int KB = g.kb, MT = g.mt;
   const int a_rows_h = MT * BH + (khg - 1) * static_cast<int>(dh);
@@ -653,7 +843,18 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   const CUtensorMapSwizzle swz = KB == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUtensorMapDataType dt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  {
+  if (fuse) {
+    // NCDHW: dims (W, H, D, C, N); one raw box {raw_w, rows, 1, 64, 1}, no swizzle.
+    cuuint64_t dims[5] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)Cin, (cuuint64_t)N};
+    cuuint64_t strides[4] = {(cuuint64_t)(W * 2), (cuuint64_t)(H * W * 2),
+                             (cuuint64_t)(D * H * W * 2), (cuuint64_t)(Cin * D * H * W * 2)};
+    cuuint32_t box[5] = {(cuuint32_t)raw_w, (cuuint32_t)a_rows_h, 1, (cuuint32_t)kBK, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = encode(&tmx, dt, 5, const_cast<void*>(xcl), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail_unsupported("NCDHW input tensor map rejected");
+  } else {
     cuuint64_t dims[5] = {(cuuint64_t)Cin, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)N};
     cuuint64_t strides[4] = {(cuuint64_t)(Cin * 2), (cuuint64_t)(W * Cin * 2),
                              (cuuint64_t)(H * W * Cin * 2), (cuuint64_t)(D * H * W * Cin * 2)};
@@ -711,6 +912,12 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   prm.bias_dt = bias_dt;
   prm.y_cl = y_cl;
   prm.flags = device_flags_ptr();
+  prm.raw_w = raw_w;
+  prm.raw_bytes = raw_bytes;
+  prm.raw_tx = raw_tx;
+  prm.wpad8 = wpad8;
+  prm.lbw = 0;
+  while ((1 << prm.lbw) < BW) ++prm.lbw;
 
   // NCDHW output through one TMA store per tile when TMA can address it:
   // 16-byte aligned base, rows of Wo elements a multiple of 16 bytes.  The
@@ -731,6 +938,11 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     prm.out_tma = (r == CUDA_SUCCESS) ? 1 : 0;
   }
   const bool stg = g.staging;
+  if (fuse) {
+    if (BN == 64) return launch_conv<T, 64, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
+    if (BN == 128) return launch_conv<T, 128, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
+    return launch_conv<T, 256, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
+  }
   if (MT == 1) {
     if (BN == 64) return launch_conv<T, 64, 1, 64>(tmx, tmw, tmy, prm, stg, stream);
     if (BN == 128) return launch_conv<T, 128, 1, 64>(tmx, tmw, tmy, prm, stg, stream);
