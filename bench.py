@@ -196,7 +196,7 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
     """Device-timed us/op, roofline fraction and rel-L2 for BASELINE configs
     1, 3, 4a, 4b (`only` selects one; `small` shrinks cfg 4b to 64 channels
     for profiler captures)."""
-    from amd_tuned_torch import ops
+    from amd_tuned_torch import fftconv_ops, ops
     out = {}
     stream = torch.cuda.current_stream(dev)
     hbm = peaks["hbm_gbs"]
@@ -287,7 +287,6 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
 
     if only in (None, "cfg4b"):
         # cfg4b: long-filter depthwise conv1d fp16 [16,1024,16384] k2048 p1024 (FFT route)
-        from amd_tuned_torch import fftconv_ops
         g = torch.Generator().manual_seed(44)
         C4 = 64 if small else 1024
         x = torch.randn(16, C4, 16384, generator=g).half()
@@ -319,14 +318,19 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         wd, bd = w.to(dev), b.to(dev)
         y = fftconv_ops.fft_conv3d(xs[0], wd, bd, padding=7)
         if y is not None:
+            # parity on a slice: batch 0, output channels {0, 31, 63}, output depth 8
+            cs = [0, 31, 63]
+            ref = torch.nn.functional.conv3d(x[:1, :, 1:16].float(), w[cs].float(), b[cs].float(),
+                                             padding=(0, 7, 7))[:, :, 0]
+            err = _rel_l2(y[:1, cs, 8].float().cpu(), ref)
             ms = _events_time(lambda i: fftconv_ops.fft_conv3d(xs[i % 4], wd, bd, padding=7), 10,
                               stream)
             byt = 61202560
             out["cfg4a_fftconv3d_fp16"] = {
                 "us_per_op": ms * 1e3, "bound": "hbm (compulsory I/O)",
                 "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
-                "effective_tflops": 3.624e12 / (ms * 1e-3) / 1e12,
-                "note": "weight spectrum cached (3.2 GB fp32) and streamed once per call"}
+                "effective_tflops": 3.624e12 / (ms * 1e-3) / 1e12, "rel_l2_slice": err,
+                "note": "weight spectrum cached (1.6 GB complex fp16) and streamed once per call"}
         del xs, y
         torch.cuda.empty_cache()
     return out

@@ -148,8 +148,9 @@ int b200_to_channels_last(const void* x, void* y, int dtype, int64_t N, int64_t 
  * zero-padded transform of length nfft, nfft >= L + 2*pad, nfft in
  * 2^a 3^b 5^c).  Replaces fftconv_ops.fftconv1d_candidate -> fft_conv
  * (amd_tuned_torch/fftconv_ops.py:889-942, :603-746) for groups == C.
- * b200_fftconv1d_prepare: w [C, K] -> spectrum [C, nfft/2 + 1] complex fp32
- *   (conjugated, i.e. ready to multiply).  b200_fftconv1d_fwd consumes it. */
+ * b200_fftconv1d_prepare: w [C, K] -> spectrum [C, nfft] complex fp32 in the
+ *   transform's digit-reversed position order (conjugated, i.e. ready to
+ *   multiply).  b200_fftconv1d_fwd consumes it. */
 int b200_fft_supported_length(int64_t n);
 size_t b200_fftconv1d_spectrum_bytes(int64_t C, int64_t nfft);
 int b200_fftconv1d_prepare(const void* w, void* spectrum, int w_dtype, int64_t C, int64_t K,
@@ -163,12 +164,17 @@ int b200_fftconv1d_fwd(const void* x, const void* spectrum, const void* bias, vo
  * crop, + bias.  Replaces fftconv_ops.fft_conv3d (fftconv_ops.py:749-781)
  * with complex_matmul (:480-543).  Transform extents (fd, fh, fw) are
  * chosen by the caller (fw even).
- * b200_fftconv3d_prepare: w [Cout, Cin, KD, KH, KW] -> conjugated spectrum,
- *   layout [bins][Cout][Cin] complex fp32 with bins = fd*fh*(fw/2+1).
+ * b200_fftconv3d_prepare: w [Cout, Cin, KD, KH, KW] -> conjugated spectrum:
+ *   a 256-byte header (fp32 scale s at offset 0) followed by [bins][Cin][Cout]
+ *   complex values s * conj(W), bins = fd*fh*(fw/2+1), 16-byte aligned.  fp32
+ *   weights: complex fp32, s = 1.  fp16 / bf16 weights: complex fp16 (re, im),
+ *   s the power of two with s * max|w| * KD*KH*KW <= 2^15 (half the bytes the
+ *   contraction streams per call).  b200_fftconv3d_fwd must be called with
+ *   dtype == the w_dtype the spectrum was prepared with.
  * Workspace: input spectrum [bins][N][Cin] + output spectrum [bins][N][Cout]
  *   + a real staging volume. */
 size_t b200_fftconv3d_spectrum_bytes(int64_t Cout, int64_t Cin, int64_t fd, int64_t fh,
-                                     int64_t fw);
+                                     int64_t fw, int w_dtype);
 int b200_fftconv3d_prepare(const void* w, void* spectrum, int w_dtype, int64_t Cout,
                            int64_t Cin, int64_t KD, int64_t KH, int64_t KW, int64_t fd,
                            int64_t fh, int64_t fw, void* workspace, size_t workspace_bytes,

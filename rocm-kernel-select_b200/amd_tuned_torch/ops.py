@@ -350,7 +350,7 @@ def fftconv3d_spectrum(w: torch.Tensor, fsize: Sequence[int]) -> Optional[torch.
     L = _lib.lib()
     Cout, Cin, KD, KH, KW = w.shape
     fd, fh, fw = fsize
-    nbytes = L.b200_fftconv3d_spectrum_bytes(Cout, Cin, fd, fh, fw)
+    nbytes = L.b200_fftconv3d_spectrum_bytes(Cout, Cin, fd, fh, fw, _code(w.dtype))
     spec = torch.empty(nbytes // 4, dtype=torch.float32, device=w.device)
     wsb = L.b200_fftconv3d_workspace_bytes(1, Cin, Cout, fd, fh, fw)
     ws = workspace(w.device, wsb)
@@ -370,6 +370,8 @@ def fftconv3d(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
     Cout, _, KD, KH, KW = w.shape
     fd, fh, fw = fsize
     if not all(L_.b200_fft_supported_length(n) for n in fsize):
+        return None
+    if w.dtype != x.dtype:   # the spectrum's storage type follows the weight dtype
         return None
     spec = fftconv3d_spectrum(w, fsize)
     if spec is None:

@@ -203,14 +203,40 @@ depth_fwd_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, in
 
 // --------------------------------------------------------------- K3 -----
 // U[f][p][co] = sum_ci Z[f][p][ci] H[hb][ci][co], and the partner -f with
-// conj(H).  One warp per stored bin, lanes over output channels.
+// conj(H).  One warp per stored bin; lane l owns output channels 2l, 2l + 1
+// of each 64-channel block, whose two fp16-complex weights are one 8-byte
+// load.  The input-channel loop runs in steps of 8 with every load of a step
+// issued first.  H is stored scaled by `hscale` (a power of two, see the
+// spectrum header); the sums are scaled back before they are written.
+constexpr int kCi = 8;
+
+__device__ __forceinline__ void cmac(float2& acc, float2 z, float2 h) {
+  acc.x = fmaf(z.x, h.x, fmaf(-z.y, h.y, acc.x));
+  acc.y = fmaf(z.x, h.y, fmaf(z.y, h.x, acc.y));
+}
+__device__ __forceinline__ void cmac_conj(float2& acc, float2 z, float2 h) {   // z * conj(h)
+  acc.x = fmaf(z.x, h.x, fmaf(z.y, h.y, acc.x));
+  acc.y = fmaf(z.y, h.x, fmaf(-z.x, h.y, acc.y));
+}
+
+// Spectrum element: complex fp32 (float2) for fp32 weights, complex fp16
+// (__half2, scaled by the header value) for fp16 / bf16 weights.
+__device__ __forceinline__ float2 spec_f2(float2 v) { return v; }
+__device__ __forceinline__ float2 spec_f2(__half2 v) { return __half22float2(v); }
+__device__ __forceinline__ void spec_zero(float2& v) { v = make_float2(0.f, 0.f); }
+__device__ __forceinline__ void spec_zero(__half2& v) { v = __floats2half2_rn(0.f, 0.f); }
+__device__ __forceinline__ void spec_put(float2* o, float a, float b) { *o = make_float2(a, b); }
+__device__ __forceinline__ void spec_put(__half2* o, float a, float b) { *o = __floats2half2_rn(a, b); }
+
+template <typename S>
 __global__ void __launch_bounds__(kThreads)
-contract_kernel(const float2* __restrict__ Z, const float2* __restrict__ Hs,
-                float2* __restrict__ U, int P, int Cin, int Cout, int Fd, int Fh, int Fw,
-                int64_t hbins) {
+contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
+                const float* __restrict__ hdr, float2* __restrict__ U, int P, int Cin, int Cout,
+                int Fd, int Fh, int Fw, int64_t hbins) {
   const int lane = threadIdx.x & 31;
   const int64_t hb = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   if (hb >= hbins) return;
+  const float inv = 1.0f / __ldg(hdr);
   const int Fw2 = Fw / 2 + 1;
   const int fw = static_cast<int>(hb % Fw2);
   const int fh = static_cast<int>((hb / Fw2) % Fh);
@@ -218,35 +244,74 @@ contract_kernel(const float2* __restrict__ Z, const float2* __restrict__ Hs,
   const int64_t f = (static_cast<int64_t>(fd) * Fh + fh) * Fw + fw;
   const bool neg = fw > 0 && 2 * fw != Fw;
   const int64_t fn = (static_cast<int64_t>((Fd - fd) % Fd) * Fh + (Fh - fh) % Fh) * Fw + (Fw - fw);
-  const float2* h = Hs + hb * Cin * Cout;
+  const S* h = Hs + hb * Cin * Cout;
+  // Half-warp `par` takes input channels of parity par; lane q of a half owns
+  // output channels 4q .. 4q + 3 of each 64-channel block (one 16-byte load
+  // of fp16 complex, two of fp32 complex).  The halves are added at the end.
+  const int par = lane >> 4, q = lane & 15;
+  constexpr int kPer = 16 / static_cast<int>(sizeof(S));   // values per 16-byte load
+  const bool vec = (Cout % 4) == 0;
   for (int p = 0; p < P; ++p) {
     const float2* zf = Z + (f * P + p) * Cin;
     const float2* zn = Z + (fn * P + p) * Cin;
     for (int co0 = 0; co0 < Cout; co0 += 64) {
-      const int c0 = co0 + lane, c1 = co0 + 32 + lane;
-      float2 a0 = make_float2(0.f, 0.f), a1 = a0, b0 = a0, b1 = a0;
-      for (int ci = 0; ci < Cin; ++ci) {
-        const float2 z = __ldg(zf + ci);
-        const float2 zz = neg ? __ldg(zn + ci) : make_float2(0.f, 0.f);
-        const float2 h0 = c0 < Cout ? __ldg(h + static_cast<int64_t>(ci) * Cout + c0) : z;
-        const float2 h1 = c1 < Cout ? __ldg(h + static_cast<int64_t>(ci) * Cout + c1) : z;
-        a0.x = fmaf(z.x, h0.x, fmaf(-z.y, h0.y, a0.x));
-        a0.y = fmaf(z.x, h0.y, fmaf(z.y, h0.x, a0.y));
-        a1.x = fmaf(z.x, h1.x, fmaf(-z.y, h1.y, a1.x));
-        a1.y = fmaf(z.x, h1.y, fmaf(z.y, h1.x, a1.y));
-        // zz * conj(h)
-        b0.x = fmaf(zz.x, h0.x, fmaf(zz.y, h0.y, b0.x));
-        b0.y = fmaf(zz.y, h0.x, fmaf(-zz.x, h0.y, b0.y));
-        b1.x = fmaf(zz.x, h1.x, fmaf(zz.y, h1.y, b1.x));
-        b1.y = fmaf(zz.y, h1.x, fmaf(-zz.x, h1.y, b1.y));
+      const int c0 = co0 + 4 * q;
+      float2 a[4], bsum[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) a[j] = bsum[j] = make_float2(0.f, 0.f);
+      for (int ci0 = 0; ci0 < Cin; ci0 += 2 * kCi) {
+        float2 z[kCi], zz[kCi];
+        S hv[kCi][4];
+#pragma unroll
+        for (int k = 0; k < kCi; ++k) {
+          const int ci = ci0 + 2 * k + par;
+          const bool in = ci < Cin;
+          z[k] = in ? __ldg(zf + ci) : make_float2(0.f, 0.f);
+          zz[k] = (in && neg) ? __ldg(zn + ci) : make_float2(0.f, 0.f);
+          const S* hr = h + static_cast<int64_t>(in ? ci : 0) * Cout + c0;
+          if (in && vec && c0 + 3 < Cout) {
+#pragma unroll
+            for (int v = 0; v < 4; v += kPer) {
+              const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(hr + v));
+              const S* e = reinterpret_cast<const S*>(&w4);
+#pragma unroll
+              for (int u = 0; u < kPer; ++u) hv[k][v + u] = e[u];
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (in && c0 + j < Cout) hv[k][j] = __ldg(hr + j);
+              else spec_zero(hv[k][j]);
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kCi; ++k) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 g = spec_f2(hv[k][j]);
+            cmac(a[j], z[k], g);
+            cmac_conj(bsum[j], zz[k], g);
+          }
+        }
       }
-      float2* uf = U + (f * P + p) * Cout;
-      float2* un = U + (fn * P + p) * Cout;
-      if (c0 < Cout) uf[c0] = a0;
-      if (c1 < Cout) uf[c1] = a1;
-      if (neg) {
-        if (c0 < Cout) un[c0] = b0;
-        if (c1 < Cout) un[c1] = b1;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        a[j].x += __shfl_xor_sync(0xffffffffu, a[j].x, 16);
+        a[j].y += __shfl_xor_sync(0xffffffffu, a[j].y, 16);
+        bsum[j].x += __shfl_xor_sync(0xffffffffu, bsum[j].x, 16);
+        bsum[j].y += __shfl_xor_sync(0xffffffffu, bsum[j].y, 16);
+      }
+      if (par == 0) {
+        float2* uf = U + (f * P + p) * Cout;
+        float2* un = U + (fn * P + p) * Cout;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (c0 + j < Cout) {
+            uf[c0 + j] = make_float2(a[j].x * inv, a[j].y * inv);
+            if (neg) un[c0 + j] = make_float2(bsum[j].x * inv, bsum[j].y * inv);
+          }
+        }
       }
     }
   }
@@ -331,8 +396,10 @@ plane_inv_kernel(const float2* __restrict__ G2, T* __restrict__ y, const void* _
 // Weight spectrum: Zw[bin][0][ci] packs output channels (co0, co0 + 1) as
 // real/imag; split them by Hermitian symmetry and store the conjugates for
 // the stored half (fw <= Fw/2) as Hs[hb][ci][co].
-__global__ void separate_kernel(const float2* __restrict__ Zw, float2* __restrict__ Hs, int Cin,
-                                int Cout, int co0, int Fd, int Fh, int Fw, int64_t hbins) {
+template <typename S>
+__global__ void separate_kernel(const float2* __restrict__ Zw, S* __restrict__ Hs,
+                                const float* __restrict__ hdr, int Cin, int Cout, int co0, int Fd,
+                                int Fh, int Fw, int64_t hbins) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= hbins * Cin) return;
   const int ci = static_cast<int>(idx % Cin);
@@ -348,9 +415,39 @@ __global__ void separate_kernel(const float2* __restrict__ Zw, float2* __restric
   // A = (a + conj(b)) / 2, B = (a - conj(b)) / (2i); store conj(A), conj(B).
   const float2 A = make_float2(0.5f * (a.x + b.x), 0.5f * (a.y - b.y));
   const float2 Bv = make_float2(0.5f * (a.y + b.y), 0.5f * (b.x - a.x));
-  float2* out = Hs + (hb * Cin + ci) * Cout;
-  out[co0] = make_float2(A.x, -A.y);
-  if (co0 + 1 < Cout) out[co0 + 1] = make_float2(Bv.x, -Bv.y);
+  const float sc = __ldg(hdr);
+  S* out = Hs + (hb * Cin + ci) * Cout;
+  spec_put(out + co0, A.x * sc, -A.y * sc);
+  if (co0 + 1 < Cout) spec_put(out + co0 + 1, Bv.x * sc, -Bv.y * sc);
+}
+
+// Spectrum scale: the largest power of two s with s * max|w| * taps <= 2^15,
+// so every stored |H| (at most sum |w| <= max|w| * taps) stays inside fp16
+// and the typical values keep full fp16 precision.  One CTA; the weight is
+// small (read once per weight).
+template <typename T>
+__global__ void __launch_bounds__(256)
+spectrum_scale_kernel(const T* __restrict__ w, int64_t n, int64_t taps, int unit,
+                      float* __restrict__ hdr) {
+  __shared__ float red[32];
+  float m = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += 256) m = fmaxf(m, fabsf(to_f32(w[i])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = 0.f;
+    for (int k = 0; k < 8; ++k) mm = fmaxf(mm, red[k]);
+    const float bound = mm * static_cast<float>(taps);
+    int e = 0;
+    if (bound > 0.f && isfinite(bound)) {
+      frexpf(32768.0f / bound, &e);   // 32768 / bound = f * 2^e, f in [0.5, 1)
+      e -= 1;                          // 2^e <= 32768 / bound
+    }
+    e = e > 60 ? 60 : (e < -60 ? -60 : e);
+    hdr[0] = unit ? 1.0f : ldexpf(1.0f, e);
+  }
 }
 
 // ------------------------------------------------------------ host ------
@@ -414,8 +511,15 @@ int forward_volume(const T* x, float2* G, float2* Z, int64_t n_items, int64_t it
   return B200_OK;
 }
 
+// Spectrum buffer: a 256-byte header (float scale at offset 0) followed by
+// Hs[hbin][Cin][Cout]: complex fp32 for fp32 weights (scale 1), complex fp16
+// scaled by the header value for fp16 / bf16 weights.
+constexpr size_t kSpecHeader = 256;
 template <typename T>
-int prepare_typed(const void* wv, float2* Hs, int64_t Cout, int64_t Cin, int64_t KD, int64_t KH,
+using SpecT = typename std::conditional<std::is_same<T, float>::value, float2, __half2>::type;
+
+template <typename T>
+int prepare_typed(const void* wv, void* spec, int64_t Cout, int64_t Cin, int64_t KD, int64_t KH,
                   int64_t KW, const Plan3& pl, void* ws, size_t ws_bytes, cudaStream_t s) {
   const Sizes sz = sizes(1, Cin, Cout, pl.d.n, pl.h.n, pl.w.n);
   const size_t need = align256(sz.g_bytes) + align256(sz.z_bytes);
@@ -423,12 +527,17 @@ int prepare_typed(const void* wv, float2* Hs, int64_t Cout, int64_t Cin, int64_t
   float2* G = static_cast<float2*>(ws);
   float2* Zw = reinterpret_cast<float2*>(static_cast<char*>(ws) + align256(sz.g_bytes));
   const T* w = static_cast<const T*>(wv);
+  float* hdr = static_cast<float*>(spec);
+  SpecT<T>* Hs = reinterpret_cast<SpecT<T>*>(static_cast<char*>(spec) + kSpecHeader);
+  spectrum_scale_kernel<T><<<1, 256, 0, s>>>(w, Cout * Cin * KD * KH * KW, KD * KH * KW,
+                                             std::is_same<T, float>::value ? 1 : 0, hdr);
+  B200_LAUNCH_CHECK("spectrum_scale_kernel");
   for (int64_t co0 = 0; co0 < Cout; co0 += 2) {
     int rc = forward_volume<T>(w, G, Zw, Cout, co0, 1, (int)Cin, (int)KD, (int)KH, (int)KW, 0, 0,
                                0, pl, s);
     if (rc != B200_OK) return rc;
     const int64_t n = sz.hbins * Cin;
-    separate_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(Zw, Hs, (int)Cin, (int)Cout,
+    separate_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(Zw, Hs, hdr, (int)Cin, (int)Cout,
                                                                 (int)co0, pl.d.n, pl.h.n,
                                                                 pl.w.n, sz.hbins);
     B200_LAUNCH_CHECK("separate_kernel");
@@ -437,7 +546,7 @@ int prepare_typed(const void* wv, float2* Hs, int64_t Cout, int64_t Cin, int64_t
 }
 
 template <typename T>
-int fwd_typed(const void* xv, const float2* Hs, const void* bias, int bias_dt, void* yv,
+int fwd_typed(const void* xv, const void* spec, const void* bias, int bias_dt, void* yv,
               int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int64_t Cout, int64_t Do,
               int64_t Ho, int64_t Wo, const int64_t* pad3, const Plan3& pl, void* ws,
               size_t ws_bytes, cudaStream_t s) {
@@ -451,8 +560,11 @@ int fwd_typed(const void* xv, const float2* Hs, const void* bias, int bias_dt, v
                              (int)H, (int)W, (int)pad3[0], (int)pad3[1], (int)pad3[2], pl, s);
   if (rc != B200_OK) return rc;
   const int64_t warps = sz.hbins;
-  contract_kernel<<<(unsigned)((warps * 32 + kThreads - 1) / kThreads), kThreads, 0, s>>>(
-      Z, Hs, U, (int)sz.P, (int)Cin, (int)Cout, pl.d.n, pl.h.n, pl.w.n, sz.hbins);
+  const float* hdr = static_cast<const float*>(spec);
+  const SpecT<T>* Hs =
+      reinterpret_cast<const SpecT<T>*>(static_cast<const char*>(spec) + kSpecHeader);
+  contract_kernel<SpecT<T>><<<(unsigned)((warps * 32 + kThreads - 1) / kThreads), kThreads, 0, s>>>(
+      Z, Hs, hdr, U, (int)sz.P, (int)Cin, (int)Cout, pl.d.n, pl.h.n, pl.w.n, sz.hbins);
   B200_LAUNCH_CHECK("contract_kernel");
   const size_t ds = depth_smem(pl, (int)Cout), ps = plane_smem(pl);
   if ((rc = set_smem(depth_inv_kernel, ds)) != B200_OK) return rc;
@@ -480,8 +592,9 @@ using namespace b200;
 extern "C" {
 
 size_t b200_fftconv3d_spectrum_bytes(int64_t Cout, int64_t Cin, int64_t fd, int64_t fh,
-                                     int64_t fw) {
-  return static_cast<size_t>(Cout * Cin * fd * fh * (fw / 2 + 1)) * sizeof(float2);
+                                     int64_t fw, int w_dtype) {
+  const size_t elem = w_dtype == B200_DTYPE_F32 ? sizeof(float2) : sizeof(__half2);
+  return kSpecHeader + static_cast<size_t>(Cout * Cin * fd * fh * (fw / 2 + 1)) * elem;
 }
 
 size_t b200_fftconv3d_workspace_bytes(int64_t N, int64_t Cin, int64_t Cout, int64_t fd,
@@ -502,12 +615,14 @@ int b200_fftconv3d_prepare(const void* w, void* spectrum, int w_dtype, int64_t C
   if (!plan3(fd, fh, fw, &pl)) return fail_unsupported("transform extents unsupported");
   if (Cin > 4096 || Cout > 65535) return fail_unsupported("too many channels");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  float2* H = static_cast<float2*>(spectrum);
+  if (!aligned16(spectrum)) return fail_arg("spectrum must be 16-byte aligned");
   if (w_dtype == B200_DTYPE_F32)
-    return prepare_typed<float>(w, H, Cout, Cin, KD, KH, KW, pl, workspace, workspace_bytes, s);
+    return prepare_typed<float>(w, spectrum, Cout, Cin, KD, KH, KW, pl, workspace,
+                                workspace_bytes, s);
   if (w_dtype == B200_DTYPE_F16)
-    return prepare_typed<__half>(w, H, Cout, Cin, KD, KH, KW, pl, workspace, workspace_bytes, s);
-  return prepare_typed<__nv_bfloat16>(w, H, Cout, Cin, KD, KH, KW, pl, workspace,
+    return prepare_typed<__half>(w, spectrum, Cout, Cin, KD, KH, KW, pl, workspace,
+                                 workspace_bytes, s);
+  return prepare_typed<__nv_bfloat16>(w, spectrum, Cout, Cin, KD, KH, KW, pl, workspace,
                                       workspace_bytes, s);
 }
 
@@ -528,7 +643,8 @@ int b200_fftconv3d_fwd(const void* x, const void* spectrum, const void* bias, vo
   if (!plan3(fd, fh, fw, &pl)) return fail_unsupported("transform extents unsupported");
   if (Cin > 4096 || Cout > 4096) return fail_unsupported("too many channels");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const float2* Hs = static_cast<const float2*>(spectrum);
+  if (!aligned16(spectrum)) return fail_arg("spectrum must be 16-byte aligned");
+  const void* Hs = spectrum;
   if (dtype == B200_DTYPE_F32)
     return fwd_typed<float>(x, Hs, bias, bias_dtype, y, N, Cin, D, H, W, Cout, Do, Ho, Wo, pad3,
                             pl, workspace, workspace_bytes, s);
