@@ -23,6 +23,7 @@ namespace {
 
 constexpr int kDwThreads = 256;
 constexpr int kDwTile = 2048;
+constexpr int kDwSubTiles = 2;   // register kernel: 16-byte vectors per thread
 
 template <typename T, int KS>
 __global__ void __launch_bounds__(kDwThreads)
@@ -112,17 +113,15 @@ dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
                     int64_t L, int64_t Lout, int64_t tiles_per_row) {
   static_assert(P <= Vec16<T>::N && K - 1 - P <= Vec16<T>::N, "halo wider than one vector");
   constexpr int V = Vec16<T>::N;
-  constexpr int kTileOut = kDwThreads * V;
+  constexpr int kSub = kDwThreads * V;           // outputs of one sub-tile
+  constexpr int kTileOut = kSub * kDwSubTiles;   // a CTA covers kDwSubTiles sub-tiles
   const int64_t row = blockIdx.x / tiles_per_row;
   const int64_t tile = blockIdx.x % tiles_per_row;
   const int64_t c = row % C;
   const int lane = threadIdx.x & 31;
-  float wk[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) wk[k] = load_param(w, wdt, c * K + k);
-  const float b = bias ? load_param(bias, wdt, c) : 0.f;
   const T* xr = x + row * L;
-  const int64_t o0 = tile * kTileOut + static_cast<int64_t>(threadIdx.x) * V;
+  T* yr = y + row * Lout;
+  const int64_t base = tile * kTileOut + static_cast<int64_t>(threadIdx.x) * V;
 
   auto load_vec = [&](int64_t p, float (&v)[V]) {
     if (p >= 0 && p + V <= L) {
@@ -132,43 +131,46 @@ dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
       for (int e = 0; e < V; ++e) v[e] = (p + e >= 0 && p + e < L) ? to_f32(xr[p + e]) : 0.f;
     }
   };
-  float cur[V], prev[V], next[V];
-  load_vec(o0, cur);
+  // All sub-tiles' input vectors are requested before any is used.
+  float cur[kDwSubTiles][V];
 #pragma unroll
-  for (int e = 0; e < V; ++e) {
-    prev[e] = __shfl_up_sync(0xffffffffu, cur[e], 1);
-    next[e] = __shfl_down_sync(0xffffffffu, cur[e], 1);
-  }
-  if (lane == 0) load_vec(o0 - V, prev);
-  if (lane == 31) load_vec(o0 + V, next);
+  for (int u = 0; u < kDwSubTiles; ++u) load_vec(base + u * kSub, cur[u]);
+  float wk[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) wk[k] = load_param(w, wdt, c * K + k);
+  const float b = bias ? load_param(bias, wdt, c) : 0.f;
 
-  float out[V];
 #pragma unroll
-  for (int v = 0; v < V; ++v) {
-    float acc = b;
+  for (int u = 0; u < kDwSubTiles; ++u) {
+    const int64_t o0 = base + u * kSub;
+    float prev[V], next[V];
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      // Input position o0 + v - pad + k, relative to the owned vector.
-      const int r = v + k - P;  // in [-P, V - 1 + K - 1 - P]; compile-time after unrolling
-      float xv;
-      if (r < 0) {
-        xv = prev[V + r];
-      } else if (r < V) {
-        xv = cur[r];
-      } else {
-        xv = next[r - V];
-      }
-      acc = fmaf(wk[k], xv, acc);
+    for (int e = 0; e < V; ++e) {
+      prev[e] = __shfl_up_sync(0xffffffffu, cur[u][e], 1);
+      next[e] = __shfl_down_sync(0xffffffffu, cur[u][e], 1);
     }
-    out[v] = acc;
-  }
-  T* yr = y + row * Lout;
-  if (o0 + V <= Lout) {
-    *reinterpret_cast<uint4*>(yr + o0) = pack16<T>(out);
-  } else {
+    if (lane == 0) load_vec(o0 - V, prev);
+    if (lane == 31) load_vec(o0 + V, next);
+    float out[V];
 #pragma unroll
-    for (int e = 0; e < V; ++e)
-      if (o0 + e < Lout) yr[o0 + e] = from_f32<T>(out[e]);
+    for (int v = 0; v < V; ++v) {
+      float acc = b;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        // Input position o0 + v - pad + k, relative to the owned vector.
+        const int r = v + k - P;  // in [-P, V - 1 + K - 1 - P]; compile-time after unrolling
+        const float xv = r < 0 ? prev[V + r] : (r < V ? cur[u][r] : next[r - V]);
+        acc = fmaf(wk[k], xv, acc);
+      }
+      out[v] = acc;
+    }
+    if (o0 + V <= Lout) {
+      *reinterpret_cast<uint4*>(yr + o0) = pack16<T>(out);
+    } else {
+#pragma unroll
+      for (int e = 0; e < V; ++e)
+        if (o0 + e < Lout) yr[o0 + e] = from_f32<T>(out[e]);
+    }
   }
 }
 
@@ -181,7 +183,7 @@ int launch(const void* xv, const void* w, const void* bias, void* yv, int wdt, i
   const bool pad_ok = pad == (K - 1) / 2 || pad == 0 || pad == K - 1;
   if (K <= 9 && pad_ok && pad <= VV && K - 1 - pad <= VV && aligned16(xv) && aligned16(yv) &&
       L % VV == 0 && Lout % VV == 0) {
-    const int64_t tiles = (Lout + kDwThreads * VV - 1) / (kDwThreads * VV);
+    const int64_t tiles = (Lout + kDwThreads * VV * kDwSubTiles - 1) / (kDwThreads * VV * kDwSubTiles);
     const int64_t blocks = B * C * tiles;
     if (blocks <= 0x7fffffffLL) {
       const T* x = static_cast<const T*>(xv);

@@ -417,7 +417,7 @@ gn_l2_stats_kernel(const T* __restrict__ x, float2* __restrict__ part, int64_t M
 // (x is not written by it), so they overlap pass 1's tail.  The channels the
 // chunk spans get their gamma / beta staged in shared memory once.
 template <typename T, bool SILU>
-__global__ void __launch_bounds__(kL2Threads)
+__global__ void __launch_bounds__(kL2Threads, 4)
 gn_l2_apply_kernel(const T* __restrict__ x, const float2* __restrict__ part,
                    const void* __restrict__ gamma, const void* __restrict__ beta,
                    T* __restrict__ y, int affine_dt, int64_t S, int G, int Cg, int64_t M,
