@@ -82,6 +82,14 @@ int b200_gn_fwd_static_scratch(const void* x, const void* gamma, const void* bet
                                int dtype, int affine_dtype, int64_t N, int64_t C, int64_t S,
                                int64_t G, float eps, void* stream);
 
+/* Merges per-rank (count, mean, M2) triples parts [ranks][groups][3] (fp32)
+ * in rank order (Chan et al., fp64) into out [groups][3]: the statistics
+ * exchange of the T-sharded GroupNorm (all-gather of b200_gn_partial_stats,
+ * then this, identical on every rank).  No counterpart in the reference (it
+ * has no sharded GroupNorm). */
+int b200_gn_merge_ranks(const float* parts, float* out, int64_t ranks, int64_t groups,
+                        void* stream);
+
 /* GroupNorm statistics only: per (n, g) mean and rstd (fp32, [N*G] each).
  * Used by the fused GroupNorm->SiLU->conv3d producer and by the T-sharded
  * stack, which merges per-rank partial statistics.  Partial form: writes

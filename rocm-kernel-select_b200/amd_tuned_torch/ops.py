@@ -181,6 +181,19 @@ def group_norm_partial_stats(x: torch.Tensor, num_groups: int) -> torch.Tensor:
     return out
 
 
+def group_norm_merge_ranks(parts: torch.Tensor) -> torch.Tensor:
+    """[R, groups, 3] fp32 per-rank (count, mean, M2) -> [groups, 3], merged in
+    rank order (fp64) on the device."""
+    L = _lib.lib()
+    parts = parts.contiguous()
+    R, groups = parts.shape[0], parts.shape[1]
+    out = torch.empty(groups, 3, dtype=torch.float32, device=parts.device)
+    rc = L.b200_gn_merge_ranks(parts.data_ptr(), out.data_ptr(), R, groups, _stream(parts.device))
+    if not _lib.check(rc, "b200_gn_merge_ranks"):
+        raise _lib.NativeError("b200_gn_merge_ranks declined")
+    return out
+
+
 def group_norm_apply(x: torch.Tensor, stats: torch.Tensor, num_groups: int,
                      weight: Optional[torch.Tensor], bias: Optional[torch.Tensor], eps: float,
                      silu: bool = False, channels_last_out: bool = False) -> torch.Tensor:

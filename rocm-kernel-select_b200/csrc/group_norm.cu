@@ -248,6 +248,29 @@ __global__ void gn_merge_kernel(const float* __restrict__ part, float* __restric
   out[ng * 3 + 2] = static_cast<float>(m2);
 }
 
+// Merges per-rank triples parts[r][g][3] in rank order (fp64) -> out[g][3]:
+// the statistics exchange of a sharded GroupNorm (every rank runs it on the
+// same gathered array and gets identical statistics).  One thread per group.
+__global__ void gn_merge_ranks_kernel(const float* __restrict__ parts, float* __restrict__ out,
+                                      int64_t groups, int ranks) {
+  const int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (g >= groups) return;
+  double n = 0.0, mean = 0.0, m2 = 0.0;
+  for (int r = 0; r < ranks; ++r) {
+    const float* p = parts + (static_cast<int64_t>(r) * groups + g) * 3;
+    const double nb = p[0];
+    if (nb <= 0.0) continue;
+    const double tot = n + nb;
+    const double d = static_cast<double>(p[1]) - mean;
+    mean += d * nb / tot;
+    m2 += static_cast<double>(p[2]) + d * d * n * nb / tot;
+    n = tot;
+  }
+  out[g * 3 + 0] = static_cast<float>(n);
+  out[g * 3 + 1] = static_cast<float>(mean);
+  out[g * 3 + 2] = static_cast<float>(m2);
+}
+
 // ------------------------------------------------------- split: apply ----
 // y = (x - mean) * rstd * gamma + beta, optional SiLU; NC[S] layout out.
 template <typename T, bool VEC, bool SILU>
@@ -518,6 +541,63 @@ gn_l2_apply_kernel(const T* __restrict__ x, const float2* __restrict__ part,
   }
 }
 
+// Same operation with 16-byte I/O (16-bit types, C % 8 == 0, S % 8 == 0,
+// aligned pointers): a tile of 64 channels x 64 positions; each thread loads
+// 8 consecutive positions of one channel, normalises (+SiLU) them, and after
+// a shared-memory transpose stores 8 consecutive channels of one position.
+template <typename T, bool SILU>
+__global__ void __launch_bounds__(256)
+gn_apply_cl16_kernel(const T* __restrict__ x, const float* __restrict__ stats,
+                     const void* __restrict__ gamma, const void* __restrict__ beta,
+                     T* __restrict__ y, int affine_dt, int64_t C, int64_t S, int G, int Cg,
+                     float eps) {
+  static_assert(sizeof(T) == 2, "16-bit elements");
+  __shared__ uint32_t tile[64 * 33];   // 64 channels x 64 positions of 16-bit, rows padded
+  pdl_launch_dependents();             // the consuming conv kernel's prologue may overlap
+  const int64_t n = blockIdx.z;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 64;
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int v = threadIdx.x & 7;
+  for (int r = threadIdx.x >> 3; r < 64; r += 32) {
+    const int64_t c = c0 + r;
+    const int64_t p = p0 + 8 * v;
+    uint4 q = make_uint4(0, 0, 0, 0);
+    if (c < C && p < S) {
+      const int64_t ng = n * G + c / Cg;
+      const float cnt = stats[ng * 3 + 0];
+      const float mean = stats[ng * 3 + 1];
+      const float rstd = 1.0f / sqrtf(stats[ng * 3 + 2] / cnt + eps);
+      const float a = gamma ? rstd * load_param(gamma, affine_dt, c) : rstd;
+      const float b = beta ? load_param(beta, affine_dt, c) : 0.f;
+      float f[8];
+      unpack16<T>(ld_stream16(x + (n * C + c) * S + p), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        f[e] = fmaf(f[e] - mean, a, b);
+        if (SILU) f[e] = silu(f[e]);
+      }
+      q = pack16<T>(f);
+    }
+    uint32_t* row = tile + r * 33 + 4 * v;
+    row[0] = q.x;
+    row[1] = q.y;
+    row[2] = q.z;
+    row[3] = q.w;
+  }
+  __syncthreads();
+  const uint16_t* t16 = reinterpret_cast<const uint16_t*>(tile);
+  for (int qp = threadIdx.x >> 3; qp < 64; qp += 32) {
+    const int64_t p = p0 + qp;
+    if (p >= S || c0 + 8 * v >= C) continue;
+    uint16_t e[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) e[k] = t16[(8 * v + k) * 66 + qp];
+    *reinterpret_cast<uint4*>(y + (n * S + p) * C + c0 + 8 * v) =
+        make_uint4(e[0] | (uint32_t(e[1]) << 16), e[2] | (uint32_t(e[3]) << 16),
+                   e[4] | (uint32_t(e[5]) << 16), e[6] | (uint32_t(e[7]) << 16));
+  }
+}
+
 // ----------------------------------------------------------- host side ---
 struct GnShape {
   int64_t N, C, S, G, Cg, M, groups;
@@ -623,6 +703,21 @@ template <typename T>
 int launch_apply(const T* x, const float* stats, const void* gamma, const void* beta, T* y,
                  int affine_dt, const GnShape& sh, float eps, bool silu, bool to_cl,
                  cudaStream_t stream) {
+  if constexpr (sizeof(T) == 2) {
+    if (to_cl && sh.C % 8 == 0 && sh.S % 8 == 0 && aligned16(x) && aligned16(y) &&
+        (sh.C + 63) / 64 <= 65535 && sh.N <= 65535 && (sh.S + 63) / 64 <= 0x7fffffffLL) {
+      dim3 grid(static_cast<unsigned>((sh.S + 63) / 64), static_cast<unsigned>((sh.C + 63) / 64),
+                static_cast<unsigned>(sh.N));
+      if (silu)
+        gn_apply_cl16_kernel<T, true><<<grid, 256, 0, stream>>>(
+            x, stats, gamma, beta, y, affine_dt, sh.C, sh.S, (int)sh.G, (int)sh.Cg, eps);
+      else
+        gn_apply_cl16_kernel<T, false><<<grid, 256, 0, stream>>>(
+            x, stats, gamma, beta, y, affine_dt, sh.C, sh.S, (int)sh.G, (int)sh.Cg, eps);
+      B200_LAUNCH_CHECK("gn_apply_cl16_kernel");
+      return B200_OK;
+    }
+  }
   if (to_cl) {
     if (sh.S > 0x7fffffffLL * 64 || (sh.C + 31) / 32 > 65535 || sh.N > 65535)
       return fail_unsupported("channels-last apply grid too large");
@@ -821,6 +916,18 @@ int b200_gn_partial_stats(const void* x, float* partial_out, int dtype, int64_t 
                                 workspace_bytes, s);
   return launch_stats<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x), partial_out, sh,
                                      workspace, workspace_bytes, s);
+}
+
+int b200_gn_merge_ranks(const float* parts, float* out, int64_t ranks, int64_t groups,
+                        void* stream) {
+  if (!parts || !out) return fail_arg("parts/out is NULL");
+  if (ranks <= 0 || groups <= 0 || ranks > 0x7fffffffLL) return fail_arg("bad size");
+  const int64_t blocks = (groups + 127) / 128;
+  if (blocks > 0x7fffffffLL) return fail_unsupported("grid too large");
+  gn_merge_ranks_kernel<<<static_cast<unsigned>(blocks), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      parts, out, groups, static_cast<int>(ranks));
+  B200_LAUNCH_CHECK("gn_merge_ranks_kernel");
+  return B200_OK;
 }
 
 int b200_gn_apply(const void* x, const float* stats, const void* gamma, const void* beta,

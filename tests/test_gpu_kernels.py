@@ -58,6 +58,22 @@ def test_group_norm_golden(cuda, case, variant):
     _no_fault()
 
 
+def test_group_norm_merge_ranks_matches_host_merge(cuda):
+    """b200_gn_merge_ranks == the rank-ordered fp64 Chan merge of the stack."""
+    from amd_tuned_torch import ops, video_stack as vs
+    g = torch.Generator().manual_seed(21)
+    R, groups = 3, 40
+    n = torch.randint(0, 5000, (R, groups), generator=g).float()
+    n[1, 7] = 0.0                      # an empty shard
+    mean = torch.randn(R, groups, generator=g) * 3
+    m2 = torch.rand(R, groups, generator=g) * n
+    parts = torch.stack([n, mean, m2], dim=2)
+    got = ops.group_norm_merge_ranks(parts.to(cuda)).cpu().double()
+    ref = vs.merge_stats(parts).double()
+    assert torch.allclose(got, ref, rtol=1e-6, atol=1e-4)
+    _no_fault()
+
+
 @pytest.mark.parametrize("variant", [0, 1, 2, 20, 24, 32])
 def test_group_norm_cfg3_full_size(cuda, variant):
     """BASELINE cfg 3: x[4,512,128,128] ~N(0,2) bf16, G=32, eps=1e-6,
@@ -91,22 +107,26 @@ def test_group_norm_ragged(cuda, shape, G, dt):
         assert oracle.rel_l2(_np(y), ref) <= TOL[dt]
 
 
-def test_group_norm_stats_and_fused_apply(cuda):
+# 16-byte channels-last apply (C, S multiples of 8, partial 64-tiles) and the
+# scalar fallback (C = 36).
+@pytest.mark.parametrize("N,C,sp,G", [(2, 64, (4, 8, 8), 32), (1, 72, (5, 5, 8), 24),
+                                      (1, 36, (3, 3, 3), 12)])
+def test_group_norm_stats_and_fused_apply(cuda, N, C, sp, G):
     """Partial statistics + apply(+SiLU, channels-last) == GroupNorm -> SiLU."""
     from amd_tuned_torch import ops
-    g = torch.Generator().manual_seed(5)
-    x = torch.randn(2, 64, 4, 8, 8, generator=g).to(torch.bfloat16)
-    w = (torch.rand(64, generator=g) + 0.5).to(torch.bfloat16)
-    b = (torch.randn(64, generator=g) * 0.1).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(5 + C)
+    x = torch.randn(N, C, *sp, generator=g).to(torch.bfloat16)
+    w = (torch.rand(C, generator=g) + 0.5).to(torch.bfloat16)
+    b = (torch.randn(C, generator=g) * 0.1).to(torch.bfloat16)
     xd = x.to(cuda)
-    st = ops.group_norm_partial_stats(xd, 32)
-    ref = torch.nn.functional.group_norm(x.float(), 32, w.float(), b.float(), 1e-5)
+    st = ops.group_norm_partial_stats(xd, G)
+    ref = torch.nn.functional.group_norm(x.float(), G, w.float(), b.float(), 1e-5)
     ref = torch.nn.functional.silu(ref)
-    y = ops.group_norm_apply(xd, st, 32, w.to(cuda), b.to(cuda), 1e-5, silu=True)
+    y = ops.group_norm_apply(xd, st, G, w.to(cuda), b.to(cuda), 1e-5, silu=True)
     assert oracle.rel_l2(_np(y), ref.numpy()) <= 2e-3
-    ycl = ops.group_norm_apply(xd, st, 32, w.to(cuda), b.to(cuda), 1e-5, silu=True,
+    ycl = ops.group_norm_apply(xd, st, G, w.to(cuda), b.to(cuda), 1e-5, silu=True,
                                channels_last_out=True)
-    ref_cl = ref.reshape(2, 64, -1).permute(0, 2, 1).numpy()
+    ref_cl = ref.reshape(N, C, -1).permute(0, 2, 1).numpy()
     assert oracle.rel_l2(_np(ycl), ref_cl) <= 2e-3
 
 
