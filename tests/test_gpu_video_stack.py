@@ -42,6 +42,25 @@ def test_stack_small_matches_cpu_chain(cuda):
     assert oracle.rel_l2(_np(yb), rb.numpy()) <= 2e-3
 
 
+def test_stack_graph_replay_matches_eager(cuda):
+    """A captured CUDA-graph step replays to exactly the eager result, also on
+    a changed input copied into the static buffer."""
+    pd = vs.make_params(channels=64, blocks=2, groups=32, dtype=torch.bfloat16, seed=9,
+                        device=cuda)
+    g = torch.Generator().manual_seed(10)
+    x1 = torch.randn(1, 64, 5, 16, 16, generator=g).bfloat16().to(cuda)
+    x2 = torch.randn(1, 64, 5, 16, 16, generator=g).bfloat16().to(cuda)
+    stack = vs.VideoStack(pd)
+    ref1, ref2 = stack.forward(x1).clone(), stack.forward(x2).clone()
+    static = x1.clone()
+    out = stack.capture(static)
+    assert torch.equal(stack.replay(), ref1)
+    static.copy_(x2)
+    assert torch.equal(stack.replay(), ref2)
+    assert out.data_ptr() == stack.replay().data_ptr()
+    stack.release()
+
+
 def test_stack_cfg5_full_size_one_gpu(cuda):
     """BASELINE cfg 5 shape on one GPU: [1,128,64,128,128] bf16, 4 blocks."""
     params = vs.make_params(channels=128, blocks=4, groups=32, dtype=torch.bfloat16, seed=5,
