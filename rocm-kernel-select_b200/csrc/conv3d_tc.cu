@@ -62,9 +62,11 @@ struct ConvParams {
   int y_cl;
   int out_tma;
   int* flags;
-  // Fused NCDHW input (FUSE kernels): one raw box {raw_w, khg rows, 1, 64, 1}
-  // per (kd, channel chunk), starting at column ow0 - wpad8 (a multiple of 8).
-  int raw_w, raw_bytes, raw_tx, wpad8, lbw;
+  // FUSE kernels: one raw box per (kd, channel chunk).  fuse_mode 1: NCDHW
+  // input, box {raw_w, rows, 1, 64, 1} starting at column ow0 - wpad8 (a
+  // multiple of 8).  fuse_mode 2: channels-last input, box {KB, raw_w, rows,
+  // 1, 1} starting at column ow0 - pw (raw_w = BW + (KW - 1) * dw).
+  int fuse_mode, raw_w, raw_bytes, raw_tx, wpad8, lbw;
 };
 
 struct TileCoord {
@@ -92,19 +94,22 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const ConvParams& p, int
 // K-major rows, SWIZZLE_128B) or 32 (64-byte rows, SWIZZLE_64B, half the
 // stage size so that MT = 4 still leaves three stages).
 //
-// FUSE: x is NCDHW.  Instead of a channels-last copy, the producer loads ONE
-// raw box {W span, rows, 1, 64 channels, 1} per (kd, channel chunk) -- its
-// innermost coordinate rounded down to a multiple of 8 elements, the rest
-// of the W span covered by a wider box -- and warps 6-9 write the K-major,
-// 128-byte-swizzled A tile of each kw shift from it into the pipeline stage
-// (generic stores, then a proxy fence before the stage is handed to the
-// MMA warp).  One global read of the input serves all KW shifts.
+// FUSE: the producer loads ONE raw box of the input per (kd, channel chunk)
+// and warps 6-9 write the swizzled K-major A tile of each kw shift from it
+// into the pipeline stage (generic stores, then a proxy fence before the
+// stage is handed to the MMA warp), so one read of the input from L2 serves
+// all KW shifts.  fuse_mode 1 (NCDHW input, MT = 1, KB = 64): the box is
+// {W span rounded to 8, rows, 1, 64 channels, 1} -- its innermost coordinate
+// rounded down to a multiple of 8 elements -- and the warps transpose it
+// with ldmatrix.trans / stmatrix.  fuse_mode 2 (channels-last input, any MT
+// and KB): the box is {KB channels, BW + (KW - 1) * dw columns, rows, 1, 1}
+// in the same swizzle as A, and the warps copy 16-byte chunks from raw row
+// r * raw_w + w + kw * dw to A row r * BW + w, re-swizzled.
 template <typename T, int BN, int MT, int KB, bool FUSE>
 __global__ void __launch_bounds__(FUSE ? kConvThreadsFused : kConvThreads, 1)
 conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                  const __grid_constant__ CUtensorMap tmy, const ConvParams p) {
   static_assert(KB == 64 || KB == 32, "k-block of 32 or 64 channels");
-  static_assert(!FUSE || (MT == 1 && KB == 64), "fused NCDHW input: one M tile, 64-channel k-blocks");
   constexpr int kRow = KB * 2;               // bytes per K-major operand row
   constexpr int kBTap = BN * kRow;           // one tap's weight box
   constexpr int kAcc = MT * BN;              // TMEM columns of one tile's accumulators
@@ -191,8 +196,12 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
         }
         if (lane == 0) {
           mbar_expect_tx(&rfull[r], static_cast<uint32_t>(p.raw_tx));
-          tma_load_5d(sRaw + r * p.raw_bytes, &tmx, &rfull[r], tc.ow0 - p.wpad8, tc.oh0 - p.ph,
-                      tc.od - p.pd + kd * p.dd, cc * KB, tc.n);
+          if (p.fuse_mode == 1)
+            tma_load_5d(sRaw + r * p.raw_bytes, &tmx, &rfull[r], tc.ow0 - p.wpad8, tc.oh0 - p.ph,
+                        tc.od - p.pd + kd * p.dd, cc * KB, tc.n);
+          else
+            tma_load_5d(sRaw + r * p.raw_bytes, &tmx, &rfull[r], cc * KB, tc.ow0 - p.pw,
+                        tc.oh0 - p.ph, tc.od - p.pd + kd * p.dd, tc.n);
         }
         __syncwarp();
         for (int kw = 0; kw < p.KW; ++kw) {
@@ -361,8 +370,8 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
     // scratch slot).  The unaligned kw shift only moves store addresses.
     const int tt = threadIdx.x - 192;
     const int twarp = tt >> 5;
-    const int rows = p.BH + (p.khg - 1) * p.dh;
-    const int plane = rows * p.raw_w;   // elements between two channels of the raw box
+    const int rows = MT * p.BH + (p.khg - 1) * p.dh;
+    const int plane = rows * p.raw_w;   // elements between two channels of the raw box (mode 1)
     const int BWm = p.BW;
     const uint32_t dummy = smem_u32(sBias + BN);   // 16 scratch bytes past the bias (see fixed_smem)
     const int m = lane >> 3, i = lane & 7;      // this lane's matrix and row
@@ -388,6 +397,35 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
             break;
           }
           const uint32_t A = smem_u32(smem + stage * p.stage_bytes);
+          if (p.fuse_mode == 2) {
+            // Shift copy: A row q = r * BW + w <- raw row r * raw_w + w + kw * dw,
+            // chunk c of a kRow-byte row stored at c ^ swz(row) in both.
+            constexpr int kCh = KB / 8;                 // 16-byte chunks per row
+            const int total = (rows << p.lbw) * kCh;
+            for (int idx = tt; idx < total; idx += 128) {
+              const int q = idx / kCh, c = idx % kCh;
+              const int rr = q >> p.lbw, w = q & (BWm - 1);
+              const int src = rr * p.raw_w + w + kw * p.dw;
+              const int sw_s = KB == 64 ? (src & 7) : ((src >> 1) & 3);
+              const int sw_d = KB == 64 ? (q & 7) : ((q >> 1) & 3);
+              uint4 v;
+              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                           : "r"(raw + static_cast<uint32_t>(src * kRow + ((c ^ sw_s) << 4))));
+              asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(
+                               A + static_cast<uint32_t>(q * kRow + ((c ^ sw_d) << 4))),
+                           "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                           : "memory");
+            }
+            fence_proxy_async();
+            tp_bar();
+            if (tt == 0) mbar_arrive(&full[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           const int xs = p.wpad8 - p.pw + kw * p.dw;   // raw column feeding output w = 0
           const int j0 = xs >> 3, j1 = (xs + BWm - 1) >> 3;
           const int nblk = j1 - j0 + 1;
@@ -818,6 +856,40 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
       if (fuse) g = f;
     }
   }
+  int fuse_mode = fuse ? 1 : 0;
+  // Channels-last input, variant bit 15 (opt-in): one raw box {KB, BW +
+  // (KW-1) dw, rows, 1, 1} per (kd, chunk) serves all KW shifts (the copier
+  // warps build each shift's A tile in shared memory), instead of one A box
+  // per (kd, kw): the input crosses L2 -> SM once instead of KW times.
+  // Measured slower on cfg2 (13.9 vs 11.0 us) and on the cfg5 conv (1406 vs
+  // 778 us): the raw boxes cost pipeline stages and the copy adds a hand-off
+  // per k-block, which matter more here than the saved L2 traffic.
+  if (x_cl && ((variant >> 15) & 1) == 1 && g.khg == KH && KW > 1) {
+    const int64_t rw = BW + (KW - 1) * dw;
+    const int64_t rows = static_cast<int64_t>(g.mt) * BH + (KH - 1) * dh;
+    if (rw <= 256 && rows <= 256) {
+      const int tx = static_cast<int>(g.kb * 2 * rw * rows);
+      const int rb = (tx + 1023) / 1024 * 1024;
+      Geo f = g;
+      bool ok = false;
+      for (int pass = 0; pass < 2 && !ok; ++pass) {
+        f.staging = tma_out_ok && pass == 0;
+        if (pass == 0 && !tma_out_ok) continue;
+        const size_t fixed = fixed_smem(BN, f.staging) + 2 * static_cast<size_t>(rb);
+        if (fixed >= kSmemBudget) continue;
+        f.stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemBudget - fixed) / f.stage_bytes));
+        if (f.stages >= (pass == 0 ? 3 : 2)) ok = true;
+      }
+      if (ok) {
+        g = f;
+        fuse = true;
+        fuse_mode = 2;
+        raw_w = static_cast<int>(rw);
+        raw_tx = tx;
+        raw_bytes = rb;
+      }
+    }
+  }
   const void* xcl = x;
   if (!x_cl && !fuse) {
     const size_t need = static_cast<size_t>(N * D * H * W * Cin) * sizeof(T);
@@ -843,7 +915,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   const CUtensorMapSwizzle swz = KB == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUtensorMapDataType dt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  if (fuse) {
+  if (fuse_mode == 1) {
     // NCDHW: dims (W, H, D, C, N); one raw box {raw_w, rows, 1, 64, 1}, no swizzle.
     cuuint64_t dims[5] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)Cin, (cuuint64_t)N};
     cuuint64_t strides[4] = {(cuuint64_t)(W * 2), (cuuint64_t)(H * W * 2),
@@ -858,7 +930,10 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     cuuint64_t dims[5] = {(cuuint64_t)Cin, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)N};
     cuuint64_t strides[4] = {(cuuint64_t)(Cin * 2), (cuuint64_t)(W * Cin * 2),
                              (cuuint64_t)(H * W * Cin * 2), (cuuint64_t)(D * H * W * Cin * 2)};
-    cuuint32_t box[5] = {(cuuint32_t)KB, (cuuint32_t)BW, (cuuint32_t)a_rows_h, 1, 1};
+    // Channels-last: one A box {KB, BW, rows, 1, 1} per (kd, kw), or in fuse
+    // mode 2 one raw box {KB, BW + (KW - 1) dw, rows, 1, 1} per kd.
+    cuuint32_t box[5] = {(cuuint32_t)KB, (cuuint32_t)(fuse_mode == 2 ? raw_w : BW),
+                         (cuuint32_t)a_rows_h, 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = encode(&tmx, dt, 5, const_cast<void*>(xcl), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
@@ -912,6 +987,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   prm.bias_dt = bias_dt;
   prm.y_cl = y_cl;
   prm.flags = device_flags_ptr();
+  prm.fuse_mode = fuse_mode;
   prm.raw_w = raw_w;
   prm.raw_bytes = raw_bytes;
   prm.raw_tx = raw_tx;
@@ -939,9 +1015,17 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   }
   const bool stg = g.staging;
   if (fuse) {
-    if (BN == 64) return launch_conv<T, 64, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
-    if (BN == 128) return launch_conv<T, 128, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
-    return launch_conv<T, 256, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
+    if (MT == 1) {
+      if (BN == 64) return launch_conv<T, 64, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
+      if (BN == 128) return launch_conv<T, 128, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
+      return launch_conv<T, 256, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
+    }
+    if (MT == 2) {
+      if (BN == 64) return launch_conv<T, 64, 2, 32, true>(tmx, tmw, tmy, prm, stg, stream);
+      return launch_conv<T, 128, 2, 32, true>(tmx, tmw, tmy, prm, stg, stream);
+    }
+    if (BN == 64) return launch_conv<T, 64, 4, 32, true>(tmx, tmw, tmy, prm, stg, stream);
+    return launch_conv<T, 128, 4, 32, true>(tmx, tmw, tmy, prm, stg, stream);
   }
   if (MT == 1) {
     if (BN == 64) return launch_conv<T, 64, 1, 64>(tmx, tmw, tmy, prm, stg, stream);
