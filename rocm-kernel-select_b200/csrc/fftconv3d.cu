@@ -49,6 +49,12 @@ __device__ __forceinline__ int dpos(int f, const fft::Plan& p) {
   return pos;
 }
 
+// Digit-reversed position table of a plan (dpos for f = 0 .. n-1) in shared
+// memory; the caller synchronises before use.
+__device__ __forceinline__ void build_pos(int* pos, const fft::Plan& p) {
+  for (int f = threadIdx.x; f < p.n; f += blockDim.x) pos[f] = dpos(f, p);
+}
+
 __device__ __forceinline__ void build_small_tw(float2* tw, int n) {
   for (int t = threadIdx.x; t < n; t += blockDim.x) {
     double s, c;
@@ -57,14 +63,25 @@ __device__ __forceinline__ void build_small_tw(float2* tw, int n) {
   }
 }
 
+// a / d for 0 <= a < 2^24 and 0 < d, from a float reciprocal of d plus one
+// correction step (the float quotient is within 1 of the true one).
+__device__ __forceinline__ int qdiv(int a, int d, float inv_d) {
+  int q = __float2int_rz(__int2float_rz(a) * inv_d);
+  const int r = a - q * d;
+  if (r < 0) --q;
+  else if (r >= d) ++q;
+  return q;
+}
+
 // One pass over nseq sequences; element j of sequence s at buf[s*ss + j*es].
 template <int R, bool INV>
 __device__ __forceinline__ void bpass(float2* buf, int n, int span, int nseq, int ss, int es,
                                       const float2* tw) {
   const int stride = span / R, per = n / R, total = nseq * per, tscale = n / span;
+  const float inv_per = 1.0f / static_cast<float>(per), inv_stride = 1.0f / static_cast<float>(stride);
   for (int b = threadIdx.x; b < total; b += blockDim.x) {
-    const int s = b / per, bb = b - s * per;
-    const int g = bb / stride, k = bb - g * stride;
+    const int s = qdiv(b, per, inv_per), bb = b - s * per;
+    const int g = qdiv(bb, stride, inv_stride), k = bb - g * stride;
     float2* base = buf + s * ss + (g * span + k) * es;
     float2 v[R];
 #pragma unroll
@@ -146,8 +163,9 @@ plane_fwd_kernel(const T* __restrict__ x, float2* __restrict__ G, int64_t n_item
   const T* x1 = x + ((min64(i1, n_items - 1) * C + c) * Dz + dz) * plane;
   build_small_tw(twh, Fh);
   build_small_tw(tww, Fw);
+  const float inv_fw0 = 1.0f / static_cast<float>(Fw);
   for (int idx = threadIdx.x; idx < Fh * Fw; idx += blockDim.x) {
-    const int hh = idx / Fw, ww = idx - hh * Fw;
+    const int hh = qdiv(idx, Fw, inv_fw0), ww = idx - hh * Fw;
     const int h = hh - oh, w = ww - ow;
     const bool in = h >= 0 && h < H && w >= 0 && w < W;
     const float re = in ? to_f32(x0[h * W + w]) : 0.f;
@@ -155,12 +173,17 @@ plane_fwd_kernel(const T* __restrict__ x, float2* __restrict__ G, int64_t n_item
     buf[hh * RS + ww] = make_float2(re, im);
   }
   __syncthreads();
-  bfft<false>(buf, pl.w, Fh, RS, 1, tww);   // rows
+  int* posh = reinterpret_cast<int*>(buf + Fh * RS);
+  int* posw = posh + Fh;
+  build_pos(posh, pl.h);
+  build_pos(posw, pl.w);
+  bfft<false>(buf, pl.w, Fh, RS, 1, tww);   // rows (its barriers also publish posh / posw)
   bfft<false>(buf, pl.h, Fw, 1, RS, twh);   // columns
   float2* g = G + ((p * C + c) * Dz + dz) * static_cast<int64_t>(Fh) * Fw;
+  const float inv_fw = 1.0f / static_cast<float>(Fw);
   for (int idx = threadIdx.x; idx < Fh * Fw; idx += blockDim.x) {
-    const int fh = idx / Fw, fw = idx - fh * Fw;
-    g[idx] = buf[dpos(fh, pl.h) * RS + dpos(fw, pl.w)];
+    const int fh = qdiv(idx, Fw, inv_fw), fw = idx - fh * Fw;
+    g[idx] = buf[posh[fh] * RS + posw[fw]];
   }
 }
 
@@ -178,9 +201,13 @@ depth_fwd_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, in
   const int col0 = (blockIdx.x % tiles) * kCols;
   build_small_tw(twd, Fd);
   const int nseq = C * kCols;
+  int* posd = reinterpret_cast<int*>(buf + nseq * SS);
+  build_pos(posd, pl.d);
+  const int fk = Fd * kCols;
+  const float inv_fk = 1.0f / static_cast<float>(fk);
   for (int idx = threadIdx.x; idx < nseq * Fd; idx += blockDim.x) {
-    const int c = idx / (Fd * kCols);
-    const int r = idx - c * Fd * kCols;
+    const int c = qdiv(idx, fk, inv_fk);
+    const int r = idx - c * fk;
     const int j = r / kCols, q = r - j * kCols;   // q fastest: contiguous columns
     const int d = j - od, col = col0 + q;
     float2 v = make_float2(0.f, 0.f);
@@ -190,14 +217,15 @@ depth_fwd_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, in
   }
   __syncthreads();
   bfft<false>(buf, pl.d, nseq, SS, 1, twd);
+  const float inv_c = 1.0f / static_cast<float>(C);
   for (int idx = threadIdx.x; idx < nseq * Fd; idx += blockDim.x) {
-    const int c = idx % C;                        // c fastest: contiguous output
-    const int r = idx / C;
+    const int r = qdiv(idx, C, inv_c);
+    const int c = idx - r * C;                    // c fastest: contiguous output
     const int q = r % kCols, fd = r / kCols;
     const int col = col0 + q;
     if (col >= cols) continue;
     Z[((static_cast<int64_t>(fd) * cols + col) * P + p) * C + c] =
-        buf[(c * kCols + q) * SS + dpos(fd, pl.d)];
+        buf[(c * kCols + q) * SS + posd[fd]];
   }
 }
 
@@ -331,20 +359,26 @@ depth_inv_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int P, i
   const int col0 = (blockIdx.x % tiles) * kCols;
   build_small_tw(twd, Fd);
   const int nseq = C * kCols;
+  int* posd = reinterpret_cast<int*>(buf + nseq * SS);
+  build_pos(posd, pl.d);
+  __syncthreads();
+  const float inv_c = 1.0f / static_cast<float>(C);
   for (int idx = threadIdx.x; idx < nseq * Fd; idx += blockDim.x) {
-    const int c = idx % C;
-    const int r = idx / C;
+    const int r = qdiv(idx, C, inv_c);
+    const int c = idx - r * C;
     const int q = r % kCols, fd = r / kCols;
     const int col = col0 + q;
     float2 v = make_float2(0.f, 0.f);
     if (col < cols) v = U[((static_cast<int64_t>(fd) * cols + col) * P + p) * C + c];
-    buf[(c * kCols + q) * SS + dpos(fd, pl.d)] = v;
+    buf[(c * kCols + q) * SS + posd[fd]] = v;
   }
   __syncthreads();
   bfft<true>(buf, pl.d, nseq, SS, 1, twd);
+  const int dk = Do * kCols;
+  const float inv_dk = 1.0f / static_cast<float>(dk);
   for (int idx = threadIdx.x; idx < C * Do * kCols; idx += blockDim.x) {
-    const int c = idx / (Do * kCols);
-    const int r = idx - c * Do * kCols;
+    const int c = qdiv(idx, dk, inv_dk);
+    const int r = idx - c * dk;
     const int o = r / kCols, q = r - o * kCols;
     const int col = col0 + q;
     if (col >= cols) continue;
@@ -372,9 +406,15 @@ plane_inv_kernel(const float2* __restrict__ G2, T* __restrict__ y, const void* _
   build_small_tw(twh, Fh);
   build_small_tw(tww, Fw);
   const float2* g = G2 + ((p * C + c) * Do + od) * static_cast<int64_t>(Fh) * Fw;
+  int* posh = reinterpret_cast<int*>(buf + Fh * RS);
+  int* posw = posh + Fh;
+  build_pos(posh, pl.h);
+  build_pos(posw, pl.w);
+  __syncthreads();
+  const float inv_fw = 1.0f / static_cast<float>(Fw);
   for (int idx = threadIdx.x; idx < Fh * Fw; idx += blockDim.x) {
-    const int fh = idx / Fw, fw = idx - fh * Fw;
-    buf[dpos(fh, pl.h) * RS + dpos(fw, pl.w)] = g[idx];
+    const int fh = qdiv(idx, Fw, inv_fw), fw = idx - fh * Fw;
+    buf[posh[fh] * RS + posw[fw]] = g[idx];
   }
   __syncthreads();
   bfft<true>(buf, pl.h, Fw, 1, RS, twh);
@@ -384,8 +424,9 @@ plane_inv_kernel(const float2* __restrict__ G2, T* __restrict__ y, const void* _
   const int64_t vol = static_cast<int64_t>(Do) * Ho * Wo;
   T* y0 = y + (n0 * C + c) * vol + static_cast<int64_t>(od) * Ho * Wo;
   T* y1 = y + (min64(n1, N - 1) * C + c) * vol + static_cast<int64_t>(od) * Ho * Wo;
+  const float inv_wo = 1.0f / static_cast<float>(Wo);
   for (int idx = threadIdx.x; idx < Ho * Wo; idx += blockDim.x) {
-    const int h = idx / Wo, w = idx - h * Wo;
+    const int h = qdiv(idx, Wo, inv_wo), w = idx - h * Wo;
     const float2 v = buf[h * RS + w];
     y0[idx] = from_f32<T>(fmaf(v.x, scale, bv));
     if (n1 < N) y1[idx] = from_f32<T>(fmaf(v.y, scale, bv));
@@ -475,11 +516,14 @@ Sizes sizes(int64_t N, int64_t Cin, int64_t Cout, int64_t fd, int64_t fh, int64_
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
+// twiddles + transform buffer + digit-reversed position tables (int)
 size_t plane_smem(const Plan3& p) {
-  return static_cast<size_t>(p.h.n + p.w.n + p.h.n * (p.w.n + 1)) * sizeof(float2);
+  return static_cast<size_t>(p.h.n + p.w.n + p.h.n * (p.w.n + 1)) * sizeof(float2) +
+         static_cast<size_t>(p.h.n + p.w.n) * sizeof(int);
 }
 size_t depth_smem(const Plan3& p, int C) {
-  return static_cast<size_t>(p.d.n + C * kCols * (p.d.n + 1)) * sizeof(float2);
+  return static_cast<size_t>(p.d.n + C * kCols * (p.d.n + 1)) * sizeof(float2) +
+         static_cast<size_t>(p.d.n) * sizeof(int);
 }
 
 template <typename K>
