@@ -313,12 +313,14 @@ __device__ __forceinline__ void build_pass_twiddles(float2* tw, const Plan& p) {
 template <int R, bool INV>
 __device__ __forceinline__ void apply_twiddle_powers(float2 (&v)[R], float2 w) {
   if (INV) w.y = -w.y;
-  float2 wm = w;
+  // Powers as a product tree, w^m = w^(m/2) * w^(m - m/2): the same R - 2
+  // multiplications as a running product, but log2(R) deep instead of R - 2.
+  float2 wp[R];
+  wp[1] = w;
 #pragma unroll
-  for (int m = 1; m < R; ++m) {
-    v[m] = cmul(v[m], wm);
-    if (m + 1 < R) wm = cmul(wm, w);
-  }
+  for (int m = 2; m < R; ++m) wp[m] = cmul(wp[m / 2], wp[m - m / 2]);
+#pragma unroll
+  for (int m = 1; m < R; ++m) v[m] = cmul(v[m], wp[m]);
 }
 
 // Middle pass (shared memory in and out), per-pass table `tw`.
