@@ -346,11 +346,18 @@ __device__ __forceinline__ void pass_t(float2* buf, int n, int span, const float
   }
 }
 
-template <bool INV>
+// MAXR: largest radix the caller's plans use (radix-16 code is only
+// instantiated when MAXR >= 16).
+template <bool INV, int MAXR = 16>
 __device__ __forceinline__ void run_pass_t(int radix, float2* buf, int n, int span,
                                            const float2* tw) {
+  if constexpr (MAXR >= 16) {
+    if (radix == 16) {
+      pass_t<16, INV>(buf, n, span, tw);
+      return;
+    }
+  }
   switch (radix) {
-    case 16: pass_t<16, INV>(buf, n, span, tw); break;
     case 8: pass_t<8, INV>(buf, n, span, tw); break;
     case 4: pass_t<4, INV>(buf, n, span, tw); break;
     case 2: pass_t<2, INV>(buf, n, span, tw); break;
@@ -362,21 +369,21 @@ __device__ __forceinline__ void run_pass_t(int radix, float2* buf, int n, int sp
 
 // Host: radix plan for n = 2^a 3^b 5^c (largest radices first); false if n
 // has another prime factor or needs too many passes.
-inline bool make_plan(int64_t n, Plan* p) {
+// max_radix 16 (default) or 8: a radix-8 plan has more passes but its
+// butterflies need half the registers, for kernels that run more threads.
+inline bool make_plan(int64_t n, Plan* p, int max_radix = 16) {
   if (n < 2 || n > (1 << 24)) return false;
   p->n = static_cast<int>(n);
   p->passes = 0;
   int64_t m = n;
   const int order[] = {16, 8, 4, 2, 9, 3, 5};
   for (int r : order) {
+    if (r > max_radix) continue;
     while (m % r == 0) {
       if (r == 2 && m % 4 == 0) break;  // prefer 4 over 2 x 2
       if (p->passes == kMaxPasses) return false;
       p->radix[p->passes++] = r;
       m /= r;
-    }
-    if (r == 2 && m % 4 == 0) {
-      // unreachable with the order above, kept for clarity
     }
   }
   return m == 1;

@@ -22,7 +22,11 @@
 namespace b200 {
 namespace {
 
+// One CTA of kFftThreads per (channel, row pair), plans of radices <= 16.
+// (1024 threads with radix <= 8 plans -- twice the resident warps -- measured
+// no faster: the kernel is not occupancy-bound.)
 constexpr int kFftThreads = 512;
+constexpr int kFftMaxRadix = 16;
 constexpr int64_t kMaxFftN = 24576;
 
 size_t fft1d_smem(int n) {
@@ -148,7 +152,7 @@ fftconv1d_kernel(const T* __restrict__ x, const float2* __restrict__ spec,
 #undef B200_FIRST
   __syncthreads();
   for (int i = 1; i < P - 1; ++i) {
-    fft::run_pass_t<false>(plan.radix[i], buf, n, span[i], tw + off[i]);
+    fft::run_pass_t<false, kFftMaxRadix>(plan.radix[i], buf, n, span[i], tw + off[i]);
     __syncthreads();
   }
   const float2* h = spec + c * n;
@@ -157,7 +161,7 @@ fftconv1d_kernel(const T* __restrict__ x, const float2* __restrict__ spec,
 #undef B200_MID
   __syncthreads();
   for (int i = P - 2; i >= 1; --i) {
-    fft::run_pass_t<true>(plan.radix[i], buf, n, span[i], tw + off[i]);
+    fft::run_pass_t<true, kFftMaxRadix>(plan.radix[i], buf, n, span[i], tw + off[i]);
     __syncthreads();
   }
   const float scale = 1.0f / static_cast<float>(n);
@@ -202,7 +206,7 @@ fftconv1d_prepare_kernel(const T* __restrict__ w, float2* __restrict__ spec, int
 }
 
 bool plan1d(int64_t n, fft::Plan* p) {
-  return n >= 2 && n <= kMaxFftN && fft::make_plan(n, p);
+  return n >= 2 && n <= kMaxFftN && fft::make_plan(n, p, kFftMaxRadix);
 }
 
 template <typename K>
