@@ -516,13 +516,13 @@ def run_stack(args, rank, world, dev, peaks) -> dict:
     x_local = vs.shard_t(x.bfloat16(), rank, world).to(dev)
     del x
     group = dist.group.WORLD if world > 1 else None
-    stack = vs.VideoStack(params, group=group)
+    stack = vs.VideoStack(params, group=group, exchange=args.stack_exchange)
     for _ in range(max(2, args.warmup // 2)):
         stack.forward(x_local)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    # The step (kernels + NCCL statistics gather + halo send/recv) runs as one
+    # The step (kernels + statistics gather + halo exchange) runs as one
     # captured CUDA graph; one untimed replay, then `steps` timed replays.
     stack.capture(x_local)
     stack.replay()
@@ -536,7 +536,11 @@ def run_stack(args, rank, world, dev, peaks) -> dict:
         y = stack.replay()
     e.record()
     torch.cuda.synchronize()
-    stack.release()
+    from amd_tuned_torch import ops
+    flags = ops.read_device_flags(dev)
+    stack.close()
+    if flags:
+        raise RuntimeError(f"video stack: device fault word {flags} (an exchange wait ran out)")
     ms = s.elapsed_time(e) / steps
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -548,8 +552,12 @@ def run_stack(args, rank, world, dev, peaks) -> dict:
             "tflops": CFG5_FLOPS / (ms * 1e-3) / 1e12,
             "frac_of_peak": CFG5_FLOPS / (ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"],
             "peak_src": peaks["src"] + " sustained bf16",
-            "collectives": "per block: all_gather of GN partial stats; NCCL send/recv of "
-                           "1 halo frame each side",
+            "collectives": ("none" if world == 1 else
+                            "per block: all_gather of GN partial stats; NCCL send/recv of "
+                            "1 halo frame each side" if args.stack_exchange == "nccl" else
+                            "per block: GN partial stats and 1 halo frame each side stored "
+                            "into the peers' memory over NVLink (CUDA IPC windows, "
+                            "device flags; no NCCL launch)"),
             "timing": "one CUDA graph per step (captured once), replayed"}
 
 
@@ -605,6 +613,8 @@ def main() -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-shapes", action="store_true")
     ap.add_argument("--no-stack", action="store_true")
+    ap.add_argument("--stack-exchange", choices=("peer", "nccl"), default="peer",
+                    help="cfg5 at N > 1: peer-memory exchange or NCCL collectives")
     ap.add_argument("--only", choices=("cfg1", "cfg3", "cfg4a", "cfg4b", "cfg5conv"), default=None,
                     help="time one per-shape config alone (profiling target), one GPU")
     ap.add_argument("--small", action="store_true", help="with --only cfg4b: 64 channels")

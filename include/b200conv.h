@@ -195,6 +195,72 @@ int b200_fftconv3d_fwd(const void* x, const void* spectrum, const void* bias, vo
                        const int64_t* pad3, int64_t fd, int64_t fh, int64_t fw,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ */
+/* Peer-memory exchange of the T-sharded conv stack (one process per GPU).
+ * No counterpart in the reference (it is single-GPU); these replace the
+ * NCCL all-gather of GroupNorm partial statistics and the NCCL send/recv of
+ * halo frames with stores into the peers' memory over NVLink, ordered by
+ * flags that bounded device waits poll.
+ *
+ * A window is one device allocation per rank, mapped into every other rank
+ * with CUDA IPC:
+ *   [control | statistics flags | halo arrival counters |
+ *    statistics slots [2][ranks][entries * 3] fp32 | pad | xp]
+ * where xp is the rank's haloed channels-last conv operand
+ * [N, T_local + 2, H, W, C] at b200_peer_window_xp_offset().  Every rank
+ * uses the same ranks / entries, so the offsets below xp agree.
+ *
+ * Per block, in stream order on every rank:
+ *   b200_peer_stats_publish  advances the window's epoch e and stores this
+ *                            rank's (count, mean, M2) triples into slot
+ *                            [e & 1][rank] of every window, then raises
+ *                            flag [e & 1][rank] = e in each;
+ *   b200_peer_stats_merge    waits for flags [e & 1][*] == e in the local
+ *                            window and merges the slots in rank order (fp64,
+ *                            Chan) -- identical statistics on every rank;
+ *   (GroupNorm apply writes the xp interior)
+ *   b200_peer_halo_push      copies the first interior frame(s) into the
+ *                            previous rank's top halo and the last into the
+ *                            next rank's bottom halo, then adds 1 per CTA to
+ *                            the receiver's arrival counter;
+ *   b200_peer_halo_wait      waits until the local counters reach
+ *                            e * B200_PEER_PUSH_CTAS.
+ * Two slot parities suffice: a rank cannot publish block e + 2 before every
+ * rank has merged block e (it needs their block e + 1 statistics, computed
+ * after their merge of e).  One xp buffer suffices for the same reason.
+ * Every wait gives up after 2 s, records code 3 (statistics) or 4 (halo) in
+ * the device fault word (b200_read_device_flags) and returns; the merge then
+ * writes NaN statistics so that a broken exchange cannot pass unnoticed. */
+#define B200_PEER_MAX_RANKS 64
+#define B200_PEER_HANDLE_BYTES 64
+#define B200_PEER_PUSH_CTAS 64
+int64_t b200_peer_window_xp_offset(int64_t ranks, int64_t entries);
+int64_t b200_peer_window_bytes(int64_t ranks, int64_t entries, int64_t xp_bytes);
+/* cudaMalloc + zero fill + IPC handle (B200_PEER_HANDLE_BYTES into `handle`). */
+int b200_peer_window_alloc(int64_t bytes, void** window, void* handle);
+/* Maps a peer's window (cudaIpcOpenMemHandle); b200_peer_window_close unmaps. */
+int b200_peer_window_open(const void* handle, void** window);
+int b200_peer_window_close(void* window);
+int b200_peer_window_free(void* window);
+/* windows: DEVICE array of `ranks` window addresses as seen by this process
+ * (windows[rank] = the local window). */
+int b200_peer_stats_publish(const float* stats, void* const* windows, int64_t ranks,
+                            int64_t rank, int64_t entries, void* local_window, void* stream);
+int b200_peer_stats_merge(void* local_window, float* out, int64_t ranks, int64_t entries,
+                          void* stream);
+/* Side "lo" sends `items` blocks of `bytes` from src_lo (+ i * src_lo_stride)
+ * to dst_lo (+ i * dst_lo_stride) inside window `lo_window` (the previous
+ * rank's) and counts the arrival there; "hi" likewise to the next rank.
+ * A side with a NULL window is skipped.  bytes and strides are multiples of
+ * 16, pointers 16-byte aligned. */
+int b200_peer_halo_push(void* local_window, const void* src_lo, void* dst_lo, void* lo_window,
+                        int64_t src_lo_stride, int64_t dst_lo_stride, const void* src_hi,
+                        void* dst_hi, void* hi_window, int64_t src_hi_stride,
+                        int64_t dst_hi_stride, int64_t items, int64_t bytes, void* stream);
+/* expect_lo: the previous rank pushes into this window (bottom halo);
+ * expect_hi: the next rank does (top halo). */
+int b200_peer_halo_wait(void* local_window, int expect_lo, int expect_hi, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -65,6 +65,17 @@ SIGNATURES = {
     "b200_fftconv3d_workspace_bytes": (c_size_t, [c_int64] * 6),
     "b200_fftconv3d_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 9
                            + [c_i64p, c_int64, c_int64, c_int64, c_vp, c_size_t, c_vp]),
+    "b200_peer_window_xp_offset": (c_int64, [c_int64, c_int64]),
+    "b200_peer_window_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "b200_peer_window_alloc": (c_int, [c_int64, ctypes.POINTER(c_vp), c_vp]),
+    "b200_peer_window_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "b200_peer_window_close": (c_int, [c_vp]),
+    "b200_peer_window_free": (c_int, [c_vp]),
+    "b200_peer_stats_publish": (c_int, [c_vp, c_vp, c_int64, c_int64, c_int64, c_vp, c_vp]),
+    "b200_peer_stats_merge": (c_int, [c_vp, c_vp, c_int64, c_int64, c_vp]),
+    "b200_peer_halo_push": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int64, c_int64, c_vp, c_vp, c_vp,
+                                    c_int64, c_int64, c_int64, c_int64, c_vp]),
+    "b200_peer_halo_wait": (c_int, [c_vp, c_int, c_int, c_vp]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

@@ -1,0 +1,58 @@
+"""Host-side geometry of the peer-memory exchange (no GPU): the halo sides
+each rank pushes and the window layout the C ABI reports."""
+from __future__ import annotations
+
+import pytest
+
+from amd_tuned_torch import _lib
+from amd_tuned_torch.peer import HaloSide, halo_plan
+from amd_tuned_torch.video_stack import t_partition
+
+
+@pytest.mark.parametrize("T,world", [(64, 8), (17, 4), (5, 3), (2, 2)])
+def test_halo_plan_targets_neighbour_halo_frames(T, world):
+    fb = 1000 * 16
+    sizes = t_partition(T, world)
+    for r in range(world):
+        lo, hi = halo_plan(r, sizes, fb)
+        assert (lo is None) == (r == 0) and (hi is None) == (r == world - 1)
+        if lo is not None:
+            # my first interior frame -> previous rank's top halo frame T_prev + 1
+            assert lo == HaloSide(r - 1, fb, (sizes[r] + 2) * fb, (sizes[r - 1] + 1) * fb,
+                                  (sizes[r - 1] + 2) * fb)
+        if hi is not None:
+            # my last interior frame -> next rank's bottom halo frame 0
+            assert hi == HaloSide(r + 1, sizes[r] * fb, (sizes[r] + 2) * fb, 0,
+                                  (sizes[r + 1] + 2) * fb)
+
+
+def test_halo_plan_is_a_permutation_of_neighbour_frames():
+    """Every halo frame of every rank is written by exactly one push, and it
+    is the neighbour's adjacent interior frame (global frame index check)."""
+    sizes = t_partition(23, 5)
+    start = [sum(sizes[:r]) for r in range(5)]
+    written = {}
+    for r in range(5):
+        for side in halo_plan(r, sizes, 1):
+            if side is None:
+                continue
+            src_global = start[r] + side.src_off - 1        # interior frame t -> global start+t-1
+            dst_local = side.dst_off                        # frame index in the receiver's xp
+            key = (side.peer, dst_local)
+            assert key not in written
+            written[key] = src_global
+    for q in range(5):
+        if q > 0:
+            assert written[(q, 0)] == start[q] - 1           # frame just below q's slice
+        if q < 4:
+            assert written[(q, sizes[q] + 1)] == start[q] + sizes[q]   # frame just above
+
+
+def test_window_layout():
+    L = _lib.lib()
+    off = L.b200_peer_window_xp_offset(8, 32)
+    assert off > 0 and off % 65536 == 0
+    assert off >= 2048 + 2 * 8 * 32 * 3 * 4
+    assert L.b200_peer_window_bytes(8, 32, 100) == off + 65536
+    assert L.b200_peer_window_xp_offset(65, 32) == -1
+    assert L.b200_peer_window_xp_offset(2, 0) == -1
