@@ -146,6 +146,21 @@ int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, in
                     int64_t Cout, int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,
                     int x_channels_last, int y_channels_last, int variant, void* workspace,
                     size_t workspace_bytes, void* stream);
+/* b200_conv3d_fwd with a halo gate for the T-sharded stack (no reference
+ * counterpart): x is a haloed operand whose first and last frames other GPUs
+ * write (b200_peer_halo_push).  Tiles of output frame 0 / Do - 1 are
+ * scheduled last, and before loading one the producer waits (bounded, fault
+ * code 4) until *gate_lo / *gate_hi reach *gate_epoch * gate_scale (u32
+ * device words; a NULL counter means that side needs no wait).  With
+ * gate_epoch NULL this is b200_conv3d_fwd.  Needs KD = 3, T padding 0,
+ * T dilation 1. */
+int b200_conv3d_fwd_gated(const void* x, const void* wp, const void* bias, void* y, int dtype,
+                          int bias_dtype, int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                          int64_t Cout, int64_t KD, int64_t KH, int64_t KW,
+                          const int64_t* params9, int x_channels_last, int y_channels_last,
+                          int variant, void* workspace, size_t workspace_bytes,
+                          const void* gate_epoch, const void* gate_lo, const void* gate_hi,
+                          int64_t gate_scale, void* stream);
 
 /* NCDHW -> channels-last copy ([N, C, S] -> [N, S, C]); conv3d operand layout. */
 int b200_to_channels_last(const void* x, void* y, int dtype, int64_t N, int64_t C, int64_t S,

@@ -53,6 +53,9 @@ SIGNATURES = {
     "b200_conv3d_workspace_bytes": (c_size_t, [c_int64] * 5 + [c_int]),
     "b200_conv3d_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 9
                         + [c_i64p, c_int, c_int, c_int, c_vp, c_size_t, c_vp]),
+    "b200_conv3d_fwd_gated": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 9
+                              + [c_i64p, c_int, c_int, c_int, c_vp, c_size_t, c_vp, c_vp, c_vp,
+                                 c_int64, c_vp]),
     "b200_to_channels_last": (c_int, [c_vp, c_vp, c_int, c_int64, c_int64, c_int64, c_vp]),
     "b200_fft_supported_length": (c_int, [c_int64]),
     "b200_fftconv1d_spectrum_bytes": (c_size_t, [c_int64, c_int64]),

@@ -30,6 +30,7 @@ from . import _lib
 
 HANDLE_BYTES = 64      # B200_PEER_HANDLE_BYTES
 MAX_RANKS = 64         # B200_PEER_MAX_RANKS
+PUSH_CTAS = 64         # B200_PEER_PUSH_CTAS
 
 
 @dataclass(frozen=True)
@@ -196,6 +197,14 @@ class PeerWindows:
         rc = _lib.lib().b200_peer_halo_push(self.local, ls, ld, lw, lss, lds, hs, hd, hw, hss,
                                             hds, self.N, self.frame_bytes, self._stream())
         _lib.check(rc, "b200_peer_halo_push")
+
+    def gate(self) -> Tuple[int, int, int, int]:
+        """(epoch, bottom counter, top counter, scale) addresses for
+        b200_conv3d_fwd_gated: the conv waits for this block's halo arrivals
+        itself, so the push can overlap the interior tiles."""
+        lo = self.local + 1024 if self.lo is not None else 0
+        hi = self.local + 1024 + 128 if self.hi is not None else 0
+        return self.local, lo, hi, PUSH_CTAS
 
     def wait(self) -> None:
         rc = _lib.lib().b200_peer_halo_wait(self.local, int(self.lo is not None),

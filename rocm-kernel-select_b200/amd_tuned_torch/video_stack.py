@@ -109,9 +109,10 @@ class StackBackend:
         ([N, T, H, W, C] contiguous view for one batch item at a time)."""
         raise NotImplementedError
 
-    def conv_cl(self, xp: torch.Tensor, weight, bias, pad_hw: int) -> torch.Tensor:
+    def conv_cl(self, xp: torch.Tensor, weight, bias, pad_hw: int, gate=None) -> torch.Tensor:
         """Conv3d over channels-last xp [N, Tp, H, W, C], T padding 0,
-        H/W padding pad_hw; returns NCDHW [N, Cout, Tp - 2, H, W]."""
+        H/W padding pad_hw; returns NCDHW [N, Cout, Tp - 2, H, W].  `gate`:
+        halo arrival words the kernel waits on before the edge frames."""
         raise NotImplementedError
 
 
@@ -134,10 +135,10 @@ class CudaBackend(StackBackend):
                                      weight, bias, eps, silu=True, channels_last_out=True)
             out_cl[n].copy_(y.reshape(out_cl[n].shape))
 
-    def conv_cl(self, xp, weight, bias, pad_hw):
+    def conv_cl(self, xp, weight, bias, pad_hw, gate=None):
         from . import ops
         out = ops.conv3d(xp, weight, bias, (1, 1, 1), (0, pad_hw, pad_hw), (1, 1, 1),
-                         x_channels_last=True)
+                         x_channels_last=True, gate=gate)
         if out is None:
             raise RuntimeError("conv3d tensor-core kernel declined the stack's shape")
         return out
@@ -255,16 +256,31 @@ class VideoStack:
         return self._peer
 
     def block_peer(self, x: torch.Tensor, i: int, pw=None) -> torch.Tensor:
-        """One block over the peer windows `pw` (default: this rank's)."""
+        """One block over the peer windows `pw` (default: this rank's).  The
+        halo push runs on a side stream while the conv computes its interior
+        frames; the conv's producer waits for the halo arrivals itself
+        before the edge frames (b200_conv3d_fwd_gated)."""
         T = x.shape[2]
         pw = pw or self.peer_windows(x)
         pw.publish(self.backend.partial_stats(x, self.p.groups))
         stats = pw.merge()
         self.backend.norm_silu_into(x, stats, self.p.groups, self.p.gn_weight[i],
                                     self.p.gn_bias[i], self.p.eps, pw.xp[:, 1:T + 1])
-        pw.push()
-        pw.wait()
-        return self.backend.conv_cl(pw.xp, self.p.conv_weight[i], self.p.conv_bias[i], 1)
+        main = torch.cuda.current_stream(x.device)
+        side = self._side_stream(x.device)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            pw.push()
+        y = self.backend.conv_cl(pw.xp, self.p.conv_weight[i], self.p.conv_bias[i], 1,
+                                 gate=pw.gate())
+        main.wait_stream(side)      # the next block's apply overwrites what the push reads
+        return y
+
+    def _side_stream(self, device) -> torch.cuda.Stream:
+        s = getattr(self, "_side", None)
+        if s is None:
+            s = self._side = torch.cuda.Stream(device=device)
+        return s
 
     # -------------------------------------------------------------- main
     def block(self, x: torch.Tensor, i: int) -> torch.Tensor:

@@ -45,7 +45,8 @@ int sm_count();
 int max_smem_optin();
 
 // Device-side fault word: bounded waits set it instead of spinning forever.
-// Codes: 1 = pipeline wait timed out in conv3d.  Kernels receive its device
+// Codes: 1 = pipeline wait timed out in conv3d; 3 = peer statistics wait,
+// 4 = peer halo wait (b200_peer_* and the gated conv3d) timed out.  Kernels receive its device
 // address as a plain pointer (no relocatable device code needed).
 int* device_flags_ptr();
 
@@ -179,6 +180,23 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// System-scope ordering for flags that other GPUs write over NVLink.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Wrap-safe "counter has reached target" for monotonically advancing words.
+__device__ __forceinline__ bool counter_reached(uint32_t v, uint32_t target) {
+  return static_cast<int32_t>(v - target) >= 0;
 }
 
 // Upper bound for any device-side wait (ns).  Normal waits are microseconds;

@@ -67,10 +67,21 @@ struct ConvParams {
   // multiple of 8).  fuse_mode 2: channels-last input, box {KB, raw_w, rows,
   // 1, 1} starting at column ow0 - pw (raw_w = BW + (KW - 1) * dw).
   int fuse_mode, raw_w, raw_bytes, raw_tx, wpad8, lbw;
+  // Halo gate (T-sharded stack): output frame 0 reads input frame 0 and
+  // frame Do - 1 reads frame Do + 1, which other GPUs write.  Before loading
+  // a tile of such a frame the producer waits until *gate_lo / *gate_hi
+  // (arrival counters, NULL = no wait) reach *gate_epoch * gate_scale; the
+  // tile order puts those frames last.  gate_epoch NULL = no gate.
+  int Nb;
+  const uint32_t* gate_epoch;
+  const uint32_t* gate_lo;
+  const uint32_t* gate_hi;
+  uint32_t gate_scale;
 };
 
 struct TileCoord {
   int n, od, oh0, ow0, n0;
+  uint32_t lin;   // schedule-independent tile id (n, od, th, tw, nt order)
 };
 
 __device__ __forceinline__ TileCoord decode_tile(int t, const ConvParams& p, int BN) {
@@ -81,12 +92,52 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const ConvParams& p, int
   t /= p.tiles_w;
   const int th = t % p.tiles_h;
   t /= p.tiles_h;
-  c.od = t % p.Do;
-  c.n = t / p.Do;
+  if (p.gate_epoch) {
+    // (n, od) pairs: interior frames first, then the gated frames 0, Do - 1.
+    const int inner = p.Do > 2 ? p.Do - 2 : 0;
+    const int I = p.Nb * inner;
+    if (t < I) {
+      c.n = t / inner;
+      c.od = 1 + t % inner;
+    } else {
+      const int B = p.Do < 2 ? p.Do : 2;
+      const int j = t - I;
+      c.n = j / B;
+      c.od = (j % B) ? p.Do - 1 : 0;
+    }
+  } else {
+    c.od = t % p.Do;
+    c.n = t / p.Do;
+  }
+  c.lin = ((((static_cast<uint32_t>(c.n) * p.Do + c.od) * p.tiles_h + th) * p.tiles_w + tw) *
+           p.tiles_n) + nt;
   c.oh0 = th * p.BH * p.MT;
   c.ow0 = tw * p.BW;
   c.n0 = nt * BN;
   return c;
+}
+
+// Waits (bounded) until the halo frames output frame `od` reads have arrived;
+// false (fault code 4 recorded) when the wait runs out.  The proxy fence
+// orders the peers' generic stores before this CTA's TMA reads of them.
+__device__ bool halo_gate_wait(const ConvParams& p, int od) {
+  const uint32_t target =
+      *reinterpret_cast<const volatile uint32_t*>(p.gate_epoch) * p.gate_scale;
+  const uint64_t t0 = globaltimer_ns();
+  for (int side = 0; side < 2; ++side) {
+    const uint32_t* c = side == 0 ? (od == 0 ? p.gate_lo : nullptr)
+                                  : (od == p.Do - 1 ? p.gate_hi : nullptr);
+    if (!c) continue;
+    while (!counter_reached(ld_acquire_sys(c), target)) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (p.flags) atomicExch(p.flags, 4);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
 }
 
 // MT: M tiles per CTA tile (1, 2 or 4); they share every weight box and the
@@ -180,9 +231,9 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
     int ru = 0;
     bool ok = true;
     const int units = p.kblocks / p.KW;
-    const int rot = p.rotate ? static_cast<int>((blockIdx.x * 7u) % units) : 0;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
       const TileCoord tc = decode_tile(t, p, BN);
+      const int rot = p.rotate ? static_cast<int>((tc.lin * 7u) % units) : 0;
       for (int uu = 0; uu < units && ok; ++uu, ++ru) {
         int u = uu + rot;
         if (u >= units) u -= units;
@@ -247,12 +298,24 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       // k-block = (kd, kh block, kw, 64-channel chunk).  One A box of
       // BH + (khg - 1) * dh input rows serves the khg kh-taps of the block
       // (tap j reads the rows starting j * dh rows down); one weight box per
-      // tap.  Each CTA starts its K walk at a different k-block: CTAs in
-      // lockstep would all fetch the same weight box at once (an L2 hot
-      // spot); the sum is order-independent.
-      const int rot = p.rotate ? static_cast<int>((blockIdx.x * 7u) % p.kblocks) : 0;
+      // tap.  Neighbouring tiles start their K walk at different k-blocks:
+      // CTAs in lockstep would all fetch the same weight box at once (an L2
+      // hot spot).  The start depends on the tile, not on the CTA, so a
+      // tile's accumulation order (and its rounding) is the same whatever
+      // the schedule or grid.
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         const TileCoord tc = decode_tile(t, p, BN);
+        const int rot = p.rotate ? static_cast<int>((tc.lin * 7u) % p.kblocks) : 0;
+        if (p.gate_epoch && (tc.od == 0 || tc.od == p.Do - 1)) {
+          int open = 1;
+          if (lane == 0) open = halo_gate_wait(p, tc.od) ? 1 : 0;
+          open = __shfl_sync(0xffffffffu, open, 0);
+          if (!open) {
+            if (lane == 0) *abort = 1;
+            ok = false;
+            break;
+          }
+        }
         for (int kk = 0; kk < p.kblocks; ++kk) {
           int kb = kk + rot;
           if (kb >= p.kblocks) kb -= p.kblocks;
@@ -710,11 +773,19 @@ int pick_bn(int64_t Cout, int code) {
   return 256;
 }
 
+struct HaloGate {
+  const uint32_t* epoch;
+  const uint32_t* lo;
+  const uint32_t* hi;
+  uint32_t scale;
+};
+
 template <typename T>
 int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int bias_dt,
                  int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int64_t Cout,
                  int64_t KD, int64_t KH, int64_t KW, const int64_t* prm9, int x_cl, int y_cl,
-                 int variant, void* ws, size_t ws_bytes, cudaStream_t stream) {
+                 int variant, void* ws, size_t ws_bytes, cudaStream_t stream,
+                 const HaloGate* gate) {
   const int64_t sd = prm9[0], sh = prm9[1], sw = prm9[2];
   const int64_t pd = prm9[3], ph = prm9[4], pw = prm9[5];
   const int64_t dd = prm9[6], dh = prm9[7], dw = prm9[8];
@@ -765,10 +836,15 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     int mt = 1, kb = kBK, khg = 1, stages = 0, a_bytes = 0, stage_bytes = 0;
     bool staging = false;
   };
+  // A gated conv may spin on halo arrivals while the push kernel that
+  // delivers this GPU's own halo to a peer still has to run: keep 8 KiB of
+  // each SM's shared memory free so a push CTA can always be resident beside
+  // a conv CTA (it needs none but the per-CTA reservation).
+  const size_t smem_cap = (gate && gate->epoch) ? kSmemBudget - 8192 : kSmemBudget;
   auto geom = [&](int mt, int kb, int khg, bool staging, Geo* g) {
     const int64_t rows = static_cast<int64_t>(mt) * BH + (khg - 1) * dh;
     if (rows > 256) return false;
-    const size_t budget = kSmemBudget - fixed_smem(BN, staging);
+    const size_t budget = smem_cap - fixed_smem(BN, staging);
     g->mt = mt;
     g->kb = kb;
     g->khg = khg;
@@ -994,6 +1070,20 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   prm.wpad8 = wpad8;
   prm.lbw = 0;
   while ((1 << prm.lbw) < BW) ++prm.lbw;
+  prm.Nb = (int)N;
+  prm.gate_epoch = nullptr;
+  prm.gate_lo = prm.gate_hi = nullptr;
+  prm.gate_scale = 0;
+  if (gate && gate->epoch) {
+    // The gate assumes one halo frame each side read only by the edge
+    // output frames: KD = 3, no T padding, no T dilation, unfused producer.
+    if (KD != 3 || pd != 0 || dd != 1 || fuse_mode != 0)
+      return fail_unsupported("halo gate: needs KD = 3, T padding 0, T dilation 1, unfused");
+    prm.gate_epoch = gate->epoch;
+    prm.gate_lo = gate->lo;
+    prm.gate_hi = gate->hi;
+    prm.gate_scale = gate->scale;
+  }
 
   // NCDHW output through one TMA store per tile when TMA can address it:
   // 16-byte aligned base, rows of Wo elements a multiple of 16 bytes.  The
@@ -1085,7 +1175,23 @@ int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, in
                     int64_t Cout, int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,
                     int x_channels_last, int y_channels_last, int variant, void* workspace,
                     size_t workspace_bytes, void* stream) {
+  return b200_conv3d_fwd_gated(x, wp, bias, y, dtype, bias_dtype, N, Cin, D, H, W, Cout, KD, KH,
+                               KW, params9, x_channels_last, y_channels_last, variant, workspace,
+                               workspace_bytes, nullptr, nullptr, nullptr, 0, stream);
+}
+
+int b200_conv3d_fwd_gated(const void* x, const void* wp, const void* bias, void* y, int dtype,
+                          int bias_dtype, int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                          int64_t Cout, int64_t KD, int64_t KH, int64_t KW,
+                          const int64_t* params9, int x_channels_last, int y_channels_last,
+                          int variant, void* workspace, size_t workspace_bytes,
+                          const void* gate_epoch, const void* gate_lo, const void* gate_hi,
+                          int64_t gate_scale, void* stream) {
   if (!x || !wp || !y || !params9) return fail_arg("NULL pointer");
+  if (gate_epoch && (gate_scale < 1 || gate_scale > 0xffff)) return fail_arg("gate_scale");
+  const HaloGate gate{static_cast<const uint32_t*>(gate_epoch),
+                      static_cast<const uint32_t*>(gate_lo),
+                      static_cast<const uint32_t*>(gate_hi), static_cast<uint32_t>(gate_scale)};
   if (dtype != B200_DTYPE_F16 && dtype != B200_DTYPE_BF16)
     return fail_unsupported("conv3d tensor-core path: fp16/bf16 only");
   if (bias && !dtype_ok(bias_dtype)) return fail_arg("bad bias dtype");
@@ -1096,10 +1202,10 @@ int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, in
   if (dtype == B200_DTYPE_F16)
     return conv3d_typed<__half>(x, wp, bias, y, bias_dtype, N, Cin, D, H, W, Cout, KD, KH, KW,
                                 params9, x_channels_last, y_channels_last, variant, workspace,
-                                workspace_bytes, s);
+                                workspace_bytes, s, &gate);
   return conv3d_typed<__nv_bfloat16>(x, wp, bias, y, bias_dtype, N, Cin, D, H, W, Cout, KD, KH,
                                      KW, params9, x_channels_last, y_channels_last, variant,
-                                     workspace, workspace_bytes, s);
+                                     workspace, workspace_bytes, s, &gate);
 }
 
 int b200_to_channels_last(const void* x, void* y, int dtype, int64_t N, int64_t C, int64_t S,

@@ -31,26 +31,11 @@ constexpr int kFaultHalo = 4;
 static_assert(sizeof(cudaIpcMemHandle_t) == B200_PEER_HANDLE_BYTES, "IPC handle size");
 static_assert(kFlagOff + 2 * B200_PEER_MAX_RANKS * 4 <= kCntOff, "flag area overlaps");
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Wrap-safe "counter has reached target" for monotonically advancing words.
-__device__ __forceinline__ bool reached(uint32_t v, uint32_t target) {
-  return static_cast<int32_t>(v - target) >= 0;
-}
 __device__ bool poll_bounded(const uint32_t* p, uint32_t target) {
-  if (reached(ld_acquire_sys(p), target)) return true;
+  if (counter_reached(ld_acquire_sys(p), target)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
-    if (reached(ld_acquire_sys(p), target)) return true;
+    if (counter_reached(ld_acquire_sys(p), target)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
     __nanosleep(32);
   }

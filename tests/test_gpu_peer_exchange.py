@@ -47,8 +47,9 @@ def _host_route(xs, sizes, params, i, backend):
     return [backend.conv_cl(xp, params.conv_weight[i], params.conv_bias[i], 1) for xp in xps], stats
 
 
-@pytest.mark.parametrize("N,T,R", [(1, 7, 2), (2, 9, 3), (1, 12, 4)])
-def test_peer_route_emulated_matches_host_route(cuda, N, T, R):
+@pytest.mark.parametrize("gated", [False, True])
+@pytest.mark.parametrize("N,T,R", [(1, 7, 2), (2, 9, 3), (1, 12, 4), (1, 5, 4)])
+def test_peer_route_emulated_matches_host_route(cuda, N, T, R, gated):
     C, H, W, G = 64, 8, 16, 8
     params = vs.make_params(channels=C, blocks=2, groups=G, dtype=torch.bfloat16, seed=3,
                             device=cuda)
@@ -71,9 +72,11 @@ def test_peer_route_emulated_matches_host_route(cuda, N, T, R):
                                  params.eps, wins[r].xp[:, 1:sizes[r] + 1])
             for r in range(R):
                 wins[r].push()
-            for r in range(R):
-                wins[r].wait()
-            yp = [b.conv_cl(wins[r].xp, params.conv_weight[i], params.conv_bias[i], 1)
+            if not gated:
+                for r in range(R):
+                    wins[r].wait()
+            yp = [b.conv_cl(wins[r].xp, params.conv_weight[i], params.conv_bias[i], 1,
+                            gate=wins[r].gate() if gated else None)
                   for r in range(R)]
             yh, hstats = _host_route(yh, sizes, params, i, b)
             for r in range(R):
@@ -98,6 +101,31 @@ def test_peer_waits_time_out_into_fault_word(cuda):
         wins[0].wait()                                   # rank 1 never pushes
         torch.cuda.synchronize()
         assert ops.read_device_flags(cuda) == 4
+    finally:
+        for w in wins:
+            w.close()
+
+
+def test_gated_conv_times_out_without_halo(cuda):
+    """The conv's producer gives up on a halo that never arrives: fault code
+    4, the kernel unwinds, and the context stays usable."""
+    C, H, W, G = 64, 4, 16, 8
+    params = vs.make_params(channels=C, blocks=1, groups=G, dtype=torch.bfloat16, seed=3,
+                            device=cuda)
+    wins = PeerWindows.emulate([3, 3], G, 1, H, W, C, torch.bfloat16, cuda)
+    try:
+        ops.read_device_flags(cuda)
+        wins[0].publish(torch.ones(G, 3, device=cuda))   # epoch 1; rank 1 never pushes
+        wins[0].xp.normal_()
+        vs.CudaBackend().conv_cl(wins[0].xp, params.conv_weight[0], params.conv_bias[0], 1,
+                                 gate=wins[0].gate())
+        torch.cuda.synchronize()
+        assert ops.read_device_flags(cuda) == 4
+        # the context is still usable: an ungated conv runs and is finite
+        y = vs.CudaBackend().conv_cl(wins[0].xp, params.conv_weight[0], params.conv_bias[0], 1)
+        torch.cuda.synchronize()
+        assert torch.isfinite(y.float()).all()
+        assert ops.read_device_flags(cuda) == 0
     finally:
         for w in wins:
             w.close()
