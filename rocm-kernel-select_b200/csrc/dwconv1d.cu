@@ -131,10 +131,17 @@ dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
       for (int e = 0; e < V; ++e) v[e] = (p + e >= 0 && p + e < L) ? to_f32(xr[p + e]) : 0.f;
     }
   };
-  // All sub-tiles' input vectors are requested before any is used.
-  float cur[kDwSubTiles][V];
+  // All input vectors -- each sub-tile's own vector and, for lanes 0 / 31,
+  // the neighbouring vector outside the warp -- are requested before any is
+  // used, so a warp waits for one memory round trip, not two.
+  float cur[kDwSubTiles][V], edge[kDwSubTiles][V];
 #pragma unroll
   for (int u = 0; u < kDwSubTiles; ++u) load_vec(base + u * kSub, cur[u]);
+  if (lane == 0 || lane == 31) {
+    const int64_t off = lane == 0 ? -V : V;
+#pragma unroll
+    for (int u = 0; u < kDwSubTiles; ++u) load_vec(base + u * kSub + off, edge[u]);
+  }
   float wk[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) wk[k] = load_param(w, wdt, c * K + k);
@@ -148,9 +155,9 @@ dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
     for (int e = 0; e < V; ++e) {
       prev[e] = __shfl_up_sync(0xffffffffu, cur[u][e], 1);
       next[e] = __shfl_down_sync(0xffffffffu, cur[u][e], 1);
+      if (lane == 0) prev[e] = edge[u][e];
+      if (lane == 31) next[e] = edge[u][e];
     }
-    if (lane == 0) load_vec(o0 - V, prev);
-    if (lane == 31) load_vec(o0 + V, next);
     float out[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) {
