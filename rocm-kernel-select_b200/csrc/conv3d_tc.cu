@@ -51,6 +51,7 @@ struct ConvParams {
   int pd, ph, pw, dd, dh, dw;
   int BW, BH;
   int MT;                       // M tiles (of 128 positions) per CTA tile, stacked along H
+  int pair;                     // CTA pairs (cta_group::2): a tile is 2 x MT M tiles
   int tiles_w, tiles_h, tiles_n, num_tiles;
   int cchunks, kblocks;
   int khg, khb;                 // kh taps per k-block (1 or KH), kh blocks = KH / khg
@@ -111,7 +112,7 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const ConvParams& p, int
   }
   c.lin = ((((static_cast<uint32_t>(c.n) * p.Do + c.od) * p.tiles_h + th) * p.tiles_w + tw) *
            p.tiles_n) + nt;
-  c.oh0 = th * p.BH * p.MT;
+  c.oh0 = th * p.BH * p.MT * (p.pair ? 2 : 1);
   c.ow0 = tw * p.BW;
   c.n0 = nt * BN;
   return c;
@@ -156,19 +157,36 @@ __device__ bool halo_gate_wait(const ConvParams& p, int od) {
 // and KB): the box is {KB channels, BW + (KW - 1) * dw columns, rows, 1, 1}
 // in the same swizzle as A, and the warps copy 16-byte chunks from raw row
 // r * raw_w + w + kw * dw to A row r * BW + w, re-swizzled.
-template <typename T, int BN, int MT, int KB, bool FUSE>
+//
+// PAIR: a cluster of two CTAs on two SMs computes 2 x MT M tiles with MMAs
+// of M = 256 (tcgen05 cta_group::2): each CTA loads its own A rows and HALF
+// of the weight box (BN / 2 output channels), so the pair streams the
+// weights once instead of twice.  The even CTA (leader) issues the MMAs;
+// both producers' copies count on the leader's stage barriers; the leader's
+// MMA completions are committed to both CTAs' barriers; each CTA's epilogue
+// drains its own TMEM and tells the leader (one arrival per warp).
+template <typename T, int BN, int MT, int KB, bool FUSE, bool PAIR = false>
 __global__ void __launch_bounds__(FUSE ? kConvThreadsFused : kConvThreads, 1)
 conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                  const __grid_constant__ CUtensorMap tmy, const ConvParams p) {
   static_assert(KB == 64 || KB == 32, "k-block of 32 or 64 channels");
+  static_assert(!(FUSE && PAIR), "pairs use the unfused producer");
   constexpr int kRow = KB * 2;               // bytes per K-major operand row
-  constexpr int kBTap = BN * kRow;           // one tap's weight box
+  constexpr int kBNl = PAIR ? BN / 2 : BN;   // weight rows (output channels) this CTA loads
+  constexpr int kBTap = kBNl * kRow;         // this CTA's share of one tap's weight box
   constexpr int kAcc = MT * BN;              // TMEM columns of one tile's accumulators
   constexpr int kBufs = (2 * kAcc <= 512) ? 2 : 1;
   constexpr uint32_t kTmemCols = kBufs * kAcc < 32 ? 32u : static_cast<uint32_t>(kBufs * kAcc);
   static_assert(kBufs * kAcc <= 512 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM columns");
-  constexpr uint32_t kIdesc = umma_idesc_f16(sizeof(T) == 2 && std::is_same<T, __half>::value ? 0 : 1, kBM, BN);
+  constexpr uint32_t kIdesc = umma_idesc_f16(sizeof(T) == 2 && std::is_same<T, __half>::value ? 0 : 1,
+                                             PAIR ? 2 * kBM : kBM, BN);
   const int STAGES = p.stages;
+  // Tile walk: per CTA, or per CTA pair (both CTAs walk the same tiles).
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const int tile0 = PAIR ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int tstep = PAIR ? static_cast<int>(nclusters_x()) : static_cast<int>(gridDim.x);
+  const bool leader = crank == 0u;
+  const int oh_rank = PAIR ? static_cast<int>(crank) * p.BH * MT : 0;   // this CTA's first row
 
   // Stage s = [A box: a_bytes][B boxes: khg * kBTap], every piece 1024-byte
   // aligned, then the output staging tile (present when out_tma is set).
@@ -206,15 +224,23 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      // PAIR: one arrival per epilogue warp of both CTAs (on the leader's).
+      mbar_init(&tempty[a], PAIR ? 8 : 128);
     }
     mbar_init(drain, 1);
     *abort = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == 1) {
+    if (PAIR)
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+    else
+      tmem_alloc(tmem_slot, kTmemCols);
+  }
   tc_fence_before();
   __syncthreads();
+  // Both CTAs' barriers exist before either CTA touches the other's.
+  if (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Launched with programmatic stream serialisation: everything above (barrier
@@ -231,7 +257,7 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
     int ru = 0;
     bool ok = true;
     const int units = p.kblocks / p.KW;
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+    for (int t = tile0; t < p.num_tiles && ok; t += tstep) {
       const TileCoord tc = decode_tile(t, p, BN);
       const int rot = p.rotate ? static_cast<int>((tc.lin * 7u) % units) : 0;
       for (int uu = 0; uu < units && ok; ++uu, ++ru) {
@@ -303,8 +329,11 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       // hot spot).  The start depends on the tile, not on the CTA, so a
       // tile's accumulation order (and its rounding) is the same whatever
       // the schedule or grid.
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int t = tile0; t < p.num_tiles && ok; t += tstep) {
         const TileCoord tc = decode_tile(t, p, BN);
+        // Both CTAs of a pair walk the k-blocks in the same order (the
+        // rotation depends on the tile only): stage s holds the same k-block
+        // in both.
         const int rot = p.rotate ? static_cast<int>((tc.lin * 7u) % p.kblocks) : 0;
         if (p.gate_epoch && (tc.od == 0 || tc.od == p.Do - 1)) {
           int open = 1;
@@ -331,12 +360,27 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
           }
           if (lane == 0) {
             uint8_t* st = smem + stage * p.stage_bytes;
-            mbar_expect_tx(&full[stage], p.stage_bytes);
-            tma_load_5d(st, &tmx, &full[stage], cc * KB, tc.ow0 - p.pw + kw * p.dw,
-                        tc.oh0 - p.ph + hb * p.khg * p.dh, tc.od - p.pd + kd * p.dd, tc.n);
-            for (int j = 0; j < p.khg; ++j) {
-              const int tap = (kd * p.KH + hb * p.khg + j) * p.KW + kw;
-              tma_load_3d(st + p.a_bytes + j * kBTap, &tmw, &full[stage], cc * KB, tc.n0, tap);
+            if (PAIR) {
+              // The leader's barrier counts both CTAs' bytes; only the leader
+              // arrives on it.
+              if (leader) mbar_expect_tx(&full[stage], 2u * static_cast<uint32_t>(p.stage_bytes));
+              const uint32_t fb = mapa_u32(&full[stage], 0);
+              tma_load_5d_pair(st, &tmx, fb, cc * KB, tc.ow0 - p.pw + kw * p.dw,
+                               tc.oh0 + oh_rank - p.ph + hb * p.khg * p.dh,
+                               tc.od - p.pd + kd * p.dd, tc.n);
+              for (int j = 0; j < p.khg; ++j) {
+                const int tap = (kd * p.KH + hb * p.khg + j) * p.KW + kw;
+                tma_load_3d_pair(st + p.a_bytes + j * kBTap, &tmw, fb, cc * KB,
+                                 tc.n0 + static_cast<int>(crank) * kBNl, tap);
+              }
+            } else {
+              mbar_expect_tx(&full[stage], p.stage_bytes);
+              tma_load_5d(st, &tmx, &full[stage], cc * KB, tc.ow0 - p.pw + kw * p.dw,
+                          tc.oh0 - p.ph + hb * p.khg * p.dh, tc.od - p.pd + kd * p.dd, tc.n);
+              for (int j = 0; j < p.khg; ++j) {
+                const int tap = (kd * p.KH + hb * p.khg + j) * p.KW + kw;
+                tma_load_3d(st + p.a_bytes + j * kBTap, &tmw, &full[stage], cc * KB, tc.n0, tap);
+              }
             }
           }
           __syncwarp();
@@ -346,13 +390,16 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
           }
         }
       }
-      if (!ok && lane == 0) {
-        // Let the loads already issued land before shared memory goes away.
+      if (!ok && lane == 0 && leader) {
+        // Let the loads already issued land before shared memory goes away
+        // (a pair's loads all count on the leader's barriers).
         const int last = (stage + STAGES - 1) % STAGES;
         mbar_wait_bounded(&full[last], (stage == 0 ? phase ^ 1u : phase), nullptr, nullptr, 0);
       }
       __syncwarp();
     }
+  } else if (warp == 1 && PAIR && !leader) {
+    // The pair's MMAs are issued by the leader only.
   } else if (warp == 1) {
     // -------------------------------------------------------- MMA issuer
     // Converged warp; lane 0 issues the MMAs and commits.
@@ -361,7 +408,7 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++it) {
+      for (int t = tile0; t < p.num_tiles && ok; t += tstep, ++it) {
         const int acc = kBufs == 2 ? (it & 1) : 0;
         const uint32_t aphase = static_cast<uint32_t>(kBufs == 2 ? (it >> 1) : it) & 1u;
         const bool free_acc = mbar_wait_bounded(&tempty[acc], aphase ^ 1u, abort, p.flags, 1);
@@ -397,14 +444,25 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
                 for (int k = 0; k < KB / 16; ++k) {
                   // +32 bytes along K inside the swizzled row = +2 in the
                   // descriptor's address field.
-                  umma_f16_ss(d_tmem + static_cast<uint32_t>(i * BN),
-                              adesc + static_cast<uint64_t>(2 * k),
-                              bdesc + static_cast<uint64_t>(2 * k), kIdesc,
-                              (kb > 0 || j > 0 || k > 0) ? 1u : 0u);
+                  const uint32_t accum = (kb > 0 || j > 0 || k > 0) ? 1u : 0u;
+                  if (PAIR)
+                    umma_f16_ss_pair(d_tmem + static_cast<uint32_t>(i * BN),
+                                     adesc + static_cast<uint64_t>(2 * k),
+                                     bdesc + static_cast<uint64_t>(2 * k), kIdesc, accum);
+                  else
+                    umma_f16_ss(d_tmem + static_cast<uint32_t>(i * BN),
+                                adesc + static_cast<uint64_t>(2 * k),
+                                bdesc + static_cast<uint64_t>(2 * k), kIdesc, accum);
                 }
               }
             }
-            umma_commit(&empty[stage]);
+            if (PAIR) {
+              // The stage is free in both CTAs once these MMAs are done.
+              umma_commit_pair(smem_u32(&empty[stage]));
+              umma_commit_pair(mapa_u32(&empty[stage], 1));
+            } else {
+              umma_commit(&empty[stage]);
+            }
           }
           __syncwarp();
           if (++stage == STAGES) {
@@ -412,11 +470,23 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
             phase ^= 1u;
           }
         }
-        if (ok && lane == 0) umma_commit(&tfull[acc]);
+        if (ok && lane == 0) {
+          if (PAIR) {
+            umma_commit_pair(smem_u32(&tfull[acc]));
+            umma_commit_pair(mapa_u32(&tfull[acc], 1));
+          } else {
+            umma_commit(&tfull[acc]);
+          }
+        }
         __syncwarp();
       }
       // Drain: every MMA issued above has completed once `drain` flips.
-      if (lane == 0) umma_commit(drain);
+      if (lane == 0) {
+        if (PAIR)
+          umma_commit_pair(smem_u32(drain));
+        else
+          umma_commit(drain);
+      }
       __syncwarp();
       mbar_wait_bounded(drain, 0, nullptr, nullptr, 0);
       __syncwarp();
@@ -443,7 +513,7 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
     int ru = 0;
     bool ok = true;
     const int units = p.kblocks / p.KW;
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+    for (int t = tile0; t < p.num_tiles && ok; t += tstep) {
       for (int uu = 0; uu < units && ok; ++uu, ++ru) {
         const int r = ru & 1;
         const uint32_t rph = static_cast<uint32_t>(ru >> 1) & 1u;
@@ -531,7 +601,7 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
     T* y = static_cast<T*>(p.y);
     uint16_t* stage16 = reinterpret_cast<uint16_t*>(sOut);
     const int64_t plane = static_cast<int64_t>(p.Ho) * p.Wo;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
+    for (int t = tile0; t < p.num_tiles; t += tstep, ++it) {
       const int acc = kBufs == 2 ? (it & 1) : 0;
       const uint32_t aphase = static_cast<uint32_t>(kBufs == 2 ? (it >> 1) : it) & 1u;
       // All 128 threads leave together or not at all (a named barrier
@@ -553,7 +623,7 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
           if (etid == 0) bulk_wait_read0();
           epi_bar();
         }
-        const int oh0 = tc.oh0 + i * p.BH;
+        const int oh0 = tc.oh0 + oh_rank + i * p.BH;
         const int oh = oh0 + row / p.BW, ow = tc.ow0 + row % p.BW;
         const bool valid = oh < p.Ho && ow < p.Wo;
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -597,8 +667,19 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
           }
         }
         if (i == MT - 1) {
+          // Accumulators drained: the MMA warp may reuse them.
           tc_fence_before();
-          mbar_arrive(&tempty[acc]);  // accumulators drained: the MMA warp may reuse them
+          if (PAIR) {
+            __syncwarp();
+            if (lane == 0) {
+              if (leader)
+                mbar_arrive(&tempty[acc]);
+              else
+                mbar_arrive_remote(mapa_u32(&tempty[acc], 0));
+            }
+          } else {
+            mbar_arrive(&tempty[acc]);
+          }
         }
         if (p.out_tma) {
           fence_proxy_async();        // staging writes -> visible to the TMA engine
@@ -615,9 +696,15 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
 
   tc_fence_before();
   __syncthreads();
+  // A pair's CTAs exchange barrier arrivals until the end: neither leaves
+  // (and gives up its shared memory) before the other is done.
+  if (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    else
+      tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -739,27 +826,33 @@ constexpr size_t fixed_smem(int BN, bool staging) {
 }
 constexpr size_t kSmemBudget = 232448;  // sm_100 opt-in maximum per CTA
 
-template <typename T, int BN, int MT, int KB, bool FUSE = false>
+template <typename T, int BN, int MT, int KB, bool FUSE = false, bool PAIR = false>
 int launch_conv(const CUtensorMap& tmx, const CUtensorMap& tmw, const CUtensorMap& tmy,
                 const ConvParams& prm, bool staging, cudaStream_t stream) {
   const size_t smem = static_cast<size_t>(prm.stages) * prm.stage_bytes + fixed_smem(BN, staging) +
                       (FUSE ? 2 * static_cast<size_t>(prm.raw_bytes) : 0);
   if (smem > kSmemBudget) return fail_unsupported("conv3d stage geometry exceeds shared memory");
   if (prm.out_tma && !staging) return fail_arg("conv3d TMA output without staging");
-  auto kern = conv3d_tc_kernel<T, BN, MT, KB, FUSE>;
+  auto kern = conv3d_tc_kernel<T, BN, MT, KB, FUSE, PAIR>;
   B200_CUDA_CHECK(
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const int grid = std::min(prm.num_tiles, sm_count());
+  // Pairs: clusters of two CTAs, one tile per cluster per turn.
+  const int grid = PAIR ? 2 * std::min(prm.num_tiles, std::max(1, sm_count() / 2))
+                        : std::min(prm.num_tiles, sm_count());
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(FUSE ? kConvThreadsFused : kConvThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = PAIR ? 2 : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = PAIR ? 2 : 1;
   B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tmx, tmw, tmy, prm));
   return B200_OK;
 }
@@ -819,8 +912,15 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   const int64_t taps = KD * KH * KW;
   const int64_t Cin_pad = (Cin + kBK - 1) / kBK * kBK;   // packed weight row length
   const int64_t tiles_w = (Wo + BW - 1) / BW, tiles_n = (Cout + BN - 1) / BN;
+  // Variant bit 16: CTA pairs (cta_group::2 MMAs of M = 256; each CTA of the
+  // pair loads half of the weight box).  A pair tile is 2 x MT M tiles.
+  const bool pair = ((variant >> 16) & 1) != 0;
+  if (pair && (BN > 128 || ((variant >> 14) & 3) != 0))
+    return fail_unsupported("conv3d CTA pairs: Cout tiles <= 128, unfused producer");
+  const int BNl = pair ? BN / 2 : BN;   // weight rows one CTA loads
+  const int prow = pair ? 2 : 1;
   auto tiles_for = [&](int mt) {
-    return N * Do * ((Ho + BH * mt - 1) / (BH * mt)) * tiles_w * tiles_n;
+    return N * Do * ((Ho + BH * mt * prow - 1) / (BH * mt * prow)) * tiles_w * tiles_n;
   };
   // NCDHW output through TMA stores when TMA can address it: 16-byte aligned
   // base, rows of Wo elements a multiple of 16 bytes (variant bit 9 disables).
@@ -850,7 +950,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     g->khg = khg;
     g->staging = staging;
     g->a_bytes = static_cast<int>(rows * BW * kb * 2);
-    g->stage_bytes = g->a_bytes + khg * BN * kb * 2;
+    g->stage_bytes = g->a_bytes + khg * BNl * kb * 2;
     g->stages = static_cast<int>(std::min<size_t>(kMaxStages, budget / g->stage_bytes));
     return g->stages >= 2;
   };
@@ -884,9 +984,10 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     // so the epilogue of one tile overlaps the MMAs of the next): MT = 4 for
     // BN = 64, MT = 2 for BN = 128.  (MT = 4 at BN = 128 single-buffers and
     // measured slower than MT = 2 on the video stack's conv.)
-    const int64_t want = 2LL * sm_count();
+    const int64_t want = 2LL * sm_count() / prow;
     for (int mt : {4, 2}) {
       if (planned || BN > 128 || 2 * mt * BN > 512 || tiles_for(mt) < want) continue;
+      if (pair && mt > 2) continue;
       Geo c;
       if (plan(mt, &c) && c.stages >= 3) {
         g = c;
@@ -1019,7 +1120,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   {
     cuuint64_t dims[3] = {(cuuint64_t)Cin_pad, (cuuint64_t)Cout, (cuuint64_t)taps};
     cuuint64_t strides[2] = {(cuuint64_t)(Cin_pad * 2), (cuuint64_t)(Cout * Cin_pad * 2)};
-    cuuint32_t box[3] = {(cuuint32_t)KB, (cuuint32_t)BN, 1};
+    cuuint32_t box[3] = {(cuuint32_t)KB, (cuuint32_t)BNl, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = encode(&tmw, dt, 3, const_cast<void*>(wp), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
@@ -1044,7 +1145,8 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   prm.BH = BH;
   prm.MT = MT;
   prm.tiles_w = (int)tiles_w;
-  prm.tiles_h = (int)((Ho + BH * MT - 1) / (BH * MT));
+  prm.tiles_h = (int)((Ho + BH * MT * prow - 1) / (BH * MT * prow));
+  prm.pair = pair ? 1 : 0;
   prm.tiles_n = (int)tiles_n;
   const int64_t nt = tiles_for(MT);
   if (nt > 0x7fffffffLL) return fail_unsupported("too many tiles");
@@ -1116,6 +1218,17 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     }
     if (BN == 64) return launch_conv<T, 64, 4, 32, true>(tmx, tmw, tmy, prm, stg, stream);
     return launch_conv<T, 128, 4, 32, true>(tmx, tmw, tmy, prm, stg, stream);
+  }
+  if (pair) {
+    if (MT == 1) {
+      if (BN == 64) return launch_conv<T, 64, 1, 64, false, true>(tmx, tmw, tmy, prm, stg, stream);
+      return launch_conv<T, 128, 1, 64, false, true>(tmx, tmw, tmy, prm, stg, stream);
+    }
+    if (MT == 2) {
+      if (BN == 64) return launch_conv<T, 64, 2, 32, false, true>(tmx, tmw, tmy, prm, stg, stream);
+      return launch_conv<T, 128, 2, 32, false, true>(tmx, tmw, tmy, prm, stg, stream);
+    }
+    return fail_unsupported("conv3d CTA pairs: MT <= 2");
   }
   if (MT == 1) {
     if (BN == 64) return launch_conv<T, 64, 1, 64>(tmx, tmw, tmy, prm, stg, stream);

@@ -282,6 +282,44 @@ def test_conv3d_auto_multi_mtile_large(cuda):
     _no_fault()
 
 
+# CTA pairs (variant bit 16): cta_group::2 MMAs of M = 256, each CTA loading
+# half of the weight box.  Shapes: the cfg2 headline shape, a partial pair tile
+# (Ho not a multiple of the pair's rows), more pair tiles than SM pairs, bf16,
+# Cout = 128, two M tiles per CTA, channels-last in/out, a partial Cin chunk.
+_PAIR = 1 << 16
+
+
+@pytest.mark.parametrize("dt,N,Cin,D,H,W,Cout,k,p,dil,variant,cl", [
+    ("f16", 1, 64, 16, 32, 32, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), _PAIR, False),
+    ("f16", 1, 64, 5, 13, 32, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), _PAIR, False),
+    ("bf16", 2, 64, 24, 32, 32, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), _PAIR, False),
+    ("bf16", 1, 128, 6, 16, 32, 128, (3, 3, 3), (1, 1, 1), (1, 1, 1), _PAIR, True),
+    ("f16", 1, 64, 8, 32, 64, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), _PAIR | _MT2, True),
+    ("bf16", 1, 96, 4, 8, 32, 128, (3, 3, 3), (1, 1, 1), (1, 1, 1), _PAIR | _MT2, False),
+    ("f16", 1, 40, 3, 9, 16, 64, (3, 1, 3), (1, 0, 1), (1, 1, 1), _PAIR, False),
+])
+def test_conv3d_cta_pairs(cuda, dt, N, Cin, D, H, W, Cout, k, p, dil, variant, cl):
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(Cin * 5 + Cout + H)
+    x = torch.randn(N, Cin, D, H, W, generator=g).to(torch_dtype(dt))
+    w = _kaiming((Cout, Cin) + k, g).to(torch_dtype(dt))
+    b = torch.randn(Cout, generator=g).to(torch_dtype(dt)) * 0.1
+    ref = torch.nn.functional.conv3d(x.float(), w.float(), b.float(), padding=p, dilation=dil)
+    xin = x.permute(0, 2, 3, 4, 1).contiguous() if cl else x
+    y = ops.conv3d(xin.to(cuda), w.to(cuda), b.to(cuda), (1, 1, 1), p, dil, variant=variant,
+                   x_channels_last=cl, out_channels_last=cl)
+    assert y is not None
+    y0 = ops.conv3d(xin.to(cuda), w.to(cuda), b.to(cuda), (1, 1, 1), p, dil,
+                    x_channels_last=cl, out_channels_last=cl)
+    torch.cuda.synchronize()
+    if cl:
+        y, y0 = y.permute(0, 4, 1, 2, 3), y0.permute(0, 4, 1, 2, 3)
+    assert tuple(y.shape) == tuple(ref.shape)
+    assert oracle.rel_l2(_np(y), ref.numpy()) <= TOL[dt]
+    assert oracle.rel_l2(_np(y), _np(y0)) <= 1e-3      # same op as the unpaired kernel
+    _no_fault()
+
+
 # NCDHW input with the channels-last transposition fused into the kernel
 # (variant bit 14; the default is a separate transposition): same results on
 # shapes with W % 8 == 0, padding / dilation along W, a partial channel chunk,
