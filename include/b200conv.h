@@ -181,6 +181,15 @@ int b200_fftconv1d_prepare(const void* w, void* spectrum, int w_dtype, int64_t C
 int b200_fftconv1d_fwd(const void* x, const void* spectrum, const void* bias, void* y,
                        int dtype, int bias_dtype, int64_t B, int64_t C, int64_t L,
                        int64_t pad, int64_t L_out, int64_t nfft, void* stream);
+/* Overlap-save form: the row is cut into segments of nfft - K + 1 outputs,
+ * each one transform of length nfft >= K over inputs [start - pad, + nfft)
+ * (one CTA per channel, row pair and segment); spectrum from
+ * b200_fftconv1d_prepare with the same nfft.  L_out = L + 2*pad - K + 1.
+ * Same result as b200_fftconv1d_fwd (same fft_conv semantics), with short
+ * transforms that several CTAs per SM can hold. */
+int b200_fftconv1d_fwd_os(const void* x, const void* spectrum, const void* bias, void* y,
+                          int dtype, int bias_dtype, int64_t B, int64_t C, int64_t L, int64_t K,
+                          int64_t pad, int64_t L_out, int64_t nfft, void* stream);
 
 /* Dense (groups = 1) conv3d through the FFT for large kernels:
  * rfft3(x) . conj(rfft3(w)) summed over Cin per frequency bin, irfft3,

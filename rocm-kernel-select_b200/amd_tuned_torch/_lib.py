@@ -62,6 +62,8 @@ SIGNATURES = {
     "b200_fftconv1d_prepare": (c_int, [c_vp, c_vp, c_int, c_int64, c_int64, c_int64, c_vp]),
     "b200_fftconv1d_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 6
                            + [c_vp]),
+    "b200_fftconv1d_fwd_os": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 7
+                              + [c_vp]),
     "b200_fftconv3d_spectrum_bytes": (c_size_t, [c_int64] * 5 + [c_int]),
     "b200_fftconv3d_prepare": (c_int, [c_vp, c_vp, c_int] + [c_int64] * 8
                                + [c_vp, c_size_t, c_vp]),

@@ -34,18 +34,18 @@ size_t fft1d_smem(int n) {
   return static_cast<size_t>(fft::kLo + nhi + fft::padded_len(n)) * sizeof(float2);
 }
 
-// Forward pass 0 (span n, stride n/R) fed straight from the two input rows
-// (zero outside [0, L) after shifting by `pad`).
+// Forward pass 0 (span n, stride n/R) fed straight from the two input rows:
+// transform position i holds input position q0 + i (zero outside [0, L)).
 template <typename T, int R>
 __device__ __forceinline__ void first_pass_from_rows(float2* buf, int n, const float2* tw0,
                                                      const T* x0, const T* x1, bool has1,
-                                                     int64_t pad, int64_t L) {
+                                                     int64_t q0, int64_t L) {
   const int stride = n / R;
   for (int k = threadIdx.x; k < stride; k += blockDim.x) {
     float2 v[R];
 #pragma unroll
     for (int m = 0; m < R; ++m) {
-      const int64_t l = static_cast<int64_t>(k + m * stride) - pad;
+      const int64_t l = static_cast<int64_t>(k + m * stride) + q0;
       const bool in = l >= 0 && l < L;
       v[m] = make_float2(in ? to_f32(x0[l]) : 0.f, (in && has1) ? to_f32(x1[l]) : 0.f);
     }
@@ -77,12 +77,14 @@ __device__ __forceinline__ void last_fwd_product_first_inv(float2* buf, int n,
   }
 }
 
-// Inverse pass 0 (span n) written straight to the two output rows: crop to
-// L_out, scale 1/n, + bias, dtype conversion.
+// Inverse pass 0 (span n) written straight to the two output rows:
+// transform position i < vlen is output position o0 + i (cropped to L_out),
+// scale 1/n, + bias, dtype conversion.
 template <typename T, int R>
 __device__ __forceinline__ void last_pass_to_rows(const float2* buf, int n, const float2* tw0,
-                                                  T* y0, T* y1, bool has1, int64_t Lout,
-                                                  float scale, float bv) {
+                                                  T* y0, T* y1, bool has1, int64_t o0,
+                                                  int64_t vlen, int64_t Lout, float scale,
+                                                  float bv) {
   const int stride = n / R;
   for (int k = threadIdx.x; k < stride; k += blockDim.x) {
     float2 v[R];
@@ -92,8 +94,8 @@ __device__ __forceinline__ void last_pass_to_rows(const float2* buf, int n, cons
     fft::Dft<R, true>::run(v);
 #pragma unroll
     for (int m = 0; m < R; ++m) {
-      const int64_t l = k + m * stride;
-      if (l < Lout) {
+      const int64_t i = k + m * stride, l = o0 + i;
+      if (i < vlen && l < Lout) {
         y0[l] = from_f32<T>(fmaf(v[m].x, scale, bv));
         if (has1) y1[l] = from_f32<T>(fmaf(v[m].y, scale, bv));
       }
@@ -112,20 +114,27 @@ __device__ __forceinline__ void last_pass_to_rows(const float2* buf, int n, cons
     default: CALL(5); break;           \
   }
 
-template <typename T>
-__global__ void __launch_bounds__(kFftThreads, 1)
+// One CTA per (channel, row pair, segment).  Segment s of seg_len outputs
+// (overlap-save): the transform holds inputs [s * seg_len - pad, + n) and its
+// first seg_len circular-correlation outputs are exact when
+// seg_len <= n - K + 1.  One segment covering L_out = the whole padded row.
+template <typename T, int THREADS>
+__global__ void __launch_bounds__(THREADS, THREADS >= 512 ? 1 : 2)
 fftconv1d_kernel(const T* __restrict__ x, const float2* __restrict__ spec,
                  const void* __restrict__ bias, int bias_dt, T* __restrict__ y, int64_t B,
-                 int64_t C, int64_t L, int64_t pad, int64_t Lout, const fft::Plan plan,
-                 int tw_count) {
+                 int64_t C, int64_t L, int64_t pad, int64_t Lout, int64_t seg_len, int64_t segs,
+                 const fft::Plan plan, int tw_count) {
   extern __shared__ float2 sm[];
   const int n = plan.n;
   float2* tw = sm;
   float2* buf = tw + ((tw_count + 1) & ~1);
 
   const int64_t pairs = (B + 1) / 2;
-  const int64_t c = blockIdx.x / pairs;
-  const int64_t b0 = 2 * (blockIdx.x % pairs), b1 = b0 + 1;
+  const int64_t seg = blockIdx.x % segs;
+  const int64_t rest = blockIdx.x / segs;
+  const int64_t c = rest / pairs;
+  const int64_t b0 = 2 * (rest % pairs), b1 = b0 + 1;
+  const int64_t o0 = seg * seg_len;
   const bool has1 = b1 < B;
   const T* x0 = x + (b0 * C + c) * L;
   const T* x1 = x + (min64(b1, B - 1) * C + c) * L;
@@ -147,7 +156,7 @@ fftconv1d_kernel(const T* __restrict__ x, const float2* __restrict__ spec,
   }
   const int P = plan.passes;
 
-#define B200_FIRST(R) first_pass_from_rows<T, R>(buf, n, tw, x0, x1, has1, pad, L)
+#define B200_FIRST(R) first_pass_from_rows<T, R>(buf, n, tw, x0, x1, has1, o0 - pad, L)
   B200_FFT_RADIX_SWITCH(plan.radix[0], B200_FIRST)
 #undef B200_FIRST
   __syncthreads();
@@ -166,7 +175,8 @@ fftconv1d_kernel(const T* __restrict__ x, const float2* __restrict__ spec,
   }
   const float scale = 1.0f / static_cast<float>(n);
   const float bv = bias ? load_param(bias, bias_dt, c) : 0.f;
-#define B200_LAST(R) last_pass_to_rows<T, R>(buf, n, tw, y0, y1, has1, Lout, scale, bv)
+#define B200_LAST(R) \
+  last_pass_to_rows<T, R>(buf, n, tw, y0, y1, has1, o0, seg_len, Lout, scale, bv)
   B200_FFT_RADIX_SWITCH(plan.radix[0], B200_LAST)
 #undef B200_LAST
 }
@@ -216,6 +226,51 @@ int prep_smem(K kern, size_t smem) {
   return B200_OK;
 }
 
+// Short transforms (segments) run as CTAs of 256 threads, two per SM; the
+// whole-row transform as one 512-thread CTA per SM.
+template <typename T, int THREADS>
+int launch_fftconv1d_t(const T* x, const float2* sp, const void* bias, int bias_dt, T* y,
+                       int64_t B, int64_t C, int64_t L, int64_t pad, int64_t Lout,
+                       int64_t seg_len, int64_t segs, const fft::Plan& plan, cudaStream_t s) {
+  const int twc = host_tw_count(plan);
+  const size_t smem =
+      static_cast<size_t>(((twc + 1) & ~1) + fft::padded_len(plan.n)) * sizeof(float2);
+  int rc;
+  if ((rc = prep_smem(fftconv1d_kernel<T, THREADS>, smem)) != B200_OK) return rc;
+  const int64_t blocks = C * ((B + 1) / 2) * segs;
+  fftconv1d_kernel<T, THREADS><<<static_cast<unsigned>(blocks), THREADS, smem, s>>>(
+      x, sp, bias, bias_dt, y, B, C, L, pad, Lout, seg_len, segs, plan, twc);
+  B200_LAUNCH_CHECK("fftconv1d_kernel");
+  return B200_OK;
+}
+
+template <typename T>
+int launch_fftconv1d_typed(const void* x, const void* spectrum, const void* bias, int bias_dt,
+                           void* y, int64_t B, int64_t C, int64_t L, int64_t pad, int64_t Lout,
+                           int64_t seg_len, int64_t segs, const fft::Plan& plan, cudaStream_t s) {
+  const T* xt = static_cast<const T*>(x);
+  T* yt = static_cast<T*>(y);
+  const float2* sp = static_cast<const float2*>(spectrum);
+  if (plan.n <= 8192)
+    return launch_fftconv1d_t<T, 256>(xt, sp, bias, bias_dt, yt, B, C, L, pad, Lout, seg_len,
+                                      segs, plan, s);
+  return launch_fftconv1d_t<T, kFftThreads>(xt, sp, bias, bias_dt, yt, B, C, L, pad, Lout,
+                                            seg_len, segs, plan, s);
+}
+
+int launch_fftconv1d(const void* x, const void* spectrum, const void* bias, void* y, int dtype,
+                     int bias_dt, int64_t B, int64_t C, int64_t L, int64_t pad, int64_t Lout,
+                     int64_t seg_len, int64_t segs, const fft::Plan& plan, cudaStream_t s) {
+  if (dtype == B200_DTYPE_F32)
+    return launch_fftconv1d_typed<float>(x, spectrum, bias, bias_dt, y, B, C, L, pad, Lout,
+                                         seg_len, segs, plan, s);
+  if (dtype == B200_DTYPE_F16)
+    return launch_fftconv1d_typed<__half>(x, spectrum, bias, bias_dt, y, B, C, L, pad, Lout,
+                                          seg_len, segs, plan, s);
+  return launch_fftconv1d_typed<__nv_bfloat16>(x, spectrum, bias, bias_dt, y, B, C, L, pad,
+                                               Lout, seg_len, segs, plan, s);
+}
+
 }  // namespace
 }  // namespace b200
 
@@ -260,6 +315,25 @@ int b200_fftconv1d_prepare(const void* w, void* spectrum, int w_dtype, int64_t C
   return B200_OK;
 }
 
+int b200_fftconv1d_fwd_os(const void* x, const void* spectrum, const void* bias, void* y,
+                          int dtype, int bias_dtype, int64_t B, int64_t C, int64_t L, int64_t K,
+                          int64_t pad, int64_t L_out, int64_t nfft, void* stream) {
+  if (!x || !spectrum || !y) return fail_arg("NULL pointer");
+  if (!dtype_ok(dtype) || (bias && !dtype_ok(bias_dtype))) return fail_arg("bad dtype");
+  if (B <= 0 || C <= 0 || L <= 0 || K <= 0 || pad < 0 || L_out <= 0) return fail_arg("bad size");
+  if (L_out != L + 2 * pad - K + 1) return fail_arg("L_out != L + 2 * pad - K + 1");
+  fft::Plan plan;
+  if (!plan1d(nfft, &plan)) return fail_unsupported("FFT length not 2^a 3^b 5^c or too long");
+  if (K > nfft) return fail_arg("nfft shorter than the filter");
+  if (plan.passes < 2) return fail_unsupported("FFT length too short for the fused kernel");
+  const int64_t seg_len = nfft - K + 1;
+  const int64_t segs = (L_out + seg_len - 1) / seg_len;
+  const int64_t blocks = C * ((B + 1) / 2) * segs;
+  if (blocks > 0x7fffffffLL) return fail_unsupported("grid too large");
+  return launch_fftconv1d(x, spectrum, bias, y, dtype, bias_dtype, B, C, L, pad, L_out, seg_len,
+                          segs, plan, static_cast<cudaStream_t>(stream));
+}
+
 int b200_fftconv1d_fwd(const void* x, const void* spectrum, const void* bias, void* y,
                        int dtype, int bias_dtype, int64_t B, int64_t C, int64_t L,
                        int64_t pad, int64_t L_out, int64_t nfft, void* stream) {
@@ -273,30 +347,8 @@ int b200_fftconv1d_fwd(const void* x, const void* spectrum, const void* bias, vo
   const int64_t blocks = C * ((B + 1) / 2);
   if (blocks > 0x7fffffffLL) return fail_unsupported("grid too large");
   if (plan.passes < 2) return fail_unsupported("FFT length too short for the fused kernel");
-  const int twc = host_tw_count(plan);
-  const size_t smem =
-      static_cast<size_t>(((twc + 1) & ~1) + fft::padded_len(plan.n)) * sizeof(float2);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const float2* sp = static_cast<const float2*>(spectrum);
-  int rc;
-  if (dtype == B200_DTYPE_F32) {
-    if ((rc = prep_smem(fftconv1d_kernel<float>, smem)) != B200_OK) return rc;
-    fftconv1d_kernel<float><<<(unsigned)blocks, kFftThreads, smem, s>>>(
-        static_cast<const float*>(x), sp, bias, bias_dtype, static_cast<float*>(y), B, C, L, pad,
-        L_out, plan, twc);
-  } else if (dtype == B200_DTYPE_F16) {
-    if ((rc = prep_smem(fftconv1d_kernel<__half>, smem)) != B200_OK) return rc;
-    fftconv1d_kernel<__half><<<(unsigned)blocks, kFftThreads, smem, s>>>(
-        static_cast<const __half*>(x), sp, bias, bias_dtype, static_cast<__half*>(y), B, C, L,
-        pad, L_out, plan, twc);
-  } else {
-    if ((rc = prep_smem(fftconv1d_kernel<__nv_bfloat16>, smem)) != B200_OK) return rc;
-    fftconv1d_kernel<__nv_bfloat16><<<(unsigned)blocks, kFftThreads, smem, s>>>(
-        static_cast<const __nv_bfloat16*>(x), sp, bias, bias_dtype,
-        static_cast<__nv_bfloat16*>(y), B, C, L, pad, L_out, plan, twc);
-  }
-  B200_LAUNCH_CHECK("fftconv1d_kernel");
-  return B200_OK;
+  return launch_fftconv1d(x, spectrum, bias, y, dtype, bias_dtype, B, C, L, pad, L_out, L_out, 1,
+                          plan, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -61,6 +61,35 @@ def test_fftconv1d_shapes(cuda, B, C, L, K, pad, dt):
     assert oracle.rel_l2(_np(y), ref) <= tol
 
 
+# Overlap-save segments (b200_fftconv1d_fwd_os) against the whole-row
+# transform and the float64 oracle: several segments with a ragged last one,
+# pad 0 / pad > K, an odd batch, and a row longer than one transform holds.
+@pytest.mark.parametrize("B,C,L,K,pad,nfft,dt", [
+    (3, 2, 20000, 1000, 500, 4096, "f32"), (2, 3, 9000, 257, 0, 2048, "bf16"),
+    (1, 2, 5000, 100, 300, 1024, "f16"), (2, 2, 40000, 2048, 1024, 8192, "f16"),
+])
+def test_fftconv1d_overlap_save(cuda, B, C, L, K, pad, nfft, dt):
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(L + K + nfft)
+    x = torch.randn(B, C, L, generator=g).to(torch_dtype(dt))
+    w = _kaiming((C, 1, K), g).to(torch_dtype(dt))
+    b = torch.randn(C, generator=g).to(torch_dtype(dt))
+    y = ops.fftconv1d(x.to(cuda), w.to(cuda), b.to(cuda), pad, nfft, segmented=True)
+    assert y is not None and tuple(y.shape) == (B, C, L + 2 * pad - K + 1)
+    ref = oracle.fft_conv_np(x.float().numpy(), w.float().numpy(), b.float().numpy(), (pad,),
+                             groups=C)
+    tol = 1e-5 if dt == "f32" else FFT_TOL
+    assert oracle.rel_l2(_np(y), ref) <= tol
+    assert ops.read_device_flags() == 0
+
+
+def test_fftconv1d_plan_choice():
+    from amd_tuned_torch import fftconv_ops
+    assert fftconv_ops.fftconv1d_plan(16384, 2048, 1024) == (8192, True)    # cfg 4b
+    assert fftconv_ops.fftconv1d_plan(4000, 64, 0) == (4000, False)
+    assert fftconv_ops.fftconv1d_plan(60000, 257, 128)[1] is True           # too long for one
+
+
 def test_fftconv1d_cfg4b_full_size(cuda):
     """BASELINE cfg 4b: x[16,1024,16384] fp16 ~N(0,1), w[1024,1,2048] kaiming-U,
     bias, groups 1024, padding 1024 -> L_out 16385.  Checked on a slice of
