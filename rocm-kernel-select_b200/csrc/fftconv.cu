@@ -119,7 +119,7 @@ __device__ __forceinline__ void last_pass_to_rows(const float2* buf, int n, cons
 // first seg_len circular-correlation outputs are exact when
 // seg_len <= n - K + 1.  One segment covering L_out = the whole padded row.
 template <typename T, int THREADS>
-__global__ void __launch_bounds__(THREADS, THREADS >= 512 ? 1 : 2)
+__global__ void __launch_bounds__(THREADS, THREADS >= 512 ? 1 : 3)
 fftconv1d_kernel(const T* __restrict__ x, const float2* __restrict__ spec,
                  const void* __restrict__ bias, int bias_dt, T* __restrict__ y, int64_t B,
                  int64_t C, int64_t L, int64_t pad, int64_t Lout, int64_t seg_len, int64_t segs,
@@ -226,7 +226,8 @@ int prep_smem(K kern, size_t smem) {
   return B200_OK;
 }
 
-// Short transforms (segments) run as CTAs of 256 threads, two per SM; the
+// Short transforms (segments) run as CTAs of 256 threads, three per SM (80
+// registers; an 8192-point segment takes ~70 KB of shared memory); the
 // whole-row transform as one 512-thread CTA per SM.
 template <typename T, int THREADS>
 int launch_fftconv1d_t(const T* x, const float2* sp, const void* bias, int bias_dt, T* y,
