@@ -30,6 +30,10 @@ namespace b200 {
 namespace {
 
 constexpr int kThreads = 256;
+// Residency: the transforms run three CTAs per SM (<= 85 registers; a few
+// spilled bytes), the contraction two (<= 128 registers): at the unbounded
+// register counts (90-147) they ran one or two, too few warps to hide shared-
+// memory and HBM latency (cfg4a 1.10 -> 0.93 ms on one box).
 constexpr int kMaxDim = 256;
 constexpr int kCols = 4;   // transform columns per depth-FFT CTA
 
@@ -144,7 +148,7 @@ __device__ __forceinline__ void bfft(float2* buf, const fft::Plan& p, int nseq, 
 // Output G[p][c][dz][Fh][Fw] complex, natural order.  Placement offset
 // (oh, ow) of the real data inside the transform plane.
 template <typename T>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
 plane_fwd_kernel(const T* __restrict__ x, float2* __restrict__ G, int64_t n_items, int64_t item0,
                  int C, int Dz, int H, int W, int oh, int ow, const Plan3 pl) {
   extern __shared__ float2 sm[];
@@ -189,7 +193,7 @@ plane_fwd_kernel(const T* __restrict__ x, float2* __restrict__ G, int64_t n_item
 
 // --------------------------------------------------------------- K2 -----
 // G[p][c][dz][Fh*Fw] (Dz planes at depth offset od) -> Z[bin][p][c].
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
 depth_fwd_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, int C, int Dz,
                  int od, const Plan3 pl) {
   extern __shared__ float2 sm[];
@@ -257,7 +261,7 @@ __device__ __forceinline__ void spec_put(float2* o, float a, float b) { *o = mak
 __device__ __forceinline__ void spec_put(__half2* o, float a, float b) { *o = __floats2half2_rn(a, b); }
 
 template <typename S>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
 contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
                 const float* __restrict__ hdr, float2* __restrict__ U, int P, int Cin, int Cout,
                 int Fd, int Fh, int Fw, int64_t hbins) {
@@ -347,7 +351,7 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
 
 // --------------------------------------------------------------- K4 -----
 // U[bin][p][co] -> G2[p][co][od < Do][Fh*Fw] (inverse depth FFT).
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
 depth_inv_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int P, int C, int Do,
                  const Plan3 pl) {
   extern __shared__ float2 sm[];
@@ -390,7 +394,7 @@ depth_inv_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int P, i
 // G2[p][co][od][Fh*Fw] -> y[n][co][od][Ho][Wo] (inverse plane FFT, crop,
 // scale, bias).
 template <typename T>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
 plane_inv_kernel(const float2* __restrict__ G2, T* __restrict__ y, const void* __restrict__ bias,
                  int bias_dt, int64_t N, int C, int Do, int Ho, int Wo, float scale,
                  const Plan3 pl) {
