@@ -177,9 +177,11 @@ def _conv3d_candidates(input, weight, bias, stride, padding, dilation, groups):
 
 def _conv3d_accelerated_forward(input, weight, bias, stride, padding, dilation, groups):
     orig = _ORIGINALS[(F, "conv3d")]
-    if groups != 1 or not _usable(input, weight, bias, dtypes=_FFTCONV_CONV_DTYPES):
+    if (groups != 1 or not _usable(input, weight, bias, dtypes=_FFTCONV_CONV_DTYPES)
+            or input.numel() == 0 or weight.numel() == 0):
         if _DEBUG:
-            _debug("conv3d", "stock", "groups != 1 or not a plain CUDA fp tensor", input=input)
+            _debug("conv3d", "stock", "groups != 1, empty, or not a plain CUDA fp tensor",
+                   input=input)
         return orig(input, weight, bias, stride, padding, dilation, groups)
     if kernel_select.enabled():
         won = kernel_select.cached(_CONV3D_KIND, input, weight, stride, padding, dilation)
@@ -275,7 +277,7 @@ def _group_norm_candidates(input, num_groups, weight, bias, eps):
 def _group_norm_accelerated_forward(input, num_groups, weight, bias, eps):
     orig = _ORIGINALS[(F, "group_norm")]
     if (input.dim() < 2 or input.shape[1] % num_groups != 0 or not input.is_contiguous()
-            or not _usable(input, weight, bias, dtypes=_GROUPNORM_DTYPES)):
+            or input.numel() == 0 or not _usable(input, weight, bias, dtypes=_GROUPNORM_DTYPES)):
         if _DEBUG:
             _debug("group_norm", "stock", "layout/dtype outside this tier", input=input)
         return orig(input, num_groups, weight, bias, eps)

@@ -50,6 +50,8 @@ def _try_fftconv1d_fastpath(input, weight, bias, stride, padding, dilation, grou
     applies (the caller then calls stock directly)."""
     if not input.is_cuda or not _lib.available() or isinstance(_scalar(padding), str):
         return None
+    if input.numel() == 0 or weight.numel() == 0:   # empty: stock's own result
+        return None
     depthwise = (depthwise_conv1d_ops.available()
                  and _is_depthwise_conv1d_eligible(input, weight, stride, dilation, groups))
     fft = (fftconv_ops.fft_conv1d_enabled()

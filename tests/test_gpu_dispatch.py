@@ -114,6 +114,27 @@ def test_dense_conv1d_and_cpu_tensors_go_to_stock(cuda, patched):
     torch.testing.assert_close(y.cpu(), torch.conv1d(x, w, None, 1, 1, 1, 1), rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("contest", [True, False])
+def test_empty_inputs_match_stock(cuda, patched, contest, monkeypatch):
+    """Empty batches (and an empty spatial extent) go to stock: same shapes,
+    no error, with the contest on and off."""
+    from amd_tuned_torch import kernel_select
+    monkeypatch.setattr(kernel_select, "_ENABLED", contest)
+    if True:
+        x1 = torch.randn(0, 16, 128, device=cuda, dtype=torch.float16)
+        w1 = torch.randn(16, 1, 3, device=cuda, dtype=torch.float16)
+        assert F.conv1d(x1, w1, padding=1, groups=16).shape == (0, 16, 128)
+        w1l = torch.randn(16, 1, 65, device=cuda, dtype=torch.float16)
+        assert F.conv1d(x1, w1l, padding=32, groups=16).shape == (0, 16, 128)
+        x3 = torch.randn(0, 64, 4, 8, 8, device=cuda, dtype=torch.float16)
+        w3 = torch.randn(64, 64, 3, 3, 3, device=cuda, dtype=torch.float16)
+        assert F.conv3d(x3, w3, padding=1).shape == (0, 64, 4, 8, 8)
+        xg = torch.randn(0, 64, 8, 8, device=cuda, dtype=torch.bfloat16)
+        assert F.group_norm(xg, 32).shape == (0, 64, 8, 8)
+        xs = torch.randn(2, 64, 0, device=cuda, dtype=torch.bfloat16)
+        assert F.group_norm(xs, 32).shape == (2, 64, 0)
+
+
 def test_disable_restores_stock(cuda):
     import amd_tuned_torch
     stock = (F.conv1d, F.conv3d, F.group_norm)
