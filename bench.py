@@ -336,6 +336,78 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         del xs, ys, y
         torch.cuda.empty_cache()
 
+    if only in (None, "cfg5block"):
+        # One cfg 5 block on one GPU, x[1,128,64,128,128] bf16: GroupNorm(32) ->
+        # SiLU -> Conv3d(128,128,3,p1) as nn.Sequential (patched: the fused
+        # GN+SiLU -> channels-last operand -> conv) vs the same three ops called
+        # one by one (patched F.group_norm, torch F.silu, patched F.conv3d).
+        import amd_tuned_torch
+        from amd_tuned_torch import conv_fusion_ops
+        g = torch.Generator().manual_seed(5)
+        torch.manual_seed(5)
+        blk = torch.nn.Sequential(torch.nn.GroupNorm(32, 128), torch.nn.SiLU(),
+                                  torch.nn.Conv3d(128, 128, 3, padding=1)).to(dev, torch.bfloat16)
+        blk.eval()
+        xs = [torch.randn(1, 128, 64, 128, 128, generator=g).bfloat16().to(dev) for _ in range(2)]
+        was = amd_tuned_torch.is_enabled()
+        amd_tuned_torch.enable()
+        try:
+            with torch.no_grad():
+                def fused(i):
+                    return conv_fusion_ops._fused_block(xs[i % 2], blk[0], blk[2])
+
+                def unfused(i):
+                    h = F.silu(F.group_norm(xs[i % 2], 32, blk[0].weight, blk[0].bias, blk[0].eps))
+                    return F.conv3d(h, blk[2].weight, blk[2].bias, padding=1)
+                ya, yb = fused(0), unfused(0)
+                err = _rel_l2(ya.float().cpu(), yb.float().cpu())
+                del ya, yb
+                for i in range(2):
+                    fused(i)
+                    unfused(i)
+                ms_f = _graph_time(fused, 4, stream)
+                ms_u = _graph_time(unfused, 4, stream)
+        finally:
+            if not was:
+                amd_tuned_torch.disable()
+        out["cfg5_block_gn_silu_conv3d_bf16"] = {
+            "fused_us": ms_f * 1e3, "unfused_us": ms_u * 1e3, "rel_l2_fused_vs_unfused": err,
+            "note": "fused: GN statistics + GN/SiLU written channels-last + conv on it; "
+                    "unfused: GN (NCDHW) + SiLU + conv3d (its own channels-last transpose)"}
+        del xs
+        torch.cuda.empty_cache()
+
+    if only in (None, "conv2d"):
+        # conv2d route (F.conv2d as a depth-1 conv3d on the same tcgen05 kernel)
+        # at an SD-VAE decoder shape: x[1,512,128,128] bf16 * w[512,512,3,3] p1,
+        # against stock torch (cuDNN) on the same inputs.
+        g = torch.Generator().manual_seed(9)
+        w2 = _kaiming((512, 512, 3, 3), g).bfloat16().to(dev)
+        b2 = (torch.randn(512, generator=g) * 0.1).bfloat16().to(dev)
+        xs = [torch.randn(1, 512, 128, 128, generator=g).bfloat16().to(dev) for _ in range(2)]
+        from amd_tuned_torch.conv_fusion_ops import _weight5
+        w5 = _weight5(w2)
+
+        def ours(i):
+            return ops.conv3d(xs[i % 2].unsqueeze(2), w5, b2, (1, 1, 1), (0, 1, 1),
+                              (1, 1, 1)).squeeze(2)
+
+        def stock(i):
+            return torch.conv2d(xs[i % 2], w2, b2, 1, 1, 1, 1)
+        err = _rel_l2(ours(0).float().cpu(), stock(0).float().cpu())
+        for i in range(2):
+            ours(i)
+            stock(i)
+        ms_o = _graph_time(ours, 10, stream)
+        ms_s = _graph_time(stock, 10, stream)
+        flop = 2.0 * 128 * 128 * 512 * 512 * 9
+        out["conv2d_sdvae_bf16"] = {"us_per_op": ms_o * 1e3, "stock_us_per_op": ms_s * 1e3,
+                                    "tflops": flop / (ms_o * 1e-3) / 1e12,
+                                    "frac": flop / (ms_o * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                                    "rel_l2_vs_stock": err}
+        del xs
+        torch.cuda.empty_cache()
+
     if only in (None, "cfg4b"):
         # cfg4b: long-filter depthwise conv1d fp16 [16,1024,16384] k2048 p1024 (FFT route)
         g = torch.Generator().manual_seed(44)
@@ -622,7 +694,9 @@ def main() -> int:
     ap.add_argument("--no-stack", action="store_true")
     ap.add_argument("--stack-exchange", choices=("peer", "nccl"), default="peer",
                     help="cfg5 at N > 1: peer-memory exchange or NCCL collectives")
-    ap.add_argument("--only", choices=("cfg1", "cfg3", "cfg4a", "cfg4b", "cfg5conv"), default=None,
+    ap.add_argument("--only", choices=("cfg1", "cfg3", "cfg4a", "cfg4b", "cfg5conv", "cfg5block",
+                                       "conv2d"),
+                    default=None,
                     help="time one per-shape config alone (profiling target), one GPU")
     ap.add_argument("--small", action="store_true", help="with --only cfg4b: 64 channels")
     args = ap.parse_args()

@@ -114,6 +114,56 @@ def test_dense_conv1d_and_cpu_tensors_go_to_stock(cuda, patched):
     torch.testing.assert_close(y.cpu(), torch.conv1d(x, w, None, 1, 1, 1, 1), rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("N,C,H,W,Co,k,p,d,dt,cl", [
+    (1, 64, 32, 32, 64, 3, 1, 1, torch.float16, False),
+    (2, 128, 24, 40, 96, 3, 1, 1, torch.bfloat16, False),
+    (1, 64, 33, 17, 64, 3, 2, 2, torch.float16, False),
+    (2, 32, 16, 16, 64, (3, 5), (1, 2), 1, torch.bfloat16, True),
+    (1, 40, 20, 20, 48, 3, 0, 1, torch.float16, False),
+])
+@pytest.mark.parametrize("contest", [False, True])
+def test_conv2d_through_patch(cuda, patched, monkeypatch, N, C, H, W, Co, k, p, d, dt, cl, contest):
+    """Contest off: the tcgen05 route runs first and must meet the 2e-3 bar.
+    Contest on: whichever candidate wins (stock cuDNN included) within one
+    bf16 ulp (3.9e-3)."""
+    from amd_tuned_torch import kernel_select
+    monkeypatch.setattr(kernel_select, "_ENABLED", contest)
+    g = torch.Generator().manual_seed(C + Co + H)
+    x = torch.randn(N, C, H, W, generator=g).to(dt)
+    kk = (k, k) if isinstance(k, int) else k
+    w = (torch.rand(Co, C, *kk, generator=g) * 2 - 1) / math.sqrt(C * kk[0] * kk[1])
+    w = w.to(dt)
+    b = (torch.randn(Co, generator=g) * 0.1).to(dt)
+    xd = x.to(cuda)
+    if cl:
+        xd = xd.contiguous(memory_format=torch.channels_last)
+    y = F.conv2d(xd, w.to(cuda), b.to(cuda), padding=p, dilation=d)
+    ref = torch.nn.functional.conv2d(x.float(), w.float(), b.float(), padding=p, dilation=d)
+    assert tuple(y.shape) == tuple(ref.shape)
+    assert oracle.rel_l2(_np(y), ref.numpy()) <= (3.9e-3 if contest else 2e-3)
+
+
+def test_conv2d_stock_routes_and_backward(cuda, patched):
+    x = torch.randn(2, 64, 16, 16, device=cuda, dtype=torch.float16)
+    wg = torch.randn(64, 32, 3, 3, device=cuda, dtype=torch.float16) * 0.05
+    assert F.conv2d(x, wg, padding=1, groups=2).shape == (2, 64, 16, 16)   # grouped -> stock
+    w1 = torch.randn(32, 64, 1, 1, device=cuda, dtype=torch.float16) * 0.1
+    assert F.conv2d(x, w1).shape == (2, 32, 16, 16)                      # pointwise -> stock
+    xr = torch.randn(1, 64, 12, 12, device=cuda, dtype=torch.float32, requires_grad=True)
+    wr = (torch.randn(64, 64, 3, 3, device=cuda) * 0.05).requires_grad_()
+    xh, wh = xr.half(), wr.half()
+    F.conv2d(xh, wh, padding=1).float().square().sum().backward()
+    gx, gw = xr.grad.clone(), wr.grad.clone()
+    xr.grad = None
+    wr.grad = None
+    import amd_tuned_torch
+    amd_tuned_torch.disable()
+    F.conv2d(xr.half(), wr.half(), padding=1).float().square().sum().backward()
+    amd_tuned_torch.enable()
+    assert oracle.rel_l2(_np(gx), _np(xr.grad)) <= 1e-2
+    assert oracle.rel_l2(_np(gw), _np(wr.grad)) <= 1e-2
+
+
 @pytest.mark.parametrize("contest", [True, False])
 def test_empty_inputs_match_stock(cuda, patched, contest, monkeypatch):
     """Empty batches (and an empty spatial extent) go to stock: same shapes,
