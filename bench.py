@@ -390,7 +390,7 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
 
         def ours(i):
             return ops.conv3d(xs[i % 2].unsqueeze(2), w5, b2, (1, 1, 1), (0, 1, 1),
-                              (1, 1, 1)).squeeze(2)
+                              (1, 1, 1), weight_key=w2).squeeze(2)
 
         def stock(i):
             return torch.conv2d(xs[i % 2], w2, b2, 1, 1, 1, 1)

@@ -280,6 +280,7 @@ def _conv2d_tc_thunk(input, weight, bias, stride, padding, dilation):
             return None
         p2, d2 = _pair(padding), _pair(dilation)
         out = ops.conv3d(x, _weight5(weight), bias, (1, 1, 1), (0,) + p2, (1,) + d2,
+                         weight_key=weight,
                          x_channels_last=cl, out_channels_last=cl)
         if out is None:
             return None

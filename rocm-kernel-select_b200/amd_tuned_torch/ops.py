@@ -255,9 +255,13 @@ def depthwise_conv1d(x: torch.Tensor, weight2d: torch.Tensor, bias: Optional[tor
 
 
 # --------------------------------------------------------------- conv3d ---
-def conv3d_packed_weight(w: torch.Tensor) -> torch.Tensor:
-    """[Cout, Cin, KD, KH, KW] -> packed K-major GEMM operand (cached)."""
-    hit = _packed_weights.get(w)
+def conv3d_packed_weight(w: torch.Tensor, key: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[Cout, Cin, KD, KH, KW] -> packed K-major GEMM operand, cached on `key`
+    (default: w itself).  A caller that passes a fresh view of a longer-lived
+    tensor (a conv2d weight seen as depth 1) keys on that tensor instead, so
+    the cache hits on every call."""
+    key = w if key is None else key
+    hit = _packed_weights.get(key)
     if hit is not None:
         return hit
     L = _lib.lib()
@@ -268,7 +272,7 @@ def conv3d_packed_weight(w: torch.Tensor) -> torch.Tensor:
                                    Cout, Cin, KD, KH, KW, _stream(w.device))
     if not _lib.check(rc, "b200_conv3d_pack_weight"):
         raise _lib.NativeError("conv3d weight packing declined")
-    _packed_weights.put(w, (), wp)
+    _packed_weights.put(key, (), wp)
     return wp
 
 
@@ -276,12 +280,15 @@ def conv3d(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
            stride: Sequence[int], padding: Sequence[int], dilation: Sequence[int],
            variant: int = 0, x_channels_last: bool = False,
            out_channels_last: bool = False, out: Optional[torch.Tensor] = None,
-           gate: Optional[Sequence[int]] = None) -> Optional[torch.Tensor]:
+           gate: Optional[Sequence[int]] = None,
+           weight_key: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
     """Dense conv3d on tensor cores.  x NCDHW (or [N, D, H, W, C] contiguous
     when x_channels_last), w [Cout, Cin, KD, KH, KW].  Returns NCDHW, or an
     [N, Do, Ho, Wo, Cout] contiguous tensor when out_channels_last.
     gate = (epoch, lo, hi, scale) device addresses (lo/hi may be 0) for
-    b200_conv3d_fwd_gated: the edge output frames wait for halo arrivals."""
+    b200_conv3d_fwd_gated: the edge output frames wait for halo arrivals.
+    weight_key: the tensor the packed-weight cache is keyed on when w is a
+    per-call view of it (conv2d weights seen as depth 1)."""
     key = (x.shape, x.dtype, w.shape, w.dtype, tuple(stride), tuple(padding), tuple(dilation),
            variant, x_channels_last, out_channels_last)
     plan = _conv_plans.get(key)
@@ -293,7 +300,7 @@ def conv3d(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
     dims, out_shape, prm, wsb, dcode = plan
     if not x.is_contiguous():
         x = x.contiguous()
-    wp = conv3d_packed_weight(w)
+    wp = conv3d_packed_weight(w, weight_key)
     if bias is not None and not bias.is_contiguous():
         bias = bias.contiguous()
     dev = x.device

@@ -11,6 +11,8 @@ import amd_tuned_torch
 from amd_tuned_torch import _dispatch, conv1d_dispatch, kernel_select, ops
 
 STOCK = (F.conv1d, F.conv3d, F.group_norm)
+STOCK_CONV2D = F.conv2d
+STOCK_SEQ_FORWARD = torch.nn.Sequential.forward
 
 
 @pytest.fixture
@@ -33,7 +35,7 @@ def force_eligible(monkeypatch):
         return STOCK[2](x, G, w, b, eps)
 
     def fake_conv3d(x, w, b, stride, padding, dilation, variant=0, x_channels_last=False,
-                    out_channels_last=False, out=None):
+                    out_channels_last=False, out=None, gate=None, weight_key=None):
         calls.append(("conv3d", x_channels_last))
         if x_channels_last:
             x = x.permute(0, 4, 1, 2, 3)
@@ -55,11 +57,45 @@ def test_enable_disable_install_set():
         assert getattr(F.conv1d, "_amd_tuned_torch_wrapper", False)
         amd_tuned_torch.enable()                    # idempotent
         assert F.conv3d is _dispatch._patched_conv3d
+        assert F.conv2d is _dispatch._patched_conv2d
+        assert torch.nn.Sequential.forward is _dispatch._patched_sequential_forward
     finally:
         amd_tuned_torch.disable()
     assert (F.conv1d, F.conv3d, F.group_norm) == STOCK
+    assert F.conv2d is STOCK_CONV2D
+    assert torch.nn.Sequential.forward is STOCK_SEQ_FORWARD
     assert not amd_tuned_torch.is_enabled()
     amd_tuned_torch.disable()                       # idempotent
+
+
+def test_cpu_conv2d_and_sequential_blocks_go_to_stock(patched):
+    x = torch.randn(2, 8, 6, 6)
+    w = torch.randn(4, 8, 3, 3)
+    torch.testing.assert_close(F.conv2d(x, w, padding=1), STOCK_CONV2D(x, w, padding=1))
+    torch.manual_seed(0)
+    for conv in (torch.nn.Conv3d(8, 8, 3, padding=1), torch.nn.Conv2d(8, 8, 3, padding=1)):
+        blk = torch.nn.Sequential(torch.nn.GroupNorm(4, 8), torch.nn.SiLU(), conv).eval()
+        xi = torch.randn(1, 8, 3, 5, 5) if isinstance(conv, torch.nn.Conv3d) else x
+        with torch.no_grad():
+            torch.testing.assert_close(blk(xi), STOCK_SEQ_FORWARD(blk, xi))
+    other = torch.nn.Sequential(torch.nn.Linear(4, 4), torch.nn.ReLU(), torch.nn.Linear(4, 2))
+    xl = torch.randn(3, 4)
+    torch.testing.assert_close(other(xl), STOCK_SEQ_FORWARD(other, xl))
+
+
+def test_conv2d_routes_as_depth1_conv3d(patched, force_eligible):
+    x = torch.randn(2, 8, 6, 7)
+    w = torch.randn(4, 8, 3, 3)
+    b = torch.randn(4)
+    torch.testing.assert_close(F.conv2d(x, w, b, padding=1), STOCK_CONV2D(x, w, b, padding=1))
+    xc = x.contiguous(memory_format=torch.channels_last)
+    torch.testing.assert_close(F.conv2d(xc, w, b, padding=(1, 2), dilation=(1, 2)),
+                               STOCK_CONV2D(x, w, b, padding=(1, 2), dilation=(1, 2)))
+    assert force_eligible == [("conv3d", False), ("conv3d", True)]
+    F.conv2d(x, torch.randn(8, 4, 3, 3), padding=1, groups=2)   # grouped -> stock
+    F.conv2d(x, torch.randn(4, 8, 1, 1))                          # pointwise -> stock
+    F.conv2d(x, w, padding=1, stride=2)                           # stride 2 -> kernel declines
+    assert force_eligible == [("conv3d", False), ("conv3d", True)]
 
 
 def test_conv1d_fallback_toggle_is_independent():

@@ -72,6 +72,17 @@ def test_block_matches_chain(cuda, patched, monkeypatch, conv_cls, shape, Co, G,
     assert oracle.rel_l2(_np(y), ref.numpy()) <= tol
 
 
+def test_fused_conv2d_block_repeated_calls(cuda, patched, monkeypatch):
+    from amd_tuned_torch import kernel_select
+    monkeypatch.setattr(kernel_select, "_ENABLED", False)
+    m = _block(nn.Conv2d, 64, 64, 32, torch.float16, cuda, seed=9)
+    x = torch.randn(2, 64, 16, 16, device=cuda, dtype=torch.float16)
+    with torch.no_grad():
+        ys = [m(x) for _ in range(3)]
+    for y in ys[1:]:
+        assert torch.equal(y, ys[0])
+
+
 def test_fused_block_is_what_runs_with_contest_off(cuda, patched, monkeypatch):
     from amd_tuned_torch import conv_fusion_ops, kernel_select
     monkeypatch.setattr(kernel_select, "_ENABLED", False)

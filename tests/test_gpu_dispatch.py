@@ -143,6 +143,22 @@ def test_conv2d_through_patch(cuda, patched, monkeypatch, N, C, H, W, Co, k, p, 
     assert oracle.rel_l2(_np(y), ref.numpy()) <= (3.9e-3 if contest else 2e-3)
 
 
+def test_conv2d_repeated_calls_reuse_the_packed_weight(cuda, patched, monkeypatch):
+    """Same weight, several calls: every call runs the tcgen05 route (the
+    packed-weight cache is keyed on the 4-D weight, not on its per-call
+    depth-1 view) and gives the same result."""
+    from amd_tuned_torch import kernel_select, ops
+    monkeypatch.setattr(kernel_select, "_ENABLED", False)
+    x = torch.randn(2, 64, 20, 24, device=cuda, dtype=torch.float16)
+    w = torch.randn(64, 64, 3, 3, device=cuda, dtype=torch.float16) * 0.05
+    ys = [F.conv2d(x, w, padding=1) for _ in range(3)]
+    assert ops._packed_weights.get(w) is not None
+    for y in ys[1:]:
+        assert torch.equal(y, ys[0])
+    ref = torch.nn.functional.conv2d(x.float().cpu(), w.float().cpu(), padding=1)
+    assert oracle.rel_l2(_np(ys[0]), ref.numpy()) <= 2e-3
+
+
 def test_conv2d_stock_routes_and_backward(cuda, patched):
     x = torch.randn(2, 64, 16, 16, device=cuda, dtype=torch.float16)
     wg = torch.randn(64, 32, 3, 3, device=cuda, dtype=torch.float16) * 0.05
