@@ -83,13 +83,6 @@ def test_fftconv1d_overlap_save(cuda, B, C, L, K, pad, nfft, dt):
     assert ops.read_device_flags() == 0
 
 
-def test_fftconv1d_plan_choice():
-    from amd_tuned_torch import fftconv_ops
-    assert fftconv_ops.fftconv1d_plan(16384, 2048, 1024) == (8192, True)    # cfg 4b
-    assert fftconv_ops.fftconv1d_plan(4000, 64, 0) == (4000, False)
-    assert fftconv_ops.fftconv1d_plan(60000, 257, 128)[1] is True           # too long for one
-
-
 def test_fftconv1d_cfg4b_full_size(cuda):
     """BASELINE cfg 4b: x[16,1024,16384] fp16 ~N(0,1), w[1024,1,2048] kaiming-U,
     bias, groups 1024, padding 1024 -> L_out 16385.  Checked on a slice of

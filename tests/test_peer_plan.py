@@ -1,5 +1,6 @@
-"""Host-side geometry of the peer-memory exchange (no GPU): the halo sides
-each rank pushes and the window layout the C ABI reports."""
+"""Host-side planning (no GPU): the peer-memory exchange's halo sides and
+window layout, and the FFT conv1d transform plan (whole row or overlap-save
+segments)."""
 from __future__ import annotations
 
 import pytest
@@ -56,3 +57,12 @@ def test_window_layout():
     assert L.b200_peer_window_bytes(8, 32, 100) == off + 65536
     assert L.b200_peer_window_xp_offset(65, 32) == -1
     assert L.b200_peer_window_xp_offset(2, 0) == -1
+
+
+def test_fftconv1d_plan_choice():
+    from amd_tuned_torch import fftconv_ops
+    assert fftconv_ops.fftconv1d_plan(16384, 2048, 1024) == (8192, True)    # cfg 4b
+    assert fftconv_ops.fftconv1d_plan(4000, 64, 0) == (4000, False)
+    assert fftconv_ops.fftconv1d_plan(60000, 257, 128)[1] is True           # too long for one
+    nfft, seg = fftconv_ops.fftconv1d_plan(1000, 257, 128)
+    assert not seg and nfft >= 1000 + 2 * 128
