@@ -242,6 +242,14 @@ def _rel_l2(a, b) -> float:
     return float((a - b).norm() / b.norm().clamp_min(1e-300))
 
 
+def _stock_us(fn, iters: int, stream, warmup: int = 1) -> float:
+    """Stock torch on the GPU (cuDNN / ATen kernels) for the same op: average
+    us per call over `iters` calls after `warmup`, CUDA events on `stream`."""
+    for i in range(warmup):
+        fn(i)
+    return _events_time(fn, iters, stream) * 1e3
+
+
 # ------------------------------------------------------------ per shape ---
 def per_shape(dev, peaks, only=None, small=False) -> dict:
     """Device-timed us/op, roofline fraction and rel-L2 for BASELINE configs
@@ -270,9 +278,12 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         ms = _graph_time(lambda i: ops.depthwise_conv1d(xs[i % nbuf], wd, bd, 1, out=ys[i % nbuf]),
                          200, stream)
         byt = 33558528
+        w3 = w.to(dev)
+        stock = _stock_us(lambda i: torch.conv1d(xs[i % nbuf], w3, bd, 1, 1, 1, 256), 50, stream)
         out["cfg1_dwconv1d_fp32"] = {"us_per_op": ms * 1e3, "bound": "hbm",
                                      "achieved_gbs": byt / (ms * 1e-3) / 1e9,
-                                     "frac": byt / (ms * 1e-3) / 1e9 / hbm, "rel_l2": err}
+                                     "frac": byt / (ms * 1e-3) / 1e9 / hbm, "rel_l2": err,
+                                     "stock_gpu_us_per_op": stock}
         del xs, ys
 
     if only in (None, "cfg3"):
@@ -288,10 +299,8 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         ref = F.group_norm(x.float(), 32, w.float(), b.float(), 1e-6)
         byt = 134219776
         best = None
-        for name, var in (("auto", ops.GN_AUTO), ("cluster4", ops.gn_cluster_variant(4)),
-                          ("cluster8", ops.gn_cluster_variant(8)),
-                          ("cluster16", ops.gn_cluster_variant(16)), ("split", ops.GN_SPLIT),
-                          ("l2", ops.GN_L2)):
+        stock = _stock_us(lambda i: torch.group_norm(xs[i % nbuf], 32, wd, bd, 1e-6), 50, stream)
+        for name, var in (("auto", ops.GN_AUTO),):
             y = ops.group_norm(xs[0], 32, wd, bd, 1e-6, variant=var)
             if y is None:
                 continue
@@ -302,7 +311,7 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
                                                       out=ys[i % nbuf]), 100, stream)
             rec = {"variant": name, "us_per_op": ms * 1e3, "bound": "hbm",
                    "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
-                   "rel_l2": err}
+                   "rel_l2": err, "stock_gpu_us_per_op": stock}
             out[f"cfg3_group_norm_bf16_{name}"] = rec
         del xs, ys
         torch.cuda.empty_cache()
@@ -331,8 +340,12 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         ms = _graph_time(conv, 10, stream)
         flop = 2.0 * 64 * 128 * 128 * 128 * 128 * 27
         tf = flop / (ms * 1e-3) / 1e12
+        xs_cl = [x_.permute(0, 4, 1, 2, 3) for x_ in xs]    # channels-last NCDHW views
+        stock = _stock_us(lambda i: torch.conv3d(xs_cl[i % 2], w, b, 1, (0, 1, 1)), 5, stream)
         out["cfg5_conv3d_bf16"] = {"us_per_op": ms * 1e3, "bound": "tensor", "tflops": tf,
-                                   "frac": tf / peaks["bf16_tflops"], "rel_l2_slice": err}
+                                   "frac": tf / peaks["bf16_tflops"], "rel_l2_slice": err,
+                                   "stock_gpu_us_per_op": stock}
+        del xs_cl
         del xs, ys, y
         torch.cuda.empty_cache()
 
@@ -425,11 +438,12 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         for i in range(2):
             fftconv_ops.fftconv1d(xs[i], wd, bd, 1024)
         ms = _graph_time(lambda i: fftconv_ops.fftconv1d(xs[i % 2], wd, bd, 1024), 6, stream)
+        stock = _stock_us(lambda i: torch.conv1d(xs[i % 2], wd, bd, 1, 1024, 1, C4), 2, stream)
         byt = 1077970944 * C4 // 1024
         out["cfg4b_fftconv1d_fp16"] = {"us_per_op": ms * 1e3, "bound": "hbm",
                                        "achieved_gbs": byt / (ms * 1e-3) / 1e9,
                                        "frac": byt / (ms * 1e-3) / 1e9 / hbm,
-                                       "rel_l2_slice": err,
+                                       "rel_l2_slice": err, "stock_gpu_us_per_op": stock,
                                        "plan": dict(zip(("nfft", "overlap_save"),
                                                         fftconv_ops.fftconv1d_plan(16384, 2048,
                                                                                    1024)))}
@@ -455,11 +469,13 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
                 fftconv_ops.fft_conv3d(xs[i], wd, bd, padding=7)
             ms = _graph_time(lambda i: fftconv_ops.fft_conv3d(xs[i % 4], wd, bd, padding=7), 6,
                              stream)
+            stock = _stock_us(lambda i: torch.conv3d(xs[i % 4], wd, bd, 1, 7), 2, stream)
             byt = 61202560
             out["cfg4a_fftconv3d_fp16"] = {
                 "us_per_op": ms * 1e3, "bound": "hbm (compulsory I/O)",
                 "achieved_gbs": byt / (ms * 1e-3) / 1e9, "frac": byt / (ms * 1e-3) / 1e9 / hbm,
                 "effective_tflops": 3.624e12 / (ms * 1e-3) / 1e12, "rel_l2_slice": err,
+                "stock_gpu_us_per_op": stock,
                 "note": "weight spectrum cached (1.6 GB complex fp16) and streamed once per call"}
         del xs, y
         torch.cuda.empty_cache()
@@ -550,6 +566,10 @@ def run_ours(args, rank, world, dev) -> dict:
     stack = run_stack(args, rank, world, dev, peaks) if not args.no_stack else None
     torch.cuda.empty_cache()
     shapes = per_shape(dev, peaks) if (rank == 0 and not args.no_shapes) else {}
+    sharded = None
+    if world > 1 and not args.no_shapes:
+        dist.barrier()
+        sharded = sharded_shapes(rank, world, dev, peaks, shapes)
     cpu = cpu_baseline(x, w, b) if (rank == 0 and world == 1) else None
     tr = _traffic("conv3d_tc_kernel")
     return {
@@ -577,11 +597,107 @@ def run_ours(args, rank, world, dev) -> dict:
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
         "per_shape": shapes,
+        "per_shape_sharded": sharded,
         "video_stack": stack,
     }
 
 
 CFG5_FLOPS = 4 * 2 * 134217728 * 128 * 27   # 3.7108e12 per step (4 conv layers)
+
+
+def sharded_shapes(rank: int, world: int, dev, peaks, single: dict) -> dict:
+    """BASELINE cfgs 1, 3, 4a, 4b split across the ranks with no
+    communication (strong scaling: the total work is the single-GPU op's):
+    cfg1 and cfg4b by channels (depthwise: channels are independent), cfg3 by
+    whole groups (C/R channels = G/R groups per rank), cfg4a by output
+    channels (every rank reads all of x and its slice of the weight).  Each
+    rank times its shard with CUDA-graph replay; the job time is the max over
+    ranks.  Shard inputs are seeded synthetic tensors of the config's
+    distribution (values do not change the kernels' timing; parity is
+    covered by the tests)."""
+    from amd_tuned_torch import fftconv_ops, ops
+    stream = torch.cuda.current_stream(dev)
+    hbm = peaks["hbm_gbs"]
+    out = {}
+
+    def job(ms: float) -> float:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def record(name, ms, byt, key):
+        rec = {"us_per_op": ms * 1e3, "n_gpus": world, "scaling": "strong",
+               "achieved_gbs": byt / (ms * 1e-3) / 1e9,
+               "frac_of_world_hbm": byt / (ms * 1e-3) / 1e9 / (world * hbm)}
+        base = single.get(key, {}).get("us_per_op") if single else None
+        if base:
+            rec["single_gpu_us_per_op"] = base
+            rec["speedup_vs_1gpu"] = base / (ms * 1e3)
+        out[name] = rec
+
+    g = torch.Generator().manual_seed(100 + rank)
+    # cfg1: depthwise conv1d fp32 [8, 256, 2048] k3, channels split.
+    c = 256 // world
+    x = torch.randn(8, c, 2048, generator=g)
+    nbuf = _nbuf(x.numel() * 4 * 2)
+    xs = [x.to(dev) for _ in range(nbuf)]
+    ys = [torch.empty_like(xs[0]) for _ in range(nbuf)]
+    wd = _kaiming((c, 3), g).to(dev)
+    bd = torch.randn(c, generator=g).to(dev)
+    for i in range(3):
+        ops.depthwise_conv1d(xs[i], wd, bd, 1, out=ys[i])
+    ms = _graph_time(lambda i: ops.depthwise_conv1d(xs[i % nbuf], wd, bd, 1, out=ys[i % nbuf]),
+                     200, stream)
+    record("cfg1_dwconv1d_fp32", job(ms), 33558528, "cfg1_dwconv1d_fp32")
+    del xs, ys
+
+    # cfg3: GroupNorm bf16 [4, 512, 128, 128] G32, whole groups per rank.
+    c, gr = 512 // world, 32 // world
+    x = (torch.randn(4, c, 128, 128, generator=g) * 2).bfloat16()
+    nbuf = _nbuf(x.numel() * 2 * 2)
+    xs = [x.to(dev) for _ in range(nbuf)]
+    ys = [torch.empty_like(xs[0]) for _ in range(nbuf)]
+    wd = (torch.rand(c, generator=g) + 0.5).bfloat16().to(dev)
+    bd = (torch.randn(c, generator=g) * 0.1).bfloat16().to(dev)
+    for i in range(3):
+        ops.group_norm(xs[i], gr, wd, bd, 1e-6, out=ys[i])
+    ms = _graph_time(lambda i: ops.group_norm(xs[i % nbuf], gr, wd, bd, 1e-6, out=ys[i % nbuf]),
+                     100, stream)
+    record("cfg3_group_norm_bf16", job(ms), 134219776, "cfg3_group_norm_bf16_auto")
+    del xs, ys
+    torch.cuda.empty_cache()
+
+    # cfg4b: long-filter FFT conv1d fp16 [16, 1024, 16384] k2048, channels split.
+    c = 1024 // world
+    x = torch.randn(16, c, 16384, generator=g).half()
+    xs = [x.to(dev) for _ in range(2)]
+    wd = _kaiming((c, 1, 2048), g).half().to(dev)
+    bd = (torch.randn(c, generator=g) * 0.02).half().to(dev)
+    for i in range(2):
+        fftconv_ops.fftconv1d(xs[i], wd, bd, 1024)
+    ms = _graph_time(lambda i: fftconv_ops.fftconv1d(xs[i % 2], wd, bd, 1024), 6, stream)
+    record("cfg4b_fftconv1d_fp16", job(ms), 1077970944, "cfg4b_fftconv1d_fp16")
+    del xs
+    torch.cuda.empty_cache()
+
+    # cfg4a: FFT conv3d fp16 [2, 64, 16, 64, 64] x [64, 64, 15^3] p7, output channels split.
+    c = 64 // world
+    x = torch.randn(2, 64, 16, 64, 64, generator=g).half()
+    xs = [x.to(dev) for _ in range(4)]
+    wd = _kaiming((c, 64, 15, 15, 15), g).half().to(dev)
+    bd = (torch.randn(c, generator=g) * 0.01).half().to(dev)
+    y = fftconv_ops.fft_conv3d(xs[0], wd, bd, padding=7)
+    if y is not None:
+        for i in range(2):
+            fftconv_ops.fft_conv3d(xs[i], wd, bd, padding=7)
+        ms = _graph_time(lambda i: fftconv_ops.fft_conv3d(xs[i % 4], wd, bd, padding=7), 6,
+                         stream)
+    else:
+        ms = float("nan")
+    record("cfg4a_fftconv3d_fp16", job(ms), 61202560, "cfg4a_fftconv3d_fp16")
+    del xs, y
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_stack(args, rank, world, dev, peaks) -> dict:
@@ -625,12 +741,21 @@ def run_stack(args, rank, world, dev, peaks) -> dict:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    del y
-    return {"workload": "cfg5 video stack bf16 [1,128,64,128,128] x 4 blocks, T-sharded",
+    del y, x_local
+    torch.cuda.empty_cache()
+    single = None
+    if world > 1:
+        # The same step unsharded on one GPU, timed in this run (rank 0 while
+        # the other ranks wait), so the record carries the 1 -> N speed-up.
+        if rank == 0:
+            single = _stack_single_gpu_ms(args, dev)
+        dist.barrier()
+    rec = {"workload": "cfg5 video stack bf16 [1,128,64,128,128] x 4 blocks, T-sharded",
             "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
             "tflops": CFG5_FLOPS / (ms * 1e-3) / 1e12,
-            "frac_of_peak": CFG5_FLOPS / (ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"],
-            "peak_src": peaks["src"] + " sustained bf16",
+            "frac_of_peak": (CFG5_FLOPS / (ms * 1e-3) / 1e12
+                             / (world * peaks["bf16_tflops_sustained"])),
+            "peak_src": peaks["src"] + " sustained bf16, x n_gpus",
             "collectives": ("none" if world == 1 else
                             "per block: all_gather of GN partial stats; NCCL send/recv of "
                             "1 halo frame each side" if args.stack_exchange == "nccl" else
@@ -638,6 +763,42 @@ def run_stack(args, rank, world, dev, peaks) -> dict:
                             "into the peers' memory over NVLink (CUDA IPC windows, "
                             "device flags; no NCCL launch)"),
             "timing": "one CUDA graph per step (captured once), replayed"}
+    if single is not None:
+        rec["single_gpu_ms_per_step"] = single
+        rec["speedup_vs_1gpu"] = single / ms
+        rec["efficiency"] = single / ms / world
+    return rec
+
+
+def _stack_single_gpu_ms(args, dev) -> float:
+    """cfg 5 step on one GPU (no sharding), same graph-replay timing."""
+    from amd_tuned_torch import ops
+    from amd_tuned_torch import video_stack as vs
+    params = vs.make_params(channels=128, blocks=4, groups=32, dtype=torch.bfloat16, seed=5,
+                            device=dev)
+    x = torch.randn(1, 128, 64, 128, 128, generator=torch.Generator().manual_seed(5))
+    xd = x.bfloat16().to(dev)
+    del x
+    stack = vs.VideoStack(params, group=None)
+    for _ in range(2):
+        stack.forward(xd)
+    stack.capture(xd)
+    stack.replay()
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 10))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        stack.replay()
+    e.record()
+    torch.cuda.synchronize()
+    flags = ops.read_device_flags(dev)
+    stack.close()
+    del xd
+    torch.cuda.empty_cache()
+    if flags:
+        raise RuntimeError(f"video stack (1 GPU): device fault word {flags}")
+    return s.elapsed_time(e) / steps
 
 
 def cpu_baseline(x, w, b, budget_s: float = 10.0) -> dict:

@@ -77,7 +77,8 @@ int b200_gn_fwd(const void* x, const void* gamma, const void* beta, void* y, int
  * 3 * N * G * (ceil(C/G * S / 65536) + 1) floats <= 65536, else B200_ERR_ARG.
  * Calls share the array: calls that may overlap on the GPU race.  The first
  * call on a device resolves the array's address (make it before any stream
- * capture).  No counterpart in the reference. */
+ * capture); it is resolved again if the device's context is re-created
+ * (cudaDeviceReset).  No counterpart in the reference. */
 int b200_gn_fwd_static_scratch(const void* x, const void* gamma, const void* beta, void* y,
                                int dtype, int affine_dtype, int64_t N, int64_t C, int64_t S,
                                int64_t G, float eps, void* stream);
@@ -118,10 +119,41 @@ int b200_gn_apply(const void* x, const float* stats, const void* gamma, const vo
  * Replaces _native_depthwise_conv1d.conv1d_forward(u, weight[C,K], bias[C],
  * padding, is_bhl=True) (amd_tuned_torch/_vendor/flashfftconv_depthwise_conv1d/
  * host.cpp:7-11 -> conv1d.h:56-83 -> conv1d_bhl.cu:100-140).  x: [B, C, L],
- * w: [C, K], bias: [C] or NULL (w_dtype for both), y: [B, C, L_out]. */
+ * w: [C, K], bias: [C] or NULL (w_dtype for both), y: [B, C, L_out].
+ * variant: 0, or B200_DWCONV1D_FLIP_TAPS to use w[c, K-1-k] for tap k -- the
+ * input gradient of the forward at padding p is this op applied to dy with
+ * the flipped taps at padding K-1-p (no bias), output length L. */
+#define B200_DWCONV1D_FLIP_TAPS 1
 int b200_dwconv1d_fwd(const void* x, const void* w, const void* bias, void* y, int dtype,
                       int w_dtype, int64_t B, int64_t C, int64_t L, int64_t K, int64_t pad,
                       int64_t L_out, int variant, void* stream);
+
+/* Depthwise conv1d weight and bias gradients of the forward above:
+ *   dw[c,k] = sum_{b,o} dy[b,c,o] * x[b,c,o-pad+k],  dbias[c] = sum_{b,o} dy[b,c,o]
+ * x: [B, C, L], dy: [B, C, L_out] (dtype), dw: [C, K], dbias: [C] or NULL
+ * (w_dtype).  Fixed-order reduction (deterministic).  workspace: at least
+ * b200_dwconv1d_bwd_workspace_bytes() bytes.  Replaces the weight/bias half
+ * of conv1d_bwd (amd_tuned_torch/_vendor/flashfftconv_depthwise_conv1d/
+ * conv1d.h:85-104 -> conv1d_bwd_cuda_bhl.cu:19-114); the input half is
+ * b200_dwconv1d_fwd with B200_DWCONV1D_FLIP_TAPS. */
+size_t b200_dwconv1d_bwd_workspace_bytes(int64_t B, int64_t C, int64_t K, int64_t L_out);
+int b200_dwconv1d_bwd_weight(const void* x, const void* dy, void* dw, void* dbias, int dtype,
+                             int w_dtype, int64_t B, int64_t C, int64_t L, int64_t K, int64_t pad,
+                             int64_t L_out, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* GroupNorm backward: dx [N, C, S] (dtype; NULL to skip), dgamma / dbeta [C]
+ * (affine_dtype; NULL to skip) of y = (x - mean) * rstd * gamma + beta.
+ * stats: (count, mean, M2) per (n, g) of x as written by
+ * b200_gn_partial_stats.  gamma NULL = no affine scale.  Reductions in fp32
+ * per chunk, fp64 across chunks and channels (fixed order).  workspace: at
+ * least b200_gn_bwd_workspace_bytes() bytes.  Replaces the torch-ops
+ * derivative _group_norm_backward (amd_tuned_torch/_dispatch.py:2212-2302). */
+size_t b200_gn_bwd_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G);
+int b200_gn_bwd(const void* x, const void* dy, const float* stats, const void* gamma, void* dx,
+                void* dgamma, void* dbeta, int dtype, int affine_dtype, int64_t N, int64_t C,
+                int64_t S, int64_t G, float eps, void* workspace, size_t workspace_bytes,
+                void* stream);
 
 /* ------------------------------------------------------------------ */
 /* Dense conv3d (groups = 1) as an implicit GEMM on tcgen05 tensor cores.

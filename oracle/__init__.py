@@ -161,6 +161,78 @@ def stock_group_norm(x, G: int, gamma=None, beta=None, eps: float = 1e-5):
     return F.group_norm(t(x), G, t(gamma), t(beta), eps).numpy()
 
 
+# ------------------------------------------------------------ backward
+def np_group_norm_backward(x, dy, G: int, gamma=None, eps: float = 1e-5):
+    """(dx, dgamma, dbeta) of GroupNorm in float64: the derivative the
+    reference's _group_norm_backward computes (amd_tuned_torch/_dispatch.py:
+    2212-2302): xhat = (x - mean) * rstd per (n, g); dbeta = sum dy;
+    dgamma = sum dy * xhat; dx = rstd * (gamma dy - mean_g(gamma dy)
+    - xhat * mean_g(gamma dy xhat))."""
+    x = np.asarray(x, dtype=np.float64)
+    dy = np.asarray(dy, dtype=np.float64)
+    N, C = x.shape[:2]
+    xg = x.reshape(N, G, C // G, -1)
+    dg = dy.reshape(N, G, C // G, -1)
+    mean = xg.mean(axis=(2, 3), keepdims=True)
+    rstd = 1.0 / np.sqrt(((xg - mean) ** 2).mean(axis=(2, 3), keepdims=True) + eps)
+    xhat = (xg - mean) * rstd
+    gm = (np.ones(C) if gamma is None else np.asarray(gamma, dtype=np.float64))
+    gdy = dg * gm.reshape(1, G, C // G, 1)
+    dx = rstd * (gdy - gdy.mean(axis=(2, 3), keepdims=True)
+                 - xhat * (gdy * xhat).mean(axis=(2, 3), keepdims=True))
+    dgamma = (dg * xhat).sum(axis=(0, 3)).reshape(C)
+    dbeta = dg.sum(axis=(0, 3)).reshape(C)
+    return dx.reshape(x.shape), dgamma, dbeta
+
+
+def np_dwconv1d_backward(x, dy, w, pad: int):
+    """(dx, dw [C, K], dbias) of the depthwise conv1d
+    y[b,c,o] = bias[c] + sum_k w[c,k] x[b,c,o-pad+k] in float64 -- the
+    gradients the reference's vendored backward kernel produces
+    (amd_tuned_torch/_vendor/flashfftconv_depthwise_conv1d/
+    conv1d_bwd_cuda_bhl.cu:34-72: du[j] = sum_k dout[j-pad+k] w[K-1-k]
+    (valid there for L_out = L), dk[k] = sum_j u[k-pad+j] dout[j]; dbias =
+    sum of dout), here for any padding and output length."""
+    x = np.asarray(x, dtype=np.float64)
+    dy = np.asarray(dy, dtype=np.float64)
+    B, C, L = x.shape
+    w = np.asarray(w, dtype=np.float64).reshape(C, -1)
+    K = w.shape[1]
+    Lout = dy.shape[-1]
+    xp = np.pad(x, [(0, 0), (0, 0), (pad, pad)])
+    dxp = np.zeros_like(xp)
+    dw = np.zeros((C, K))
+    for k in range(K):
+        dxp[:, :, k:k + Lout] += dy * w[None, :, k, None]
+        dw[:, k] = (dy * xp[:, :, k:k + Lout]).sum(axis=(0, 2))
+    return dxp[:, :, pad:pad + L], dw, dy.sum(axis=(0, 2))
+
+
+def stock_group_norm_backward(x, dy, G: int, gamma=None, beta=None, eps: float = 1e-5):
+    """Stock torch CPU fp32 autograd of F.group_norm: (dx, dgamma, dbeta)."""
+    import torch
+    import torch.nn.functional as F
+    t = lambda a: None if a is None else torch.tensor(np.asarray(a, dtype=np.float32),
+                                                      requires_grad=True)
+    xt, gt, bt = t(x), t(gamma), t(beta)
+    F.group_norm(xt, G, gt, bt, eps).backward(torch.as_tensor(np.asarray(dy, np.float32)))
+    g = lambda a: None if a is None else a.grad.numpy()
+    return g(xt), g(gt), g(bt)
+
+
+def stock_dwconv1d_backward(x, dy, w, bias, pad: int):
+    """Stock torch CPU fp32 autograd of the depthwise F.conv1d: (dx, dw, dbias)."""
+    import torch
+    import torch.nn.functional as F
+    t = lambda a: None if a is None else torch.tensor(np.asarray(a, dtype=np.float32),
+                                                      requires_grad=True)
+    xt, wt, bt = t(x), t(w), t(bias)
+    C = xt.shape[1]
+    F.conv1d(xt, wt.reshape(C, 1, -1), bt, 1, pad, 1, C).backward(
+        torch.as_tensor(np.asarray(dy, np.float32)))
+    return xt.grad.numpy(), wt.grad.numpy(), None if bt is None else bt.grad.numpy()
+
+
 def rel_l2(y, ref) -> float:
     """||y - ref||_2 / ||ref||_2 in float64 (the BASELINE parity metric)."""
     y = np.asarray(y, dtype=np.float64)

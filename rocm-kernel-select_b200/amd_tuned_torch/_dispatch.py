@@ -4,7 +4,7 @@ Mirrors the reference's amd_tuned_torch/_dispatch.py for the conv/norm path:
 `_ORIGINALS` / `_install` / `_restore` (:662-672), `_grad_safe` (:528-553),
 `_usable` + the exact-type tensor guard (:643-659), `_patched_conv3d` with
 `_Conv3dFn` (:2029-2093), `_patched_group_norm` with `_GroupNormFn` and its
-torch-ops backward (:2118-2370), `enable`/`disable`/`is_enabled`
+backward (:2118-2370, here on the native backward kernels), `enable`/`disable`/`is_enabled`
 (:2913-3050).  The candidate lists differ: every contested kernel is one of
 this project's sm_100a kernels, with stock torch kept last as kernel_select's
 verification reference.
@@ -27,9 +27,13 @@ from typing import Any, Callable
 import torch
 import torch.nn.functional as F
 
-from . import _lib, fftconv_ops, kernel_select, ops
+from . import _lib, compile_ops, fftconv_ops, kernel_select, ops
 
 _ORIGINALS: dict = {}
+# The stock torch.nn.functional entry points saved by enable(), by name.  The
+# wrappers read these (string keys) rather than _ORIGINALS (keyed by the module
+# object), which torch.compile's tracer cannot look up.
+_STOCK: dict = {}
 _ENABLED = False
 
 _GROUPNORM_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
@@ -104,11 +108,15 @@ def _install(target: Any, name: str, wrapper: Callable) -> None:
     key = (target, name)
     if key not in _ORIGINALS:
         _ORIGINALS[key] = getattr(target, name)
+        if target is F:
+            _STOCK[name] = _ORIGINALS[key]
     setattr(target, name, wrapper)
 
 
 def _restore(target: Any, name: str) -> None:
     original = _ORIGINALS.pop((target, name), None)
+    if target is F:
+        _STOCK.pop(name, None)
     if original is not None:
         setattr(target, name, original)
 
@@ -164,7 +172,7 @@ def _fftconv3d_candidate(input, weight, bias, stride, padding, dilation, groups)
 
 
 def _conv3d_candidates(input, weight, bias, stride, padding, dilation, groups):
-    orig = _ORIGINALS[(F, "conv3d")]
+    orig = _STOCK["conv3d"]
     cands = []
     if _usable(input, weight, bias, dtypes=_CONV_TC_DTYPES) and _lib.available():
         cands.append(("tcgen05", _conv3d_tc_thunk(input, weight, bias, stride, padding, dilation)))
@@ -176,7 +184,7 @@ def _conv3d_candidates(input, weight, bias, stride, padding, dilation, groups):
 
 
 def _conv3d_accelerated_forward(input, weight, bias, stride, padding, dilation, groups):
-    orig = _ORIGINALS[(F, "conv3d")]
+    orig = _STOCK["conv3d"]
     if (groups != 1 or not _usable(input, weight, bias, dtypes=_FFTCONV_CONV_DTYPES)
             or input.numel() == 0 or weight.numel() == 0):
         if _DEBUG:
@@ -245,10 +253,18 @@ class _Conv3dFn(torch.autograd.Function):
 
 
 def _patched_conv3d(input, weight, bias=None, stride=1, padding=0, dilation=1, groups=1):
+    if _is_compiling():
+        # While Dynamo traces: one custom-op node (fake shapes, autograd
+        # registered) for the tensor-core problems, stock for the rest.
+        if (_usable(input, weight, bias, dtypes=_CONV_TC_DTYPES)
+                and compile_ops.conv3d_native_eligible(input, weight, bias, stride, padding,
+                                                       dilation, groups)):
+            return compile_ops.conv3d_native(input, weight, bias, stride, padding, dilation)
+        return _STOCK["conv3d"](input, weight, bias, stride, padding, dilation, groups)
     if _grad_safe(input, weight, bias):
         return _conv3d_accelerated_forward(input, weight, bias, stride, padding, dilation, groups)
     if groups != 1:
-        return _ORIGINALS[(F, "conv3d")](input, weight, bias, stride, padding, dilation, groups)
+        return _STOCK["conv3d"](input, weight, bias, stride, padding, dilation, groups)
     return _Conv3dFn.apply(input, weight, bias, stride, padding, dilation, groups)
 
 
@@ -289,7 +305,7 @@ def _conv2d_tc_thunk(input, weight, bias, stride, padding, dilation):
 
 
 def _conv2d_accelerated_forward(input, weight, bias, stride, padding, dilation, groups):
-    orig = _ORIGINALS[(F, "conv2d")]
+    orig = _STOCK["conv2d"]
     if (groups != 1 or input.dim() != 4 or weight.dim() != 4 or input.numel() == 0
             or weight.numel() == 0 or tuple(weight.shape[2:]) == (1, 1)
             or not _usable(input, weight, bias, dtypes=_CONV_TC_DTYPES) or not _lib.available()):
@@ -347,7 +363,7 @@ def _patched_conv2d(input, weight, bias=None, stride=1, padding=0, dilation=1, g
     if _grad_safe(input, weight, bias):
         return _conv2d_accelerated_forward(input, weight, bias, stride, padding, dilation, groups)
     if groups != 1:
-        return _ORIGINALS[(F, "conv2d")](input, weight, bias, stride, padding, dilation, groups)
+        return _STOCK["conv2d"](input, weight, bias, stride, padding, dilation, groups)
     return _Conv2dFn.apply(input, weight, bias, stride, padding, dilation, groups)
 
 
@@ -359,24 +375,29 @@ def _gn_thunk(input, num_groups, weight, bias, eps, variant):
 
 
 def _group_norm_candidates(input, num_groups, weight, bias, eps):
-    orig = _ORIGINALS[(F, "group_norm")]
+    orig = _STOCK["group_norm"]
     cands = []
     if input.is_contiguous() and _lib.available():
+        # The library's own size rule picks the two-pass L2 kernel, the cluster
+        # kernel or the split path; the fixed cluster sizes and the split path
+        # were timed as separate entries once and never won, so only the
+        # automatic choice competes (against stock, when stock is timed).
         cands.append(("native", _gn_thunk(input, num_groups, weight, bias, eps, ops.GN_AUTO)))
-        for k in (4, 8, 16):
-            cands.append((f"native_c{k}", _gn_thunk(input, num_groups, weight, bias, eps,
-                                                    ops.gn_cluster_variant(k))))
-        cands.append(("native_split", _gn_thunk(input, num_groups, weight, bias, eps,
-                                                ops.GN_SPLIT)))
-        cands.append(("native_l2", _gn_thunk(input, num_groups, weight, bias, eps, ops.GN_L2)))
     cands.append(("stock", lambda: orig(input, num_groups, weight, bias, eps)))
     return cands
 
 
+def _group_norm_eligible(input, num_groups, weight, bias) -> bool:
+    """CUDA tensors of a GroupNorm dtype, contiguous NC[*], C divisible by G,
+    non-empty: everything else (CPU tensors included) is stock torch's, in
+    the forward and in the backward."""
+    return (input.dim() >= 2 and input.shape[1] % num_groups == 0 and input.is_contiguous()
+            and input.numel() > 0 and _usable(input, weight, bias, dtypes=_GROUPNORM_DTYPES))
+
+
 def _group_norm_accelerated_forward(input, num_groups, weight, bias, eps):
-    orig = _ORIGINALS[(F, "group_norm")]
-    if (input.dim() < 2 or input.shape[1] % num_groups != 0 or not input.is_contiguous()
-            or input.numel() == 0 or not _usable(input, weight, bias, dtypes=_GROUPNORM_DTYPES)):
+    orig = _STOCK["group_norm"]
+    if not _group_norm_eligible(input, num_groups, weight, bias):
         if _DEBUG:
             _debug("group_norm", "stock", "layout/dtype outside this tier", input=input)
         return orig(input, num_groups, weight, bias, eps)
@@ -404,34 +425,19 @@ def _group_norm_accelerated_forward(input, num_groups, weight, bias, eps):
 
 
 def _group_norm_backward(grad_output, input, num_groups, weight, eps, needs, bias_dtype=None):
-    """GroupNorm's derivative in torch ops, each gradient in its own input's
-    dtype; reductions accumulate in fp32 for fp16/bf16 (an fp16 sum over a
-    large group overflows).  Same math as the reference's
-    _group_norm_backward (_dispatch.py:2212-2302)."""
-    N, C = input.shape[0], input.shape[1]
-    M = C // num_groups
-    dtype = input.dtype
-    acc = torch.float32 if dtype in (torch.float16, torch.bfloat16) else dtype
-    x = input.reshape(N, num_groups, M, -1)
-    dy = grad_output.reshape(N, num_groups, M, -1)
+    """(dx, dweight, dbias) of F.group_norm on the sm_100a backward kernels
+    (b200_gn_bwd: per-row sums of dy and dy * (x - mean), group
+    coefficients, one elementwise pass; reductions in fp32 within a chunk and
+    fp64 across chunks, so fp16 groups of any size do not overflow).  Each
+    gradient comes back in its own parameter's dtype.  Role of the
+    reference's torch-ops _group_norm_backward (_dispatch.py:2212-2302)."""
     need_x, need_w, need_b = needs
-    gx = gw = gb = None
-    if need_b:
-        gb = dy.sum(dim=(0, 3), dtype=acc).reshape(C).to(bias_dtype or dtype)
-    if not (need_x or need_w):
-        return gx, gw, gb
-    mean = x.mean(dim=(2, 3), keepdim=True, dtype=acc)
-    xc = x - mean.to(dtype)
-    var = xc.square().mean(dim=(2, 3), keepdim=True, dtype=acc)
-    rstd = (var + eps).rsqrt().to(dtype)
-    xhat = xc * rstd
-    if need_w and weight is not None:
-        gw = (dy * xhat).sum(dim=(0, 3), dtype=acc).reshape(C).to(weight.dtype)
-    if need_x:
-        wdy = dy if weight is None else dy * weight.reshape(1, num_groups, M, 1).to(dtype)
-        c1 = wdy.mean(dim=(2, 3), keepdim=True, dtype=acc).to(dtype)
-        c2 = (wdy * xhat).mean(dim=(2, 3), keepdim=True, dtype=acc).to(dtype)
-        gx = ((wdy - c1 - xhat * c2) * rstd).reshape(input.shape)
+    need_w = bool(need_w) and weight is not None
+    adt = weight.dtype if weight is not None else (bias_dtype or input.dtype)
+    gx, gw, gb = ops.group_norm_backward(grad_output, input, num_groups, weight, eps,
+                                         (bool(need_x), need_w, bool(need_b)), affine_dtype=adt)
+    if gb is not None and bias_dtype is not None and gb.dtype != bias_dtype:
+        gb = gb.to(bias_dtype)
     return gx, gw, gb
 
 
@@ -454,8 +460,16 @@ class _GroupNormFn(torch.autograd.Function):
 
 
 def _patched_group_norm(input, num_groups, weight=None, bias=None, eps=1e-5):
+    if _is_compiling():
+        if (input.dim() >= 2 and input.shape[1] % num_groups == 0 and input.numel() > 0
+                and _usable(input, weight, bias, dtypes=_GROUPNORM_DTYPES)):
+            return compile_ops.group_norm(input, num_groups, weight, bias, eps)
+        return _STOCK["group_norm"](input, num_groups, weight, bias, eps)
     if _grad_safe(input, weight, bias):
         return _group_norm_accelerated_forward(input, num_groups, weight, bias, eps)
+    if not _group_norm_eligible(input, num_groups, weight, bias):
+        # Stock forward and stock autograd (the native backward is CUDA-only).
+        return _STOCK["group_norm"](input, num_groups, weight, bias, eps)
     return _GroupNormFn.apply(input, weight, bias, num_groups, eps)
 
 
@@ -495,7 +509,7 @@ def enable() -> None:
     _install(F, "conv3d", _patched_conv3d)
     _install(F, "conv2d", _patched_conv2d)
     if not getattr(F.conv1d, "_amd_tuned_torch_wrapper", False):
-        _install(F, "conv1d", conv1d_dispatch.make_wrapper(lambda: _ORIGINALS[(F, "conv1d")]))
+        _install(F, "conv1d", conv1d_dispatch.make_wrapper(lambda: _STOCK["conv1d"]))
     _install(torch.nn.Sequential, "forward", _patched_sequential_forward)
     _SEQ_FORWARD_ORIG = _ORIGINALS[(torch.nn.Sequential, "forward")]
     _ENABLED = True

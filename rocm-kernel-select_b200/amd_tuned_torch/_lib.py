@@ -47,6 +47,12 @@ SIGNATURES = {
                               c_int64, c_int64, c_float, c_int, c_int, c_vp]),
     "b200_dwconv1d_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int64, c_int64,
                                   c_int64, c_int64, c_int64, c_int64, c_int, c_vp]),
+    "b200_dwconv1d_bwd_workspace_bytes": (c_size_t, [c_int64] * 4),
+    "b200_dwconv1d_bwd_weight": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 6
+                                 + [c_vp, c_size_t, c_vp]),
+    "b200_gn_bwd_workspace_bytes": (c_size_t, [c_int64] * 4),
+    "b200_gn_bwd": (c_int, [c_vp] * 7 + [c_int, c_int] + [c_int64] * 4
+                    + [c_float, c_vp, c_size_t, c_vp]),
     "b200_conv3d_packed_weight_bytes": (c_size_t, [c_int64] * 5),
     "b200_conv3d_pack_weight": (c_int, [c_vp, c_vp, c_int, c_int64, c_int64, c_int64, c_int64,
                                         c_int64, c_vp]),

@@ -54,6 +54,15 @@ def _try_fftconv1d_fastpath(input, weight, bias, stride, padding, dilation, grou
         return None
     depthwise = (depthwise_conv1d_ops.available()
                  and _is_depthwise_conv1d_eligible(input, weight, stride, dilation, groups))
+    if torch.compiler.is_compiling():
+        # While Dynamo traces: the depthwise custom op (one graph node with a
+        # registered backward), no contest; anything else goes to stock.
+        if not depthwise or not isinstance(_scalar(padding), int):
+            return None
+        b = bias if bias is not None else torch.zeros(weight.shape[0], device=input.device,
+                                                      dtype=weight.dtype)
+        return depthwise_conv1d_ops.conv1d_forward(input, weight.squeeze(1), b,
+                                                   int(_scalar(padding)))
     fft = (fftconv_ops.fft_conv1d_enabled()
            and fftconv_ops._is_depthwise(input, weight, groups)
            and _scalar(stride) == 1 and _scalar(dilation) == 1)

@@ -29,7 +29,7 @@ template <typename T, int KS>
 __global__ void __launch_bounds__(kDwThreads)
 dwconv1d_kernel(const T* __restrict__ x, const void* __restrict__ w, const void* __restrict__ bias,
                 T* __restrict__ y, int wdt, int64_t C, int64_t L, int K_dyn, int64_t pad,
-                int64_t Lout, int64_t tiles_per_row, bool vec_in) {
+                int64_t Lout, int64_t tiles_per_row, bool vec_in, bool flip) {
   const int K = KS > 0 ? KS : K_dyn;
   extern __shared__ float smem[];
   float* sw = smem;                          // K weights
@@ -42,7 +42,8 @@ dwconv1d_kernel(const T* __restrict__ x, const void* __restrict__ w, const void*
   const int win = nout + K - 1;
   const T* xr = x + row * L;
 
-  for (int k = threadIdx.x; k < K; k += kDwThreads) sw[k] = load_param(w, wdt, c * K + k);
+  for (int k = threadIdx.x; k < K; k += kDwThreads)
+    sw[k] = load_param(w, wdt, c * K + (flip ? K - 1 - k : k));
   const float b = bias ? load_param(bias, wdt, c) : 0.f;
 
   const int64_t lbeg = o0 - pad;  // global index of sx[0]
@@ -110,7 +111,7 @@ template <typename T, int K, int P>
 __global__ void __launch_bounds__(kDwThreads)
 dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
                     const void* __restrict__ bias, T* __restrict__ y, int wdt, int64_t C,
-                    int64_t L, int64_t Lout, int64_t tiles_per_row) {
+                    int64_t L, int64_t Lout, int64_t tiles_per_row, bool flip) {
   static_assert(P <= Vec16<T>::N && K - 1 - P <= Vec16<T>::N, "halo wider than one vector");
   constexpr int V = Vec16<T>::N;
   constexpr int kSub = kDwThreads * V;           // outputs of one sub-tile
@@ -144,7 +145,7 @@ dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
   }
   float wk[K];
 #pragma unroll
-  for (int k = 0; k < K; ++k) wk[k] = load_param(w, wdt, c * K + k);
+  for (int k = 0; k < K; ++k) wk[k] = load_param(w, wdt, c * K + (flip ? K - 1 - k : k));
   const float b = bias ? load_param(bias, wdt, c) : 0.f;
 
 #pragma unroll
@@ -183,7 +184,8 @@ dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
 
 template <typename T>
 int launch(const void* xv, const void* w, const void* bias, void* yv, int wdt, int64_t B,
-           int64_t C, int64_t L, int64_t K, int64_t pad, int64_t Lout, cudaStream_t stream) {
+           int64_t C, int64_t L, int64_t K, int64_t pad, int64_t Lout, bool flip,
+           cudaStream_t stream) {
   constexpr int VV = Vec16<T>::N;
   // Register path: filters of up to 9 taps whose halo fits one vector per side,
   // with "same" (pad = (K-1)/2), valid (pad = 0) or causal (pad = K-1) padding.
@@ -198,7 +200,7 @@ int launch(const void* xv, const void* w, const void* bias, void* yv, int wdt, i
       const unsigned grid = static_cast<unsigned>(blocks);
       const int mode = pad == (K - 1) / 2 ? 0 : (pad == 0 ? 1 : 2);
 #define B200_DWR(KK, PP) dwconv1d_reg_kernel<T, KK, PP><<<grid, kDwThreads, 0, stream>>>( \
-    x, w, bias, y, wdt, C, L, Lout, tiles)
+    x, w, bias, y, wdt, C, L, Lout, tiles, flip)
 #define B200_DWK(KK)                                                     \
   case KK:                                                               \
     if (mode == 0) B200_DWR(KK, (KK - 1) / 2);                           \
@@ -235,7 +237,7 @@ int launch(const void* xv, const void* w, const void* bias, void* yv, int wdt, i
       B200_CUDA_CHECK(                                                                      \
           cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
     kern<<<grid, kDwThreads, smem, stream>>>(x, w, bias, y, wdt, C, L, Ki, pad, Lout, tiles, \
-                                             vec_in);                                       \
+                                             vec_in, flip);                                 \
   } while (0)
   switch (Ki) {
     case 3: B200_DW_LAUNCH(3); break;
@@ -258,13 +260,14 @@ extern "C" int b200_dwconv1d_fwd(const void* x, const void* w, const void* bias,
                                  int dtype, int w_dtype, int64_t B, int64_t C, int64_t L,
                                  int64_t K, int64_t pad, int64_t L_out, int variant,
                                  void* stream) {
-  (void)variant;
   if (!x || !w || !y) return fail_arg("x/w/y is NULL");
+  if (variant & ~B200_DWCONV1D_FLIP_TAPS) return fail_arg("unknown variant bits");
+  const bool flip = (variant & B200_DWCONV1D_FLIP_TAPS) != 0;
   if (!dtype_ok(dtype) || !dtype_ok(w_dtype)) return fail_arg("bad dtype");
   if (B <= 0 || C <= 0 || L <= 0 || K <= 0 || pad < 0) return fail_arg("bad size");
   if (L_out != L + 2 * pad - K + 1 || L_out <= 0) return fail_arg("L_out != L + 2*pad - K + 1");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == B200_DTYPE_F32) return launch<float>(x, w, bias, y, w_dtype, B, C, L, K, pad, L_out, s);
-  if (dtype == B200_DTYPE_F16) return launch<__half>(x, w, bias, y, w_dtype, B, C, L, K, pad, L_out, s);
-  return launch<__nv_bfloat16>(x, w, bias, y, w_dtype, B, C, L, K, pad, L_out, s);
+  if (dtype == B200_DTYPE_F32) return launch<float>(x, w, bias, y, w_dtype, B, C, L, K, pad, L_out, flip, s);
+  if (dtype == B200_DTYPE_F16) return launch<__half>(x, w, bias, y, w_dtype, B, C, L, K, pad, L_out, flip, s);
+  return launch<__nv_bfloat16>(x, w, bias, y, w_dtype, B, C, L, K, pad, L_out, flip, s);
 }

@@ -977,7 +977,11 @@ int b200_gn_apply(const void* x, const float* stats, const void* gamma, const vo
 //    race on the array and must not be issued.
 //  * The first call on each device resolves the array's device address
 //    with cudaGetSymbolAddress while that device is current; make that
-//    first call before any stream capture begins.
+//    first call before any stream capture begins.  The address is resolved
+//    again when the device's current context is no longer the one it was
+//    resolved in (after a cudaDeviceReset the module is reloaded into a new
+//    context); the first call after such a reset also belongs before any
+//    capture.
 namespace b200 {
 namespace {
 constexpr int64_t kStaticScratchFloats = 65536;
@@ -989,11 +993,35 @@ static __device__ __align__(256) float g_gn_static_scratch[b200::kStaticScratchF
 namespace b200 {
 namespace {
 
+// The calling thread's current driver context (nullptr when none is bound
+// or the driver entry point is unavailable).
+CUcontext current_context() {
+  using Fn = CUresult (*)(CUcontext*);
+  static Fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<Fn>(ptr);
+  });
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
+
 // Device address of g_gn_static_scratch on the current device (host code
-// cannot use the symbol itself as a device pointer).  nullptr on failure.
+// cannot use the symbol itself as a device pointer).  Resolved on the first
+// call per device and again whenever that device's current context differs
+// from the one the address was resolved in (the module is loaded afresh
+// into a context re-created after cudaDeviceReset, possibly elsewhere).
+// nullptr on failure.
 float* static_scratch_address(cudaError_t* err) {
   static std::mutex mu;
   static float* addr[64] = {nullptr};
+  static CUcontext owner[64] = {nullptr};
   int dev = 0;
   *err = cudaGetDevice(&dev);
   if (*err != cudaSuccess) return nullptr;
@@ -1001,12 +1029,14 @@ float* static_scratch_address(cudaError_t* err) {
     *err = cudaErrorInvalidDevice;
     return nullptr;
   }
+  const CUcontext ctx = current_context();
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  if (addr[dev] == nullptr || ctx == nullptr || ctx != owner[dev]) {
     void* p = nullptr;
     *err = cudaGetSymbolAddress(&p, g_gn_static_scratch);
     if (*err != cudaSuccess) return nullptr;
     addr[dev] = static_cast<float*>(p);
+    owner[dev] = current_context();   // bound now, if it was not before the lookup
   }
   return addr[dev];
 }

@@ -1,6 +1,6 @@
 """Dispatch logic on CPU with the native ops replaced by fakes (the reference
 does the same with MagicMock natives, tests/conftest.py:44-95 there): install
-set, routing, eligibility, the autograd wrappers and GroupNorm's backward math."""
+set, routing, eligibility and the autograd wrappers."""
 from __future__ import annotations
 
 import pytest
@@ -195,31 +195,58 @@ def test_depthwise_eligibility():
     assert not elig(meta, w, 1, 1, 8)
 
 
-# ---------------------------------------------------- GroupNorm backward math
-@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
-@pytest.mark.parametrize("affine", [True, False])
-def test_group_norm_backward_matches_autograd(dtype, affine):
-    g = torch.Generator().manual_seed(0)
-    x = torch.randn(2, 8, 5, 3, generator=g, dtype=dtype, requires_grad=True)
-    w = (torch.rand(8, generator=g, dtype=dtype) + 0.5).requires_grad_() if affine else None
-    b = torch.randn(8, generator=g, dtype=dtype).requires_grad_() if affine else None
-    dy = torch.randn(2, 8, 5, 3, generator=g, dtype=dtype)
-    STOCK[2](x, 4, w, b, 1e-5).backward(dy)
-    gx, gw, gb = _dispatch._group_norm_backward(dy, x.detach(), 4,
-                                                w.detach() if affine else None, 1e-5,
-                                                (True, affine, affine))
-    tol = dict(rtol=1e-4, atol=1e-5) if dtype == torch.float32 else dict(rtol=1e-9, atol=1e-10)
-    torch.testing.assert_close(gx, x.grad, **tol)
-    if affine:
-        torch.testing.assert_close(gw, w.grad, **tol)
-        torch.testing.assert_close(gb, b.grad, **tol)
+# ------------------------------------------------ GroupNorm backward route
+def test_group_norm_backward_routes_to_native_kernel(monkeypatch):
+    """_GroupNormFn's backward is the native b200_gn_bwd (ops.group_norm_backward,
+    faked here); each gradient comes back in its parameter's dtype.  The
+    numerics are checked on the GPU (tests/test_gpu_backward.py)."""
+    seen = []
 
+    def fake(dy, x, G, w, eps, needs, affine_dtype=None):
+        seen.append((G, needs, affine_dtype))
+        C = x.shape[1]
+        return (torch.zeros_like(x) if needs[0] else None,
+                torch.zeros(C, dtype=affine_dtype) if needs[1] else None,
+                torch.zeros(C, dtype=torch.float64) if needs[2] else None)
 
-def test_group_norm_backward_fp16_large_group_no_overflow():
-    """A large fp16 group must not overflow the reductions (fp32 accumulation)."""
-    x = torch.randn(1, 32, 64, 64).half() * 4
+    monkeypatch.setattr(ops, "group_norm_backward", fake)
+    x = torch.randn(2, 8, 5, 3)
     dy = torch.randn_like(x)
-    gx, gw, gb = _dispatch._group_norm_backward(dy, x, 1, torch.ones(32).half(), 1e-5,
-                                                (True, True, True))
-    assert torch.isfinite(gx.float()).all() and torch.isfinite(gw.float()).all()
-    assert torch.isfinite(gb.float()).all()
+    w = torch.rand(8).half()
+    gx, gw, gb = _dispatch._group_norm_backward(dy, x, 4, w, 1e-5, (True, True, True),
+                                                bias_dtype=torch.float32)
+    assert seen == [(4, (True, True, True), torch.float16)]
+    assert gx.shape == x.shape and gw.dtype == torch.float16 and gb.dtype == torch.float32
+    gx, gw, gb = _dispatch._group_norm_backward(dy, x, 4, None, 1e-5, (True, True, False))
+    assert seen[-1] == (4, (True, False, False), torch.float32) and gw is None and gb is None
+
+
+def test_cpu_training_through_patches_stays_stock(patched):
+    """CPU tensors with live gradients go to stock torch in the forward AND
+    the backward (the native backward kernels take CUDA tensors only; a host
+    pointer handed to them would be an illegal address on the GPU)."""
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(2, 8, 5, 5, generator=g, requires_grad=True)
+    w = (torch.rand(8, generator=g) + 0.5).requires_grad_()
+    b = torch.randn(8, generator=g).requires_grad_()
+    F.group_norm(x, 4, w, b, 1e-5).sum().backward()
+    x2, w2, b2 = (t.detach().clone().requires_grad_() for t in (x, w, b))
+    STOCK[2](x2, 4, w2, b2, 1e-5).sum().backward()
+    for a, r in ((x, x2), (w, w2), (b, b2)):
+        torch.testing.assert_close(a.grad, r.grad)
+    s = torch.randn(2, 4, 32, generator=g, requires_grad=True)
+    k = torch.randn(4, 1, 3, generator=g, requires_grad=True)
+    F.conv1d(s, k, None, 1, 1, 1, 4).sum().backward()
+    assert s.grad is not None and k.grad is not None
+
+
+def test_ops_refuse_host_tensors():
+    """Every op that launches a kernel checks its tensors are on the GPU
+    before anything is launched."""
+    x = torch.randn(2, 8, 4, 4)
+    with pytest.raises(ValueError, match="CUDA tensors required"):
+        ops._on_gpu(x)
+    with pytest.raises(ValueError, match="CUDA tensors required"):
+        ops.group_norm_backward(x, x, 4, None, 1e-5, (True, False, False))
+    with pytest.raises(ValueError, match="CUDA tensors required"):
+        ops.depthwise_conv1d_backward(x[:, :, 0], x[:, :, 0], torch.randn(8, 3), 1)

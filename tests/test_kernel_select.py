@@ -34,7 +34,7 @@ def timings(monkeypatch):
             if fn() is None:
                 return None
             return table.get(fn._name)
-        monkeypatch.setattr(kernel_select, "_time", fake_time)
+        monkeypatch.setattr(kernel_select, "_measure", fake_time)
         return calls
     return install
 
@@ -130,7 +130,7 @@ def test_wrong_fast_candidate_is_blacklisted(monkeypatch, timings):
         out = kernel_select.pick("conv3d", x, w, s, p, d,
                                  cands(["bad", "good", "stock"], outputs=outs))
     assert out is outs["good"]
-    key = kernel_select._key("conv3d", x, w, s, p, d)
+    key = kernel_select.shape_key("conv3d", x, w, s, p, d)
     assert kernel_select.debug_bad_candidates()[key] == {"bad"}
 
 
@@ -139,13 +139,32 @@ def test_verification_bar_scales_with_output_rms():
     ref[0] = 1e-3                     # one near-zero element
     cand = ref.clone()
     cand[0] = 2e-3                    # off by 1e-3: fails a plain atol of 1e-5
-    assert kernel_select._verify(cand, ref, tolerance=(1e-4, 1e-5)) is True
+    assert kernel_select._agree(cand, ref, tolerance=(1e-4, 1e-5)) is True
     wrong = ref * 1.01
-    assert kernel_select._verify(wrong, ref, tolerance=(1e-4, 1e-5)) is False
+    assert kernel_select._agree(wrong, ref, tolerance=(1e-4, 1e-5)) is False
 
 
 def test_verify_shape_mismatch_is_a_failure():
-    assert kernel_select._verify(torch.zeros(3), torch.zeros(4)) is False
+    assert kernel_select._agree(torch.zeros(3), torch.zeros(4)) is False
+
+
+def test_verify_non_contiguous_pieces_and_nan(monkeypatch):
+    monkeypatch.setattr(kernel_select, "_PIECE", 64)     # force several pieces
+    ref = torch.randn(7, 5, 9).permute(2, 0, 1)          # non-contiguous view
+    assert kernel_select._agree(ref.clone(), ref) is True
+    bad = ref.clone()
+    bad[8, 6, 4] += 1.0                                  # last element of the last piece
+    assert kernel_select._agree(bad, ref) is False
+    nan_ref = ref.clone()
+    nan_ref[0, 0, 0] = float("nan")
+    assert kernel_select._agree(nan_ref.clone(), nan_ref) is True
+
+
+def test_key_string_round_trip_nested():
+    key = ("conv3d", torch.bfloat16, (1, (2, 3)), 4, False, "x")
+    text = kernel_select.key_string(key)
+    assert kernel_select.parse_key(text) == key
+    assert text.startswith('["conv3d", {"__dtype__": "torch.bfloat16"}, {"__tuple__": [1, ')
 
 
 def test_all_candidates_wrong_falls_back_to_reference(monkeypatch, timings):
@@ -170,7 +189,7 @@ def test_oom_during_deciding_run_is_a_decline(monkeypatch, timings):
     x, w, s, p, d = args()
     stock = ("stock", lambda: "out:stock")
     stock[1]._name = "stock"
-    monkeypatch.setattr(kernel_select, "_time", lambda fn: {"a": 1.0, "stock": 2.0}[fn._name])
+    monkeypatch.setattr(kernel_select, "_measure", lambda fn: {"a": 1.0, "stock": 2.0}[fn._name])
     assert kernel_select.pick("conv3d", x, w, s, p, d, [("a", oom), stock]) == "out:stock"
 
 
@@ -180,7 +199,7 @@ def test_non_oom_errors_propagate_in_the_deciding_run(monkeypatch):
     boom._name = "a"
     ref = lambda: "out:stock"  # noqa: E731
     ref._name = "stock"
-    monkeypatch.setattr(kernel_select, "_time", lambda fn: 1.0)
+    monkeypatch.setattr(kernel_select, "_measure", lambda fn: 1.0)
     x, w, s, p, d = args()
     with pytest.raises(RuntimeError, match="kernel bug"):
         kernel_select.pick("conv3d", x, w, s, p, d, [("a", boom), ("stock", ref)])
@@ -188,7 +207,7 @@ def test_non_oom_errors_propagate_in_the_deciding_run(monkeypatch):
 
 def test_oom_while_verifying_records_nothing(monkeypatch, timings):
     monkeypatch.setattr(kernel_select, "_VERIFY_ENABLED", True)
-    monkeypatch.setattr(kernel_select, "_verify", lambda *a, **k: None)
+    monkeypatch.setattr(kernel_select, "_agree", lambda *a, **k: None)
     timings({"a": 1.0, "stock": 2.0})
     x, w, s, p, d = args()
     with pytest.warns(UserWarning, match="out of memory"):
@@ -203,46 +222,45 @@ def test_disk_cache_roundtrip_and_format(timings, monkeypatch):
     timings({"tcgen05": 1.0, "stock": 2.0})
     x, w, s, p, d = args()
     kernel_select.pick("conv3d", x, w, s, p, d, cands(["tcgen05", "stock"]))
-    path = kernel_select._cache_path()
+    path = kernel_select.cache_file()
     raw = json.load(open(path))
     assert raw["verify_bar"] == kernel_select._VERIFY_BAR_VERSION
     (k, v), = raw["winners"].items()
     assert v == "tcgen05"
     assert json.loads(k)[1] == {"__dtype__": "torch.float32"}
     assert json.loads(k)[2] == {"__tuple__": [1, 4, 8, 8, 8]}
-    with kernel_select._lock:
-        kernel_select._winners.clear()
-    kernel_select._load_disk_cache()
+    kernel_select._book.clear()
+    kernel_select.load_cache_file()
     assert kernel_select.cached("conv3d", x, w, s, p, d) == "tcgen05"
 
 
 def test_stale_verify_bar_drops_blacklist_and_its_winners(tmp_path):
-    key_a = kernel_select._key_to_str(("conv3d", torch.float16, (1,), (2,), (1,), (1,), (1,), False))
-    key_b = kernel_select._key_to_str(("group_norm", torch.bfloat16, (4,), 32, False))
+    key_a = kernel_select.key_string(("conv3d", torch.float16, (1,), (2,), (1,), (1,), (1,), False))
+    key_b = kernel_select.key_string(("group_norm", torch.bfloat16, (4,), 32, False))
     raw = {"verify_bar": 1, "winners": {key_a: "x", key_b: "y"}, "bad": {key_a: ["z"]}}
-    with open(kernel_select._cache_path(), "w") as f:
+    with open(kernel_select.cache_file(), "w") as f:
         json.dump(raw, f)
-    kernel_select._load_disk_cache()
+    kernel_select.load_cache_file()
     winners = kernel_select.debug_winners()
     assert list(winners.values()) == ["y"]
     assert kernel_select.debug_bad_candidates() == {}
 
 
 def test_flat_legacy_file_and_corrupt_file(tmp_path):
-    key = kernel_select._key_to_str(("conv1d", torch.float32, (1,), (1,), (1,), (1,), (1,), False))
-    with open(kernel_select._cache_path(), "w") as f:
+    key = kernel_select.key_string(("conv1d", torch.float32, (1,), (1,), (1,), (1,), (1,), False))
+    with open(kernel_select.cache_file(), "w") as f:
         json.dump({key: "depthwise"}, f)
-    kernel_select._load_disk_cache()
+    kernel_select.load_cache_file()
     assert "depthwise" in kernel_select.debug_winners().values()
-    with open(kernel_select._cache_path(), "w") as f:
+    with open(kernel_select.cache_file(), "w") as f:
         f.write("{not json")
-    kernel_select._load_disk_cache()   # must not raise
+    kernel_select.load_cache_file()   # must not raise
 
 
 def test_reset_removes_the_file(timings):
     timings({"a": 1.0, "stock": 2.0})
     x, w, s, p, d = args()
     kernel_select.pick("conv3d", x, w, s, p, d, cands(["a", "stock"]))
-    assert os.path.exists(kernel_select._cache_path())
+    assert os.path.exists(kernel_select.cache_file())
     kernel_select.reset()
-    assert not os.path.exists(kernel_select._cache_path())
+    assert not os.path.exists(kernel_select.cache_file())

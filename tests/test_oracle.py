@@ -95,3 +95,32 @@ def test_rel_l2_is_scale_free():
     a = np.array([1.0, 2.0, 3.0])
     assert oracle.rel_l2(a, a) == 0.0
     assert abs(oracle.rel_l2(a * 1.01, a) - 0.01) < 1e-12
+
+
+@pytest.mark.parametrize("affine", [True, False])
+def test_group_norm_backward_restatement_matches_autograd(affine):
+    rng = np.random.default_rng(0)
+    x = rng.normal(size=(2, 8, 5, 3)) * 2 + 1
+    dy = rng.normal(size=x.shape)
+    gamma = rng.uniform(0.5, 1.5, size=8) if affine else None
+    beta = rng.normal(size=8) if affine else None
+    dx, dg, db = oracle.np_group_norm_backward(x, dy, 4, gamma, 1e-5)
+    sx, sg, sb = oracle.stock_group_norm_backward(x, dy, 4, gamma, beta, 1e-5)
+    assert oracle.rel_l2(dx, sx) < 1e-5
+    if affine:
+        assert oracle.rel_l2(dg, sg) < 1e-5 and oracle.rel_l2(db, sb) < 1e-5
+
+
+@pytest.mark.parametrize("K,pad,L", [(3, 1, 40), (4, 1, 33), (5, 0, 20), (7, 6, 9), (2, 3, 11)])
+def test_dwconv1d_backward_restatement_matches_autograd(K, pad, L):
+    rng = np.random.default_rng(K * 100 + pad)
+    B, C = 3, 5
+    x = rng.normal(size=(B, C, L))
+    w = rng.normal(size=(C, K))
+    b = rng.normal(size=C)
+    dy = rng.normal(size=(B, C, L + 2 * pad - K + 1))
+    dx, dw, db = oracle.np_dwconv1d_backward(x, dy, w, pad)
+    sx, sw, sb = oracle.stock_dwconv1d_backward(x, dy, w, b, pad)
+    assert oracle.rel_l2(dx, sx) < 1e-5
+    assert oracle.rel_l2(dw, sw.reshape(C, K)) < 1e-5
+    assert oracle.rel_l2(db, sb) < 1e-5

@@ -50,7 +50,7 @@ def _no_alloc(lib, x, G, w, b, eps, stream):
     return y
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_static_scratch_matches_existing_entry_point_twice(dtype):
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
@@ -71,6 +71,44 @@ def test_static_scratch_matches_existing_entry_point_twice(dtype):
         ref = torch.nn.functional.group_norm(x.float().cpu(), G, w.float().cpu(),
                                              b.float().cpu(), eps)
         assert _rel_l2(got.float().cpu(), ref) <= TOL[dtype]
+
+
+def _limit_case(groups: int, dev):
+    """[groups, 1, 65537] fp16: one channel per group, C/G * S = 65537, so
+    every group spans two 65536-element chunks and the scratch need is
+    ceil4(3 * groups) + 3 * groups * 2 floats (65530 at 7281 groups, 65540
+    at 7282)."""
+    g = torch.Generator(device=dev).manual_seed(groups)
+    x = torch.randn(groups, 1, 65537, generator=g, device=dev, dtype=torch.float16)
+    w = torch.full((1,), 1.25, device=dev, dtype=torch.float16)
+    b = torch.full((1,), -0.5, device=dev, dtype=torch.float16)
+    return x, w, b
+
+
+def test_static_scratch_at_its_limit():
+    """The largest accepted problem: the partial statistics reach the end of
+    the array; matches b200_gn_fwd and torch's own CUDA GroupNorm, twice."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from amd_tuned_torch import _lib
+    lib = _lib.lib()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    x, w, b = _limit_case(7281, dev)
+    want = _existing(lib, x, 1, w, b, 1e-5, stream)
+    for _ in range(2):
+        got = _no_alloc(lib, x, 1, w, b, 1e-5, stream)
+        torch.cuda.synchronize()
+        assert _rel_l2(got.float(), want.float()) <= TOL[torch.float16]
+        ref = torch.nn.functional.group_norm(x.float(), 1, w.float(), b.float(), 1e-5)
+        assert _rel_l2(got.float(), ref) <= TOL[torch.float16]
+    del x, got, want, ref
+    x, w, b = _limit_case(7282, dev)
+    y = torch.empty_like(x)
+    rc = lib.b200_gn_fwd_static_scratch(x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(),
+                                        1, 1, 7282, 1, 65537, 1, 1e-5, stream)
+    assert rc == -1
+    assert b"static array holds" in lib.b200_last_error()
 
 
 def test_static_scratch_rejects_oversized_problems():
