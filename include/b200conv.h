@@ -165,14 +165,30 @@ int b200_gn_bwd(const void* x, const void* dy, const float* stats, const void* g
  *   [KD*KH*KW, Cout_pad, Cin_pad] (K-major GEMM B operand, zero padded).
  * b200_conv3d_fwd: x [N, Cin, D, H, W] (x_channels_last = 0) or
  *   [N, D, H, W, Cin] (x_channels_last = 1); y [N, Cout, Do, Ho, Wo] or
- *   channels-last.  Scratch: the channels-last copy of x when x is NCDHW.
- *   params: {stride d,h,w, pad d,h,w, dil d,h,w}. fp16/bf16 only. */
+ *   channels-last.  params: {stride d,h,w, pad d,h,w, dil d,h,w}.
+ *   fp16/bf16 only.  Two kernels: the box-per-tap kernel (stride 1, Cin a
+ *   multiple of 8; scratch = the channels-last copy of an NCDHW x) and the
+ *   slab kernel (any stride <= 4, any Cin; scratch = x staged into zero-
+ *   padded channels-last phase grids, one per stride phase, so every filter
+ *   tap reads the staged rows at a constant offset).  The slab kernel is
+ *   chosen for strides, Cin % 8 != 0 and problems of at most one box tile
+ *   per SM.  variant bits: 0-3 Cout tile (0 auto, 1/2/3 = 64/128/256),
+ *   20 force the slab kernel, 21 never use it, 22 slab kernel without CTA
+ *   pairs, 23 (with 20) the workspace already holds x staged by an earlier
+ *   call on the same shapes (the staging pass is skipped: for timing the
+ *   GEMM alone and for callers that keep the staged layout); the other bits
+ *   select box-kernel options (see conv3d_tc.cu).
+ * b200_conv3d_fwd_workspace_bytes: scratch b200_conv3d_fwd may need for
+ *   this problem (either kernel). */
 size_t b200_conv3d_packed_weight_bytes(int64_t Cout, int64_t Cin, int64_t KD, int64_t KH,
                                        int64_t KW);
 int b200_conv3d_pack_weight(const void* w, void* wp, int dtype, int64_t Cout, int64_t Cin,
                             int64_t KD, int64_t KH, int64_t KW, void* stream);
 size_t b200_conv3d_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
                                    int x_channels_last);
+size_t b200_conv3d_fwd_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                                       int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,
+                                       int x_channels_last);
 int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, int dtype,
                     int bias_dtype, int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
                     int64_t Cout, int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,

@@ -387,14 +387,17 @@ def conv3d(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
            variant: int = 0, x_channels_last: bool = False,
            out_channels_last: bool = False, out: Optional[torch.Tensor] = None,
            gate: Optional[Sequence[int]] = None,
-           weight_key: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+           weight_key: Optional[torch.Tensor] = None,
+           scratch: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
     """Dense conv3d on tensor cores.  x NCDHW (or [N, D, H, W, C] contiguous
     when x_channels_last), w [Cout, Cin, KD, KH, KW].  Returns NCDHW, or an
     [N, Do, Ho, Wo, Cout] contiguous tensor when out_channels_last.
     gate = (epoch, lo, hi, scale) device addresses (lo/hi may be 0) for
     b200_conv3d_fwd_gated: the edge output frames wait for halo arrivals.
     weight_key: the tensor the packed-weight cache is keyed on when w is a
-    per-call view of it (conv2d weights seen as depth 1)."""
+    per-call view of it (conv2d weights seen as depth 1).
+    scratch: a caller-owned uint8 workspace used instead of the per-stream
+    one (with variant bit 23 it must hold x staged by an earlier call)."""
     key = (x.shape, x.dtype, w.shape, w.dtype, tuple(stride), tuple(padding), tuple(dilation),
            variant, x_channels_last, out_channels_last)
     plan = _conv_plans.get(key)
@@ -415,15 +418,30 @@ def conv3d(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
     st = _stream(dev)
     if out is None:
         out = torch.empty(out_shape, dtype=x.dtype, device=dev)
-    ws = workspace(dev, wsb, st) if wsb > 0 else None
+    if scratch is not None:
+        if scratch.numel() < wsb:
+            raise ValueError(f"conv3d scratch holds {scratch.numel()} bytes, needs {wsb}")
+        ws = scratch
+    else:
+        ws = workspace(dev, wsb, st) if wsb > 0 else None
     g_epoch, g_lo, g_hi, g_scale = gate if gate is not None else (None, None, None, 0)
     rc = _lib.lib().b200_conv3d_fwd_gated(
         x.data_ptr(), wp.data_ptr(), bias.data_ptr() if bias is not None else None,
         out.data_ptr(), dcode, DTYPE_CODE[bias.dtype] if bias is not None else 0, *dims, prm,
         int(x_channels_last), int(out_channels_last), variant,
-        ws.data_ptr() if ws is not None else None, wsb, g_epoch or None, g_lo or None,
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+        g_epoch or None, g_lo or None,
         g_hi or None, g_scale, st)
     return out if (rc == 0 or _lib.check(rc, "b200_conv3d_fwd")) else None
+
+
+def conv3d_scratch_bytes(x: torch.Tensor, w: torch.Tensor, stride: Sequence[int],
+                         padding: Sequence[int], dilation: Sequence[int],
+                         x_channels_last: bool = False) -> int:
+    """Workspace bytes ops.conv3d needs for this problem (either kernel)."""
+    plan = _conv3d_plan(x, w, tuple(stride), tuple(padding), tuple(dilation), x_channels_last,
+                        False)
+    return 0 if plan is False else plan[3]
 
 
 # Per call signature (shapes, dtypes, conv parameters, layout flags): the
@@ -453,7 +471,8 @@ def _conv3d_plan(x, w, stride, padding, dilation, x_channels_last, out_channels_
         return False
     out_shape = (N, Do, Ho, Wo, Cout) if out_channels_last else (N, Cout, Do, Ho, Wo)
     prm = (ctypes.c_int64 * 9)(sd, sh, sw, pd, ph, pw, dd, dh, dw)
-    wsb = int(L.b200_conv3d_workspace_bytes(N, Cin, D, H, W, int(x_channels_last)))
+    wsb = int(L.b200_conv3d_fwd_workspace_bytes(N, Cin, D, H, W, KD, KH, KW, prm,
+                                                int(x_channels_last)))
     return (N, Cin, D, H, W, Cout, KD, KH, KW), out_shape, prm, wsb, _code(x.dtype)
 
 

@@ -34,6 +34,7 @@
 #include <mutex>
 #include <type_traits>
 
+#include "conv3d_slab.cuh"
 #include "sm100_ptx.cuh"
 
 namespace b200 {
@@ -803,20 +804,6 @@ to_cl_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t C, int64_t S) {
 }
 
 // ------------------------------------------------------------ host side ---
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
 // Shared memory besides the stages: output staging (when the output goes out
 // through TMA stores), bias, barriers, and the slack for aligning the dynamic
 // base to 1024 bytes.
@@ -882,8 +869,31 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   const int64_t sd = prm9[0], sh = prm9[1], sw = prm9[2];
   const int64_t pd = prm9[3], ph = prm9[4], pw = prm9[5];
   const int64_t dd = prm9[6], dh = prm9[7], dw = prm9[8];
-  if (sd != 1 || sh != 1 || sw != 1) return fail_unsupported("conv3d tensor-core path: stride != 1");
   if (pd < 0 || ph < 0 || pw < 0 || dd < 1 || dh < 1 || dw < 1) return fail_arg("bad padding/dilation");
+  if (sd < 1 || sh < 1 || sw < 1) return fail_arg("bad stride");
+  // Slab path (conv3d_slab.cu): strides, any channel count, and the small
+  // problems where one tile per SM leaves the box kernel latency-bound.
+  // Variant bit 20 forces it, bit 21 rules it out, bit 22 runs it without
+  // CTA pairs.
+  {
+    const bool force = ((variant >> 20) & 1) != 0, never = ((variant >> 21) & 1) != 0;
+    const bool strided = sd != 1 || sh != 1 || sw != 1;
+    bool want = force || strided || Cin % 8 != 0;
+    if (!want && !never && !(gate && gate->epoch)) {
+      // One box-kernel tile (128 positions x BN) per CTA for every SM or fewer.
+      const int64_t Do1 = D + 2 * pd - dd * (KD - 1), Ho1 = H + 2 * ph - dh * (KH - 1),
+                    Wo1 = W + 2 * pw - dw * (KW - 1);
+      const int64_t tiles = N * Do1 * Ho1 * Wo1 / 128 * ((Cout + 127) / 128);
+      want = Do1 > 0 && Ho1 > 0 && Wo1 > 0 && tiles <= sm_count();
+    }
+    if (want && !never && !(gate && gate->epoch)) {
+      const int rc = conv3d_slab<T>(x, wp, bias, y, bias_dt, N, Cin, D, H, W, Cout, KD, KH, KW,
+                                    prm9, x_cl, y_cl, variant & 0xF, ((variant >> 22) & 1) == 0,
+                                    ((variant >> 23) & 1) != 0, ws, ws_bytes, stream);
+      if (rc <= 0 || force || strided || Cin % 8 != 0) return rc;
+    }
+  }
+  if (sd != 1 || sh != 1 || sw != 1) return fail_unsupported("conv3d tensor-core path: stride != 1");
   if (Cin % 8 != 0) return fail_unsupported("conv3d tensor-core path: Cin % 8 != 0");
   const int64_t Do = D + 2 * pd - dd * (KD - 1);
   const int64_t Ho = H + 2 * ph - dh * (KH - 1);
@@ -892,7 +902,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   const int64_t lim = 1LL << 30;
   if (N >= 65536 || D >= lim || H >= lim || W >= lim || Cout >= lim || Cin >= lim)
     return fail_unsupported("conv3d size out of range");
-  auto encode = get_encode_fn();
+  auto encode = tensor_map_encoder();
   if (!encode) return fail_unsupported("cuTensorMapEncodeTiled unavailable");
 
   if (!aligned16(wp)) return fail_unsupported("operands not 16-byte aligned");
@@ -1281,6 +1291,16 @@ size_t b200_conv3d_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H,
                                    int x_channels_last) {
   if (x_channels_last) return 0;
   return static_cast<size_t>(N * Cin * D * H * W) * 2;
+}
+
+size_t b200_conv3d_fwd_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                                       int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,
+                                       int x_channels_last) {
+  if (!params9 || N <= 0 || Cin <= 0 || D <= 0 || H <= 0 || W <= 0) return 0;
+  size_t need = b200_conv3d_workspace_bytes(N, Cin, D, H, W, x_channels_last);
+  const SlabPlan sp = slab_plan(N, Cin, D, H, W, KD, KH, KW, params9);
+  if (sp.ok && sp.staging_bytes > need) need = sp.staging_bytes;
+  return need;
 }
 
 int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, int dtype,

@@ -395,11 +395,62 @@ def test_conv3d_channels_last_io(cuda):
     assert oracle.rel_l2(_np(y.permute(0, 4, 1, 2, 3)), ref) <= 2e-3
 
 
-def test_conv3d_declines_unsupported(cuda):
+# Slab kernel (shifted-window implicit GEMM over staged phase grids):
+# variant bit 20 forces it, 21 rules it out, 22 runs it without CTA pairs.
+_SLAB, _NOSLAB, _NOPAIR = 1 << 20, 1 << 21, 1 << 22
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("N,Cin,D,H,W,Cout,k,s,p,dil,cl,variant", [
+    (1, 64, 16, 32, 32, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), False, _SLAB),
+    (1, 64, 16, 32, 32, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), False, _SLAB | _NOPAIR),
+    (2, 64, 16, 32, 32, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), False, _SLAB),
+    (2, 32, 5, 9, 13, 48, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), False, _SLAB),
+    (1, 128, 3, 8, 8, 128, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), False, _SLAB),
+    (1, 72, 3, 5, 5, 300, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), False, _SLAB | _NOPAIR),
+    (1, 72, 3, 5, 5, 300, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), False, _SLAB),
+    (1, 3, 8, 16, 16, 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), False, 0),
+    (1, 12, 4, 4, 4, 8, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), True, 0),
+    (1, 16, 9, 17, 17, 24, (3, 3, 3), (2, 2, 2), (1, 1, 1), (1, 1, 1), False, 0),
+    (2, 32, 8, 16, 16, 64, (3, 3, 3), (1, 2, 2), (1, 1, 1), (1, 1, 1), False, 0),
+    (1, 16, 6, 10, 10, 16, (4, 4, 4), (2, 2, 2), (1, 1, 1), (1, 1, 1), True, 0),
+    (1, 8, 7, 11, 12, 16, (3, 2, 3), (3, 2, 1), (0, 1, 2), (1, 1, 2), False, 0),
+    (1, 64, 4, 16, 130, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), (1, 1, 1), False, _SLAB),
+    (1, 32, 5, 10, 10, 40, (3, 3, 3), (1, 1, 1), (2, 2, 2), (2, 2, 2), True, _SLAB),
+    (1, 16, 2, 3, 200, 80, (1, 1, 3), (1, 1, 1), (0, 0, 1), (1, 1, 1), False, _SLAB),
+])
+def test_conv3d_slab(cuda, dt, N, Cin, D, H, W, Cout, k, s, p, dil, cl, variant):
+    """The slab kernel against stock CPU fp32: one and several tiles per CTA,
+    CTA pairs and single CTAs, several channel chunks and Cout tiles,
+    strides (phase grids), Cin not a multiple of 8, dilation, wide rows
+    (slabs split per filter row), channels-last input and output."""
     from amd_tuned_torch import ops
-    x = torch.randn(1, 12, 4, 4, 4, device=cuda, dtype=torch.half)   # Cin % 8 != 0
-    w = torch.randn(8, 12, 3, 3, 3, device=cuda, dtype=torch.half)
-    assert ops.conv3d(x, w, None, (1, 1, 1), (1, 1, 1), (1, 1, 1)) is None
-    x = torch.randn(1, 16, 4, 4, 4, device=cuda, dtype=torch.half)
-    w = torch.randn(8, 16, 3, 3, 3, device=cuda, dtype=torch.half)
-    assert ops.conv3d(x, w, None, (2, 2, 2), (1, 1, 1), (1, 1, 1)) is None   # stride 2
+    g = torch.Generator().manual_seed(Cin * 3 + Cout + sum(s) + variant % 97)
+    x = torch.randn(N, Cin, D, H, W, generator=g).to(torch_dtype(dt))
+    w = _kaiming((Cout, Cin) + k, g).to(torch_dtype(dt))
+    b = torch.randn(Cout, generator=g).to(torch_dtype(dt)) * 0.1
+    ref = torch.nn.functional.conv3d(x.float(), w.float(), b.float(), stride=s, padding=p,
+                                     dilation=dil)
+    xin = x.permute(0, 2, 3, 4, 1).contiguous() if cl else x
+    y = ops.conv3d(xin.to(cuda), w.to(cuda), b.to(cuda), s, p, dil, variant=variant,
+                   x_channels_last=cl, out_channels_last=cl)
+    assert y is not None
+    torch.cuda.synchronize()
+    got = _np(y.permute(0, 4, 1, 2, 3)) if cl else _np(y)
+    assert got.shape == tuple(ref.shape)
+    assert oracle.rel_l2(got, ref.numpy()) <= TOL[dt]
+    _no_fault()
+
+
+def test_conv3d_slab_matches_box_kernel(cuda):
+    """Both kernels on the cfg2 problem agree to fp32-accumulation rounding
+    (they sum the same products in different orders)."""
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(1, 64, 16, 32, 32, generator=g).half().to(cuda)
+    w = _kaiming((64, 64, 3, 3, 3), g).half().to(cuda)
+    b = (torch.randn(64, generator=g) * 0.1).half().to(cuda)
+    a = ops.conv3d(x, w, b, (1, 1, 1), (1, 1, 1), (1, 1, 1), variant=_SLAB)
+    c = ops.conv3d(x, w, b, (1, 1, 1), (1, 1, 1), (1, 1, 1), variant=_NOSLAB)
+    assert oracle.rel_l2(_np(a), _np(c)) <= 1e-3
+    _no_fault()
