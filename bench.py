@@ -537,16 +537,34 @@ def run_ours(args, rank, world, dev) -> dict:
     ms_per_step = ms_max / args.steps
     value = ms_max * 1e3 / (args.steps * world)
 
-    # Dominant kernel alone (the tcgen05 GEMM on a channels-last operand).
-    xcl = [ops.to_channels_last(xs[i]).reshape(1, 16, 32, 32, 64) for i in range(nbuf)]
-    for i in range(3):
-        ops.conv3d(xcl[i % nbuf], wd, bd, (1, 1, 1), (1, 1, 1), (1, 1, 1), x_channels_last=True,
-                   out=ys[i % nbuf])
-    k_ms = _graph_time(lambda i: ops.conv3d(xcl[i % nbuf], wd, bd, (1, 1, 1), (1, 1, 1),
-                                            (1, 1, 1), x_channels_last=True, out=ys[i % nbuf]),
-                       max(args.steps, 50), stream)
+    # Dominant kernel alone: the tcgen05 GEMM without the layout pass in
+    # front of it.  Slab kernel (what the step runs on cfg2): inputs staged
+    # once into enough scratch buffers to exceed L2, then K GEMM launches
+    # over them (variant bit 23 skips the staging).  Box kernel: the same on
+    # channels-last copies of x.
+    P3 = ((1, 1, 1), (1, 1, 1), (1, 1, 1))
+    slab = ops.conv3d_uses_slab(xd, wd, *P3)
+    if slab:
+        wsb = ops.conv3d_scratch_bytes(xd, wd, *P3)
+        nst = _nbuf(wsb + x.numel() * 2, 4)
+        scr = [torch.empty(wsb, dtype=torch.uint8, device=dev) for _ in range(nst)]
+        for i in range(nst):
+            ops.conv3d(xs[i % nbuf], wd, bd, *P3, out=ys[i % nbuf], scratch=scr[i])
+        k_ms = _graph_time(lambda i: ops.conv3d(xs[i % nbuf], wd, bd, *P3,
+                                                variant=ops.CONV3D_SLAB | ops.CONV3D_STAGED,
+                                                out=ys[i % nbuf], scratch=scr[i % nst]),
+                           max(args.steps, 50), stream)
+        kname = "conv3d_slab_kernel"
+        del scr
+    else:
+        xcl = [ops.to_channels_last(xs[i]).reshape(1, 16, 32, 32, 64) for i in range(nbuf)]
+        for i in range(3):
+            ops.conv3d(xcl[i % nbuf], wd, bd, *P3, x_channels_last=True, out=ys[i % nbuf])
+        k_ms = _graph_time(lambda i: ops.conv3d(xcl[i % nbuf], wd, bd, *P3, x_channels_last=True,
+                                                out=ys[i % nbuf]), max(args.steps, 50), stream)
+        kname = "conv3d_tc_kernel"
+        del xcl
     achieved = CFG2_FLOPS / (k_ms * 1e-3) / 1e12
-    del xcl
 
     # e2e through the public API: every step copies its input from pinned host
     # memory, runs the patched F.conv3d and copies the result back to pinned
@@ -571,7 +589,7 @@ def run_ours(args, rank, world, dev) -> dict:
         dist.barrier()
         sharded = sharded_shapes(rank, world, dev, peaks, shapes)
     cpu = cpu_baseline(x, w, b) if (rank == 0 and world == 1) else None
-    tr = _traffic("conv3d_tc_kernel")
+    tr = _traffic(kname)
     return {
         "metric": "conv3d fp16 cfg2 (N=1,C64->64,16x32x32,k3,p1) us/op",
         "value": value, "unit": "us/op", "n_gpus": world, "steps": args.steps,
@@ -586,7 +604,7 @@ def run_ours(args, rank, world, dev) -> dict:
         "roofline": {"bound": "tensor", "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"],
-                     "traffic": tr, "kernel": "conv3d_tc_kernel",
+                     "traffic": tr, "kernel": kname,
                      "kernel_us": k_ms * 1e3, "peak_src": peaks["src"] + " burst bf16"},
         "e2e": {"value": e2e_value, "unit": "us/op",
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,

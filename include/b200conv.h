@@ -166,29 +166,41 @@ int b200_gn_bwd(const void* x, const void* dy, const float* stats, const void* g
  * b200_conv3d_fwd: x [N, Cin, D, H, W] (x_channels_last = 0) or
  *   [N, D, H, W, Cin] (x_channels_last = 1); y [N, Cout, Do, Ho, Wo] or
  *   channels-last.  params: {stride d,h,w, pad d,h,w, dil d,h,w}.
- *   fp16/bf16 only.  Two kernels: the box-per-tap kernel (stride 1, Cin a
+ *   fp16/bf16, and fp32 through the slab kernel on bf16 hi/lo splits of x
+ *   and w (x_hi w_hi + x_lo w_hi + x_hi w_lo, fp32 accumulation and output;
+ *   about 16 significant bits kept per operand, rel-L2 ~5e-6 against fp32
+ *   on unit-scale data; weights packed by b200_conv3d_pack_weight with
+ *   dtype fp32, b200_conv3d_packed_weight_bytes_for bytes).  Two kernels: the box-per-tap kernel (stride 1, Cin a
  *   multiple of 8; scratch = the channels-last copy of an NCDHW x) and the
  *   slab kernel (any stride <= 4, any Cin; scratch = x staged into zero-
  *   padded channels-last phase grids, one per stride phase, so every filter
  *   tap reads the staged rows at a constant offset).  The slab kernel is
- *   chosen for strides, Cin % 8 != 0 and problems of at most one box tile
- *   per SM.  variant bits: 0-3 Cout tile (0 auto, 1/2/3 = 64/128/256),
+ *   chosen for strides and Cin % 8 != 0.  variant bits: 0-3 Cout tile (0 auto, 1/2/3 = 64/128/256),
  *   20 force the slab kernel, 21 never use it, 22 slab kernel without CTA
  *   pairs, 23 (with 20) the workspace already holds x staged by an earlier
  *   call on the same shapes (the staging pass is skipped: for timing the
  *   GEMM alone and for callers that keep the staged layout); the other bits
  *   select box-kernel options (see conv3d_tc.cu).
  * b200_conv3d_fwd_workspace_bytes: scratch b200_conv3d_fwd may need for
- *   this problem (either kernel). */
+ *   this problem (either kernel).
+ * b200_conv3d_uses_slab: 1 when b200_conv3d_fwd with this variant runs the
+ *   slab kernel (ungated calls), else 0. */
 size_t b200_conv3d_packed_weight_bytes(int64_t Cout, int64_t Cin, int64_t KD, int64_t KH,
                                        int64_t KW);
+/* Packed size for a weight of `dtype`: fp32 weights pack as three bf16
+ * K blocks [hi | hi | lo] per tap (3x the 16-bit size). */
+size_t b200_conv3d_packed_weight_bytes_for(int64_t Cout, int64_t Cin, int64_t KD, int64_t KH,
+                                           int64_t KW, int dtype);
 int b200_conv3d_pack_weight(const void* w, void* wp, int dtype, int64_t Cout, int64_t Cin,
                             int64_t KD, int64_t KH, int64_t KW, void* stream);
 size_t b200_conv3d_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
                                    int x_channels_last);
+int b200_conv3d_uses_slab(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                          int64_t Cout, int64_t KD, int64_t KH, int64_t KW,
+                          const int64_t* params9, int dtype, int variant);
 size_t b200_conv3d_fwd_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
                                        int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,
-                                       int x_channels_last);
+                                       int dtype, int x_channels_last);
 int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, int dtype,
                     int bias_dtype, int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
                     int64_t Cout, int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,

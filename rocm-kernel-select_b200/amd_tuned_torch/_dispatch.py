@@ -171,15 +171,42 @@ def _fftconv3d_candidate(input, weight, bias, stride, padding, dilation, groups)
     return ("fftconv", thunk)
 
 
+class _ExactFp32:
+    """cuDNN may run fp32 convolutions on TF32 tensor cores (torch's default,
+    ~1e-3 relative error); as the verification reference of an fp32 contest
+    stock must compute in fp32."""
+
+    def __enter__(self):
+        self.saved = torch.backends.cudnn.allow_tf32
+        torch.backends.cudnn.allow_tf32 = False
+
+    def __exit__(self, *exc):
+        torch.backends.cudnn.allow_tf32 = self.saved
+
+
 def _conv3d_candidates(input, weight, bias, stride, padding, dilation, groups):
     orig = _STOCK["conv3d"]
     cands = []
-    if _usable(input, weight, bias, dtypes=_CONV_TC_DTYPES) and _lib.available():
+    if _usable(input, weight, bias, dtypes=_FFTCONV_CONV_DTYPES) and _lib.available():
+        # fp16 / bf16, and fp32 as bf16 hi/lo splits (slab kernel).
         cands.append(("tcgen05", _conv3d_tc_thunk(input, weight, bias, stride, padding, dilation)))
+        if (input.dtype != torch.float32 and _triple(stride) == (1, 1, 1)
+                and input.shape[1] % 8 == 0):
+            # Stride-1 problems with whole channel vectors run on the box
+            # kernel by default; the slab kernel competes for them here.
+            cands.append(("tcgen05_slab", _conv3d_tc_thunk(input, weight, bias, stride, padding,
+                                                           dilation, variant=ops.CONV3D_SLAB)))
     fft = _fftconv3d_candidate(input, weight, bias, stride, padding, dilation, groups)
     if fft is not None:
         cands.append(fft)
-    cands.append(("stock", lambda: orig(input, weight, bias, stride, padding, dilation, groups)))
+    if input.dtype == torch.float32:
+        def stock():
+            with _ExactFp32():
+                return orig(input, weight, bias, stride, padding, dilation, groups)
+    else:
+        def stock():
+            return orig(input, weight, bias, stride, padding, dilation, groups)
+    cands.append(("stock", stock))
     return cands, fft
 
 
@@ -197,11 +224,12 @@ def _conv3d_accelerated_forward(input, weight, bias, stride, padding, dilation, 
             if _DEBUG:
                 _debug("conv3d", "stock", "cached winner", input=input)
             return orig(input, weight, bias, stride, padding, dilation, groups)
-        if won == "tcgen05":
-            out = _conv3d_tc_thunk(input, weight, bias, stride, padding, dilation)()
+        if won in ("tcgen05", "tcgen05_slab"):
+            var = ops.CONV3D_SLAB if won == "tcgen05_slab" else 0
+            out = _conv3d_tc_thunk(input, weight, bias, stride, padding, dilation, variant=var)()
             if out is not None:
                 if _DEBUG:
-                    _debug("conv3d", "tcgen05", "cached winner", input=input)
+                    _debug("conv3d", won, "cached winner", input=input)
                 return out
         cands, fft = _conv3d_candidates(input, weight, bias, stride, padding, dilation, groups)
         if _DEBUG:

@@ -57,7 +57,9 @@ SIGNATURES = {
     "b200_conv3d_pack_weight": (c_int, [c_vp, c_vp, c_int, c_int64, c_int64, c_int64, c_int64,
                                         c_int64, c_vp]),
     "b200_conv3d_workspace_bytes": (c_size_t, [c_int64] * 5 + [c_int]),
-    "b200_conv3d_fwd_workspace_bytes": (c_size_t, [c_int64] * 8 + [c_i64p, c_int]),
+    "b200_conv3d_fwd_workspace_bytes": (c_size_t, [c_int64] * 8 + [c_i64p, c_int, c_int]),
+    "b200_conv3d_uses_slab": (c_int, [c_int64] * 9 + [c_i64p, c_int, c_int]),
+    "b200_conv3d_packed_weight_bytes_for": (c_size_t, [c_int64] * 5 + [c_int]),
     "b200_conv3d_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 9
                         + [c_i64p, c_int, c_int, c_int, c_vp, c_size_t, c_vp]),
     "b200_conv3d_fwd_gated": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 9

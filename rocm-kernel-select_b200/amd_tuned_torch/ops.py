@@ -372,8 +372,10 @@ def conv3d_packed_weight(w: torch.Tensor, key: Optional[torch.Tensor] = None) ->
     L = _lib.lib()
     _on_gpu(w)
     Cout, Cin, KD, KH, KW = w.shape
-    nbytes = L.b200_conv3d_packed_weight_bytes(Cout, Cin, KD, KH, KW)
-    wp = torch.empty(nbytes // 2, dtype=w.dtype, device=w.device)
+    nbytes = L.b200_conv3d_packed_weight_bytes_for(Cout, Cin, KD, KH, KW, _code(w.dtype))
+    # fp32 weights pack as bf16 hi/lo blocks; 16-bit weights keep their dtype.
+    pdt = torch.bfloat16 if w.dtype == torch.float32 else w.dtype
+    wp = torch.empty(nbytes // 2, dtype=pdt, device=w.device)
     rc = L.b200_conv3d_pack_weight(w.contiguous().data_ptr(), wp.data_ptr(), _code(w.dtype),
                                    Cout, Cin, KD, KH, KW, _stream(w.device))
     if not _lib.check(rc, "b200_conv3d_pack_weight"):
@@ -389,7 +391,8 @@ def conv3d(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
            gate: Optional[Sequence[int]] = None,
            weight_key: Optional[torch.Tensor] = None,
            scratch: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
-    """Dense conv3d on tensor cores.  x NCDHW (or [N, D, H, W, C] contiguous
+    """Dense conv3d on tensor cores (fp16 / bf16; fp32 through bf16 hi/lo
+    splits with fp32 accumulation).  x NCDHW (or [N, D, H, W, C] contiguous
     when x_channels_last), w [Cout, Cin, KD, KH, KW].  Returns NCDHW, or an
     [N, Do, Ho, Wo, Cout] contiguous tensor when out_channels_last.
     gate = (epoch, lo, hi, scale) device addresses (lo/hi may be 0) for
@@ -444,6 +447,23 @@ def conv3d_scratch_bytes(x: torch.Tensor, w: torch.Tensor, stride: Sequence[int]
     return 0 if plan is False else plan[3]
 
 
+CONV3D_SLAB, CONV3D_NO_SLAB, CONV3D_SLAB_NO_PAIRS, CONV3D_STAGED = 1 << 20, 1 << 21, 1 << 22, 1 << 23
+
+
+def conv3d_uses_slab(x: torch.Tensor, w: torch.Tensor, stride: Sequence[int],
+                     padding: Sequence[int], dilation: Sequence[int], variant: int = 0,
+                     x_channels_last: bool = False) -> bool:
+    """Whether ops.conv3d runs this problem on the slab kernel."""
+    if x_channels_last:
+        N, D, H, W, Cin = x.shape
+    else:
+        N, Cin, D, H, W = x.shape
+    Cout, _, KD, KH, KW = w.shape
+    prm = (ctypes.c_int64 * 9)(*stride, *padding, *dilation)
+    return bool(_lib.lib().b200_conv3d_uses_slab(N, Cin, D, H, W, Cout, KD, KH, KW, prm,
+                                                 _code(x.dtype), variant))
+
+
 # Per call signature (shapes, dtypes, conv parameters, layout flags): the
 # derived sizes, output shape and packed parameter array, or False when the
 # kernel cannot take it.  Keeps the per-call host work to a dict lookup.
@@ -452,7 +472,7 @@ _conv_plans: dict = {}
 
 def _conv3d_plan(x, w, stride, padding, dilation, x_channels_last, out_channels_last):
     L = _lib.lib()
-    if x.dtype not in (torch.float16, torch.bfloat16) or w.dtype != x.dtype:
+    if x.dtype not in (torch.float16, torch.bfloat16, torch.float32) or w.dtype != x.dtype:
         return False
     if x_channels_last:
         N, D, H, W, Cin = x.shape
@@ -472,7 +492,7 @@ def _conv3d_plan(x, w, stride, padding, dilation, x_channels_last, out_channels_
     out_shape = (N, Do, Ho, Wo, Cout) if out_channels_last else (N, Cout, Do, Ho, Wo)
     prm = (ctypes.c_int64 * 9)(sd, sh, sw, pd, ph, pw, dd, dh, dw)
     wsb = int(L.b200_conv3d_fwd_workspace_bytes(N, Cin, D, H, W, KD, KH, KW, prm,
-                                                int(x_channels_last)))
+                                                _code(x.dtype), int(x_channels_last)))
     return (N, Cin, D, H, W, Cout, KD, KH, KW), out_shape, prm, wsb, _code(x.dtype)
 
 

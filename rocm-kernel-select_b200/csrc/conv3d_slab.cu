@@ -49,6 +49,7 @@ constexpr int kSlabMaxGroups = 128;
 constexpr int kSlabMaxTaps = 1024;
 constexpr int kSlabMaxA = 4;
 constexpr int kSlabMaxW = 32;
+constexpr int kSlabStageTaps = 12;     // most weight boxes behind one W barrier
 constexpr int kSlabM = 128;            // output positions per CTA tile
 constexpr int kSlabMaxRows = 256;      // TMA box limit along a dimension
 constexpr size_t kSlabSmemBudget = 232448;
@@ -65,9 +66,10 @@ struct SlabTap {
 };
 
 struct SlabParams {
-  int n_groups, n_chunks;
+  int n_groups, n_taps, n_chunks;
   int slab_rows;                       // rows of every slab load (the TMA box height)
   int a_slot_bytes, a_slots, w_slot_bytes, w_slots;
+  int w_box_bytes, w_taps;             // one tap's weight box; taps per W slot (one barrier)
   int tiles_per_batch, tiles_n, num_tiles;
   int batch_rows;                      // staged rows per batch inside one phase grid
   int Hq, Wq, Do, Ho, Wo, Cout, positions;
@@ -80,11 +82,39 @@ struct SlabParams {
   SlabTap taps[kSlabMaxTaps];
 };
 
+// Order of work inside a tile.  Tiles start their walk at different units
+// and taps: CTAs in lockstep would otherwise all request the same weight box
+// at the same moment, and those few L2 lines become a hot spot every CTA
+// queues on.  The order depends on the tile only, so a tile's accumulation
+// order (and rounding) does not depend on the grid or the schedule.
+__device__ __forceinline__ int unit_start(int t, int units) {
+  return static_cast<int>((static_cast<uint32_t>(t) * 7u) % static_cast<uint32_t>(units));
+}
+__device__ __forceinline__ int tap_start(int t, int count) {
+  return static_cast<int>((static_cast<uint32_t>(t) * 5u + 3u * (static_cast<uint32_t>(t) >> 3)) %
+                          static_cast<uint32_t>(count));
+}
+
+// Slot and phase of a ring of barriers, advanced without divisions (the
+// producer and MMA loops are short enough that integer division by a
+// runtime ring size would dominate them).
+struct Ring {
+  int slot;
+  uint32_t phase;
+  int n;
+  __device__ __forceinline__ void advance() {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 // Rows a pair-tile / CTA-tile covers.
 template <bool PAIR>
 __device__ __forceinline__ int tile_rows() { return PAIR ? 2 * kSlabM : kSlabM; }
 
-template <typename T, int BN, bool PAIR>
+template <typename T, typename TO, int BN, bool PAIR>
 __global__ void __launch_bounds__(kSlabThreads, 1)
 conv3d_slab_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmw,
                    const __grid_constant__ SlabParams p) {
@@ -116,6 +146,11 @@ conv3d_slab_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constan
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // The group / tap tables, copied out of the parameter block once: read
+  // through a pointer, the parameter space costs a long-latency load per
+  // access, and the producer and MMA loops read them on every tap.
+  SlabGroup* groups = reinterpret_cast<SlabGroup*>(tmem_slot + 4);
+  SlabTap* taps = reinterpret_cast<SlabTap*>(groups + p.n_groups);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -137,6 +172,8 @@ conv3d_slab_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constan
     *abort = 0;
     fence_barrier_init();
   }
+  for (int i = threadIdx.x; i < p.n_groups; i += kSlabThreads) groups[i] = p.groups[i];
+  for (int i = threadIdx.x; i < p.n_taps; i += kSlabThreads) taps[i] = p.taps[i];
   if (warp == 1) {
     if (PAIR)
       tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -152,99 +189,93 @@ conv3d_slab_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constan
 
   if (warp == 0) {
     // -------------------------------------------------------- TMA producer
-    // Unit u = (group g, channel chunk c): one slab into an A slot, then one
+    // Unit = (group, channel chunk): one slab into an A slot, then one
     // weight box per tap of the group into W slots.  Every copy of a pair
     // completes on the leader's barriers (the leader's MMAs read both CTAs).
-    int a_it = 0, w_it = 0;
-    bool ok = true, waited = false;
-    // Weight boxes of the first unit do not depend on the previous kernel:
-    // when the host allows it they are requested before griddepcontrol.wait
-    // (while the staging kernel is still finishing).
-    int pre = 0, pre0 = 0;
-    if (p.hoist_w && tile0 < p.num_tiles) {
-      const int n0 = (tile0 % p.tiles_n) * BN;
-      const SlabGroup& g0 = p.groups[0];
-      pre = g0.tap_count < p.w_slots ? g0.tap_count : p.w_slots;
-      pre0 = pre;
-      if (lane == 0) {
-        for (int j = 0; j < pre; ++j) {
-          const int slot = j;
-          uint8_t* dst = sW + slot * p.w_slot_bytes;
-          if (PAIR) {
-            if (leader) mbar_expect_tx(&wfull[slot], 2u * p.w_slot_bytes);
-            tma_load_3d_pair(dst, &tmw, mapa_u32(&wfull[slot], 0), 0,
-                             n0 + static_cast<int>(crank) * kBNl, p.taps[g0.tap_begin + j].wtap);
-          } else {
-            mbar_expect_tx(&wfull[slot], p.w_slot_bytes);
-            tma_load_3d(dst, &tmw, &wfull[slot], 0, n0, p.taps[g0.tap_begin + j].wtap);
-          }
-        }
-      }
-      __syncwarp();
-    }
+    // Weight boxes do not depend on the previous kernel: when the host allows
+    // it, those of the very first unit (as many as the ring holds) are
+    // requested before griddepcontrol.wait, while the staging kernel is
+    // still finishing.
+    Ring ar{0, 0u, p.a_slots}, wr{0, 0u, p.w_slots};
+    int a_issued = 0, w_issued = 0;
+    bool ok = true, waited = p.hoist_w == 0;
+    if (waited) pdl_wait();
     for (int t = tile0; t < p.num_tiles && ok; t += tstep) {
       const int nt = t % p.tiles_n;
       const int pt = (t / p.tiles_n) % p.tiles_per_batch;
       const int nb = t / (p.tiles_n * p.tiles_per_batch);
-      const int n0 = nt * BN;
-      const int q0 = pt * tile_rows<PAIR>() + static_cast<int>(crank) * kSlabM;
-      const int base = nb * p.batch_rows + q0;
-      for (int u = 0; u < units && ok; ++u) {
-        const SlabGroup& g = p.groups[u / p.n_chunks];
-        const int c = u % p.n_chunks;
-        {
-          const int slot = a_it % p.a_slots;
-          const uint32_t ph = static_cast<uint32_t>(a_it / p.a_slots) & 1u;
-          const bool got = mbar_wait_bounded(&aempty[slot], ph ^ 1u, abort, p.flags, 1);
+      const int n0w = nt * BN + static_cast<int>(crank) * kBNl;
+      const int base = nb * p.batch_rows + pt * tile_rows<PAIR>() + static_cast<int>(crank) * kSlabM;
+      const int u0 = unit_start(t, units);
+      int gi = u0 / p.n_chunks, ci = u0 - (u0 / p.n_chunks) * p.n_chunks;
+      for (int uk = 0; uk < units && ok; ++uk) {
+        const SlabGroup g = groups[gi];
+        int j = tap_start(t, g.tap_count);
+        // W stages of this unit: up to w_taps weight boxes on one barrier.
+        const int stages = (g.tap_count + p.w_taps - 1) / p.w_taps;
+        const int early = waited ? 0 : (stages < p.w_slots ? stages : p.w_slots);
+        for (int k = 0; k <= stages && ok; ++k) {
+          if (k == early) {
+            // The slab of this unit, after the early weight stages.
+            if (!waited) {
+              pdl_wait();
+              waited = true;
+            }
+            const bool got = mbar_wait_bounded(&aempty[ar.slot], ar.phase ^ 1u, abort, p.flags, 1);
+            if (!__all_sync(0xffffffffu, got)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              uint8_t* dst = sA + ar.slot * p.a_slot_bytes;
+              const uint32_t bytes = static_cast<uint32_t>(p.slab_rows) * 128u;
+              if (PAIR) {
+                if (leader) mbar_expect_tx(&afull[ar.slot], 2u * bytes);
+                tma_load_2d_pair(dst, &tma, mapa_u32(&afull[ar.slot], 0), ci * 64, g.a_off + base);
+              } else {
+                mbar_expect_tx(&afull[ar.slot], bytes);
+                tma_load_2d(dst, &tma, &afull[ar.slot], ci * 64, g.a_off + base);
+              }
+            }
+            __syncwarp();
+            ar.advance();
+            ++a_issued;
+          }
+          if (k == stages) break;
+          const int nb_taps = (k == stages - 1) ? g.tap_count - k * p.w_taps : p.w_taps;
+          const bool got = mbar_wait_bounded(&wempty[wr.slot], wr.phase ^ 1u, abort, p.flags, 1);
           if (!__all_sync(0xffffffffu, got)) {
             ok = false;
             break;
           }
-          if (!waited) {
-            pdl_wait();
-            waited = true;
-          }
           if (lane == 0) {
-            uint8_t* dst = sA + slot * p.a_slot_bytes;
-            const uint32_t bytes = static_cast<uint32_t>(p.slab_rows) * 128u;
+            uint8_t* dst = sW + wr.slot * p.w_slot_bytes;
+            const uint32_t bytes = static_cast<uint32_t>(nb_taps * p.w_box_bytes);
             if (PAIR) {
-              if (leader) mbar_expect_tx(&afull[slot], 2u * bytes);
-              tma_load_2d_pair(dst, &tma, mapa_u32(&afull[slot], 0), c * 64, g.a_off + base);
+              if (leader) mbar_expect_tx(&wfull[wr.slot], 2u * bytes);
             } else {
-              mbar_expect_tx(&afull[slot], bytes);
-              tma_load_2d(dst, &tma, &afull[slot], c * 64, g.a_off + base);
+              mbar_expect_tx(&wfull[wr.slot], bytes);
+            }
+            int jj = j;
+            for (int e = 0; e < nb_taps; ++e) {
+              const int wtap = taps[g.tap_begin + jj].wtap;
+              if (PAIR)
+                tma_load_3d_pair(dst + e * p.w_box_bytes, &tmw, mapa_u32(&wfull[wr.slot], 0),
+                                 ci * 64, n0w, wtap);
+              else
+                tma_load_3d(dst + e * p.w_box_bytes, &tmw, &wfull[wr.slot], ci * 64, n0w, wtap);
+              if (++jj == g.tap_count) jj = 0;
             }
           }
           __syncwarp();
-          ++a_it;
+          j += nb_taps;
+          if (j >= g.tap_count) j -= g.tap_count;
+          wr.advance();
+          ++w_issued;
         }
-        for (int j = 0; j < g.tap_count && ok; ++j) {
-          if (pre > 0) {   // issued before the wait
-            --pre;
-            ++w_it;
-            continue;
-          }
-          const int slot = w_it % p.w_slots;
-          const uint32_t ph = static_cast<uint32_t>(w_it / p.w_slots) & 1u;
-          const bool got = mbar_wait_bounded(&wempty[slot], ph ^ 1u, abort, p.flags, 1);
-          if (!__all_sync(0xffffffffu, got)) {
-            ok = false;
-            break;
-          }
-          if (lane == 0) {
-            uint8_t* dst = sW + slot * p.w_slot_bytes;
-            const int wtap = p.taps[g.tap_begin + j].wtap;
-            if (PAIR) {
-              if (leader) mbar_expect_tx(&wfull[slot], 2u * p.w_slot_bytes);
-              tma_load_3d_pair(dst, &tmw, mapa_u32(&wfull[slot], 0), c * 64,
-                               n0 + static_cast<int>(crank) * kBNl, wtap);
-            } else {
-              mbar_expect_tx(&wfull[slot], p.w_slot_bytes);
-              tma_load_3d(dst, &tmw, &wfull[slot], c * 64, n0, wtap);
-            }
-          }
-          __syncwarp();
-          ++w_it;
+        if (++ci == p.n_chunks) {
+          ci = 0;
+          if (++gi == p.n_groups) gi = 0;
         }
       }
     }
@@ -253,11 +284,10 @@ conv3d_slab_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constan
       // Let every copy already issued land before shared memory goes away
       // (a pair's copies all complete on the leader's barriers): for each
       // slot, the phase of the last load issued into it.
-      for (int s = 0; s < p.a_slots && s < a_it; ++s) {
-        const int cnt = (a_it - 1 - s) / p.a_slots + 1;
+      for (int s = 0; s < p.a_slots && s < a_issued; ++s) {
+        const int cnt = (a_issued - 1 - s) / p.a_slots + 1;
         mbar_wait_bounded(&afull[s], static_cast<uint32_t>(cnt - 1) & 1u, nullptr, nullptr, 0);
       }
-      const int w_issued = w_it > pre0 ? w_it : pre0;
       for (int s = 0; s < p.w_slots && s < w_issued; ++s) {
         const int cnt = (w_issued - 1 - s) / p.w_slots + 1;
         mbar_wait_bounded(&wfull[s], static_cast<uint32_t>(cnt - 1) & 1u, nullptr, nullptr, 0);
@@ -269,7 +299,8 @@ conv3d_slab_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constan
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     pdl_wait();
-    int a_it = 0, w_it = 0, it = 0;
+    Ring ar{0, 0u, p.a_slots}, wr{0, 0u, p.w_slots};
+    int it = 0;
     bool ok = true;
     for (int t = tile0; t < p.num_tiles && ok; t += tstep, ++it) {
       const int acc = it & 1;
@@ -281,62 +312,82 @@ conv3d_slab_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constan
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-      bool first = true;
-      for (int u = 0; u < units && ok; ++u) {
-        const SlabGroup& g = p.groups[u / p.n_chunks];
-        const int aslot = a_it % p.a_slots;
-        const bool got_a = mbar_wait_bounded(&afull[aslot],
-                                             static_cast<uint32_t>(a_it / p.a_slots) & 1u, abort,
-                                             p.flags, 1);
+      uint32_t accum = 0u;
+      const int u0 = unit_start(t, units);
+      int gi = u0 / p.n_chunks, ci = u0 - (u0 / p.n_chunks) * p.n_chunks;
+      for (int uk = 0; uk < units && ok; ++uk) {
+        const SlabGroup g = groups[gi];
+        const bool got_a = mbar_wait_bounded(&afull[ar.slot], ar.phase, abort, p.flags, 1);
         if (!__all_sync(0xffffffffu, got_a)) {
           ok = false;
           break;
         }
-        const uint32_t a_base = smem_u32(sA + aslot * p.a_slot_bytes);
-        for (int j = 0; j < g.tap_count; ++j) {
-          const int wslot = w_it % p.w_slots;
-          const bool got_w = mbar_wait_bounded(&wfull[wslot],
-                                               static_cast<uint32_t>(w_it / p.w_slots) & 1u, abort,
-                                               p.flags, 1);
+        const uint32_t a_base = smem_u32(sA + ar.slot * p.a_slot_bytes);
+        int j = tap_start(t, g.tap_count);
+        const int stages = (g.tap_count + p.w_taps - 1) / p.w_taps;
+        for (int k = 0; k < stages; ++k) {
+          const int nb_taps = (k == stages - 1) ? g.tap_count - k * p.w_taps : p.w_taps;
+          const bool got_w = mbar_wait_bounded(&wfull[wr.slot], wr.phase, abort, p.flags, 1);
           if (!__all_sync(0xffffffffu, got_w)) {
             ok = false;
             break;
           }
           tc_fence_after();
           if (lane == 0) {
-            const uint64_t adesc =
-                umma_desc_sw128(a_base + static_cast<uint32_t>(p.taps[g.tap_begin + j].off) * 128u);
-            const uint64_t bdesc = umma_desc_sw128(smem_u32(sW + wslot * p.w_slot_bytes));
+            // Every descriptor of the stage first (the tap table lives in
+            // shared memory), then the MMAs back to back.
+            const uint32_t w_base = smem_u32(sW + wr.slot * p.w_slot_bytes);
+            uint32_t a_at[kSlabStageTaps];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t accum = (first && k == 0) ? 0u : 1u;
-              if (PAIR)
-                umma_f16_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc, accum);
-              else
-                umma_f16_ss(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc, accum);
+            for (int e = 0; e < kSlabStageTaps; ++e) {
+              a_at[e] = a_base + static_cast<uint32_t>(taps[g.tap_begin + j].off) * 128u;
+              if (e < nb_taps && ++j == g.tap_count) j = 0;
+            }
+#pragma unroll
+            for (int e = 0; e < kSlabStageTaps; ++e) {
+              if (e < nb_taps) {
+                const uint64_t adesc = umma_desc_sw128(a_at[e]);
+                const uint64_t bdesc =
+                    umma_desc_sw128(w_base + static_cast<uint32_t>(e * p.w_box_bytes));
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                  if (PAIR)
+                    umma_f16_ss_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, kIdesc, accum);
+                  else
+                    umma_f16_ss(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, kIdesc, accum);
+                  accum = 1u;
+                }
+              }
             }
             if (PAIR) {
-              umma_commit_pair(smem_u32(&wempty[wslot]));
-              umma_commit_pair(mapa_u32(&wempty[wslot], 1));
+              umma_commit_pair(smem_u32(&wempty[wr.slot]));
+              umma_commit_pair(mapa_u32(&wempty[wr.slot], 1));
             } else {
-              umma_commit(&wempty[wslot]);
+              umma_commit(&wempty[wr.slot]);
             }
+          } else {
+            j += nb_taps;
+            if (j >= g.tap_count) j -= g.tap_count;
           }
           __syncwarp();
-          first = false;
-          ++w_it;
+          accum = 1u;
+          wr.advance();
         }
         if (!ok) break;
         if (lane == 0) {
           if (PAIR) {
-            umma_commit_pair(smem_u32(&aempty[aslot]));
-            umma_commit_pair(mapa_u32(&aempty[aslot], 1));
+            umma_commit_pair(smem_u32(&aempty[ar.slot]));
+            umma_commit_pair(mapa_u32(&aempty[ar.slot], 1));
           } else {
-            umma_commit(&aempty[aslot]);
+            umma_commit(&aempty[ar.slot]);
           }
         }
         __syncwarp();
-        ++a_it;
+        ar.advance();
+        if (++ci == p.n_chunks) {
+          ci = 0;
+          if (++gi == p.n_groups) gi = 0;
+        }
       }
       if (ok && lane == 0) {
         if (PAIR) {
@@ -363,7 +414,7 @@ conv3d_slab_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constan
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int etid = threadIdx.x - 64;
-    T* y = static_cast<T*>(p.y);
+    TO* y = static_cast<TO*>(p.y);
     const int64_t HWq = static_cast<int64_t>(p.Hq) * p.Wq;
     const int64_t plane = static_cast<int64_t>(p.Ho) * p.Wo;
     int it = 0;
@@ -400,25 +451,29 @@ conv3d_slab_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constan
         for (int j = 0; j < 32; ++j) v[j] = (j < 16 ? v0[j] : v1[j - 16]) + sBias[j0 + j];
         if (!valid) continue;
         if (p.y_cl) {
-          T* dst = y + (nb * p.Do * plane + pos) * p.Cout + n0 + j0;
-          if (n0 + j0 + 32 <= p.Cout && (p.Cout & 7) == 0) {
+          TO* dst = y + (nb * p.Do * plane + pos) * p.Cout + n0 + j0;
+          constexpr int V = Vec16<TO>::N;
+          if (n0 + j0 + 32 <= p.Cout && p.Cout % V == 0) {
 #pragma unroll
-            for (int g8 = 0; g8 < 4; ++g8) {
-              float f[8];
+            for (int g8 = 0; g8 < 32 / V; ++g8) {
+              float f[V];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) f[e] = v[8 * g8 + e];
-              *reinterpret_cast<uint4*>(dst + 8 * g8) = pack16<T>(f);
+              for (int e = 0; e < V; ++e) f[e] = v[V * g8 + e];
+              *reinterpret_cast<uint4*>(dst + V * g8) = pack16<TO>(f);
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n0 + j0 + j < p.Cout) dst[j] = from_f32<T>(v[j]);
+              if (n0 + j0 + j < p.Cout) dst[j] = from_f32<TO>(v[j]);
           }
         } else {
+          const int64_t cstride = static_cast<int64_t>(p.Do) * plane;
+          TO* dst = y + (nb * p.Cout + n0 + j0) * cstride + pos;
+          const int nco = p.Cout - (n0 + j0);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int co = n0 + j0 + j;
-            if (co < p.Cout) y[((nb * p.Cout + co) * p.Do) * plane + pos] = from_f32<T>(v[j]);
+            if (j < nco) *dst = from_f32<TO>(v[j]);
+            dst += cstride;
           }
         }
       }
@@ -480,40 +535,53 @@ slab_stage_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t N, int64
   const int64_t npos = min64(64, Wq - w0);
   const int64_t orow = ((phase * N + n) * Dq + dq) * Hq * Wq + hq * Wq + w0;   // first out position
   if (CL_IN) {
-    // 16-byte vectors of 8 channels; scalar when C is not a multiple of 8.
-    for (int i = threadIdx.x; i < npos * 8; i += 256) {
+    // 16-byte vectors of 8 channels (scalar when C is not a multiple of 8):
+    // both vectors of a thread are loaded before either is stored.
+    uint4 q[2];
+    int64_t dst[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = threadIdx.x + 256 * k;
       const int pi = i >> 3, v = i & 7;
       const int64_t c = c0 + 8 * v;
-      if (c >= Cp) continue;
       const int64_t w = (w0 + pi) * sw + rw - pw;
-      uint4 q = make_uint4(0, 0, 0, 0);
-      if (row_in && w >= 0 && w < W && c < C) {
+      q[k] = make_uint4(0, 0, 0, 0);
+      dst[k] = (pi < npos && c < Cp) ? (orow + pi) * Cp + c : -1;
+      if (dst[k] >= 0 && row_in && w >= 0 && w < W && c < C) {
         const T* src = x + (((n * D + d) * H + h) * W + w) * C + c;
         if ((C & 7) == 0) {
-          q = *reinterpret_cast<const uint4*>(src);
+          q[k] = *reinterpret_cast<const uint4*>(src);
         } else {
           uint16_t e[8];
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            e[k] = (c + k < C) ? reinterpret_cast<const uint16_t*>(src)[k] : uint16_t(0);
-          q = make_uint4(e[0] | (uint32_t(e[1]) << 16), e[2] | (uint32_t(e[3]) << 16),
-                         e[4] | (uint32_t(e[5]) << 16), e[6] | (uint32_t(e[7]) << 16));
+          for (int j = 0; j < 8; ++j)
+            e[j] = (c + j < C) ? reinterpret_cast<const uint16_t*>(src)[j] : uint16_t(0);
+          q[k] = make_uint4(e[0] | (uint32_t(e[1]) << 16), e[2] | (uint32_t(e[3]) << 16),
+                            e[4] | (uint32_t(e[5]) << 16), e[6] | (uint32_t(e[7]) << 16));
         }
       }
-      *reinterpret_cast<uint4*>(out + (orow + pi) * Cp + c) = q;
     }
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      if (dst[k] >= 0) *reinterpret_cast<uint4*>(out + dst[k]) = q[k];
     return;
   }
-  // NCDHW: channel rows of the input along w into tile[c][pos] ...
-  for (int i = threadIdx.x; i < 64 * 64; i += 256) {
-    const int cc = i >> 6, pi = i & 63;
-    const int64_t c = c0 + cc;
-    const int64_t w = (w0 + pi) * sw + rw - pw;
-    uint16_t v = 0;
-    if (row_in && pi < npos && c < C && w >= 0 && w < W)
-      v = reinterpret_cast<const uint16_t*>(x)[(((n * C + c) * D + d) * H + h) * W + w];
-    tile[cc][pi] = v;
+  // NCDHW: channel rows of the input along w into tile[c][pos] -- all 16
+  // loads of a thread in flight before the first shared-memory store ...
+  const uint16_t* x16 = reinterpret_cast<const uint16_t*>(x);
+  const int pi = threadIdx.x & 63;
+  const int64_t w = (w0 + pi) * sw + rw - pw;
+  const bool col_in = row_in && pi < npos && w >= 0 && w < W;
+  const int64_t plane_in = D * H * W;
+  const int64_t src0 = ((n * C + c0) * D + d) * H * W + h * W + w;
+  uint16_t v[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int cc = (threadIdx.x >> 6) + 4 * k;
+    v[k] = (col_in && c0 + cc < C) ? x16[src0 + cc * plane_in] : uint16_t(0);
   }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) tile[(threadIdx.x >> 6) + 4 * k][pi] = v[k];
   __syncthreads();
   // ... then 16-byte vectors of 8 channels per position.
   for (int i = threadIdx.x; i < npos * 8; i += 256) {
@@ -529,11 +597,124 @@ slab_stage_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t N, int64
   }
 }
 
-size_t slab_fixed_smem(int BN) {
-  return static_cast<size_t>(BN) * 4 + (2 * kSlabMaxA + 2 * kSlabMaxW + 5) * 8 + 16 + 1024;
+// fp32 x -> phase grids of bf16 pairs: each staged position holds three
+// channel blocks of Cq = Cin rounded up to 64, [hi | lo | hi] with hi =
+// bf16(x) and lo = bf16(x - hi).  Against weights packed as [hi | hi | lo]
+// (pack_weight_split_kernel) the GEMM over the concatenated K computes
+// x_hi w_hi + x_lo w_hi + x_hi w_lo: x and w each kept to about 16
+// significant bits, fp32 accumulation, the x_lo w_lo term (2^-16 relative)
+// dropped.  Same CTA geometry as slab_stage_kernel.
+template <bool CL_IN>
+__global__ void __launch_bounds__(256)
+slab_stage_split_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out, int64_t N,
+                        int64_t C, int64_t D, int64_t H, int64_t W, int64_t Cq, int64_t Dq,
+                        int64_t Hq, int64_t Wq, int sd, int sh, int sw, int pd, int ph, int pw,
+                        int wblocks) {
+  __shared__ float tile[64][65];
+  pdl_launch_dependents();
+  const int64_t rowblk = blockIdx.x;
+  const int wb = static_cast<int>(rowblk % wblocks);
+  int64_t r = rowblk / wblocks;
+  const int64_t hq = r % Hq;
+  r /= Hq;
+  const int64_t dq = r % Dq;
+  r /= Dq;
+  const int64_t n = r % N;
+  const int64_t phase = r / N;
+  const int rw = static_cast<int>(phase % sw);
+  const int rh = static_cast<int>((phase / sw) % sh);
+  const int rd = static_cast<int>(phase / (sw * sh));
+  const int64_t d = dq * sd + rd - pd, h = hq * sh + rh - ph;
+  const bool row_in = d >= 0 && d < D && h >= 0 && h < H;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 64;
+  const int64_t w0 = static_cast<int64_t>(wb) * 64;
+  const int64_t npos = min64(64, Wq - w0);
+  const int64_t orow = ((phase * N + n) * Dq + dq) * Hq * Wq + hq * Wq + w0;
+  float v[16];
+  if (CL_IN) {
+    // consecutive threads read consecutive channels of one position
+    const int cc = threadIdx.x & 63;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int pi = (threadIdx.x >> 6) + 4 * k;
+      const int64_t w = (w0 + pi) * sw + rw - pw;
+      v[k] = (row_in && pi < npos && w >= 0 && w < W && c0 + cc < C)
+                 ? x[(((n * D + d) * H + h) * W + w) * C + c0 + cc]
+                 : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) tile[cc][(threadIdx.x >> 6) + 4 * k] = v[k];
+  } else {
+    const int pi = threadIdx.x & 63;
+    const int64_t w = (w0 + pi) * sw + rw - pw;
+    const bool col_in = row_in && pi < npos && w >= 0 && w < W;
+    const int64_t plane_in = D * H * W;
+    const int64_t src0 = ((n * C + c0) * D + d) * H * W + h * W + w;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int cc = (threadIdx.x >> 6) + 4 * k;
+      v[k] = (col_in && c0 + cc < C) ? x[src0 + cc * plane_in] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) tile[(threadIdx.x >> 6) + 4 * k][pi] = v[k];
+  }
+  __syncthreads();
+  const int64_t Ct = 3 * Cq;
+  for (int i = threadIdx.x; i < npos * 8; i += 256) {
+    const int pi = i >> 3, vg = i & 7;
+    const int64_t c = c0 + 8 * vg;
+    if (c >= Cq) continue;
+    float hi[8], lo[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float f = tile[8 * vg + k][pi];
+      hi[k] = __bfloat162float(__float2bfloat16_rn(f));
+      lo[k] = f - hi[k];
+    }
+    __nv_bfloat16* dst = out + (orow + pi) * Ct + c;
+    const uint4 qh = pack16<__nv_bfloat16>(hi), ql = pack16<__nv_bfloat16>(lo);
+    *reinterpret_cast<uint4*>(dst) = qh;
+    *reinterpret_cast<uint4*>(dst + Cq) = ql;
+    *reinterpret_cast<uint4*>(dst + 2 * Cq) = qh;
+  }
+}
+
+// w [Cout][Cin][taps] fp32 -> [taps][Cout][3 Cq] bf16 as [hi | hi | lo]
+// (zero beyond Cin in each block).
+__global__ void pack_weight_split_kernel(const float* __restrict__ w, __nv_bfloat16* __restrict__ wp,
+                                         int64_t Cout, int64_t Cin, int64_t Cq, int64_t taps) {
+  const int64_t Ct = 3 * Cq;
+  const int64_t total = taps * Cout * Ct;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t k3 = i % Ct;
+    const int64_t co = (i / Ct) % Cout;
+    const int64_t tap = i / (Ct * Cout);
+    const int64_t part = k3 / Cq, ci = k3 - part * Cq;
+    const float v = ci < Cin ? w[(co * Cin + ci) * taps + tap] : 0.f;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    wp[i] = part == 2 ? __float2bfloat16_rn(v - __bfloat162float(hi)) : hi;
+  }
+}
+
+size_t slab_fixed_smem(int BN, int n_groups, int n_taps) {
+  return static_cast<size_t>(BN) * 4 + (2 * kSlabMaxA + 2 * kSlabMaxW + 5) * 8 + 16 +
+         static_cast<size_t>(n_groups) * sizeof(SlabGroup) +
+         static_cast<size_t>(n_taps) * sizeof(SlabTap) + 1024;
 }
 
 }  // namespace
+
+int pack_weight_split(const float* w, __nv_bfloat16* wp, int64_t Cout, int64_t Cin, int64_t KD,
+                      int64_t KH, int64_t KW, cudaStream_t stream) {
+  const int64_t Cq = (Cin + 63) / 64 * 64;
+  const int64_t taps = KD * KH * KW;
+  const int64_t total = taps * Cout * 3 * Cq;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 65536));
+  pack_weight_split_kernel<<<grid, 256, 0, stream>>>(w, wp, Cout, Cin, Cq, taps);
+  B200_LAUNCH_CHECK("pack_weight_split_kernel");
+  return B200_OK;
+}
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -550,7 +731,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 SlabPlan slab_plan(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int64_t KD,
-                   int64_t KH, int64_t KW, const int64_t* prm) {
+                   int64_t KH, int64_t KW, const int64_t* prm, bool split) {
   SlabPlan s;
   const int64_t sd = prm[0], sh = prm[1], sw = prm[2];
   const int64_t pd = prm[3], ph = prm[4], pw = prm[5];
@@ -569,7 +750,7 @@ SlabPlan slab_plan(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int6
   s.Dq = (Dp + sd - 1) / sd;
   s.Hq = (Hp + sh - 1) / sh;
   s.Wq = (Wp + sw - 1) / sw;
-  s.Cp = (Cin + 7) / 8 * 8;
+  s.Cp = split ? 3 * ((Cin + 63) / 64 * 64) : (Cin + 7) / 8 * 8;
   s.rows = s.phases * N * s.Dq * s.Hq * s.Wq;
   if (s.rows + 2 * kSlabMaxRows >= (1LL << 31)) return s;
   s.staging_bytes = static_cast<size_t>(s.rows * s.Cp) * 2;
@@ -577,13 +758,17 @@ SlabPlan slab_plan(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int6
   return s;
 }
 
-template <typename T>
+template <typename TIN>
 int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bias_dt,
                 int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int64_t Cout,
                 int64_t KD, int64_t KH, int64_t KW, const int64_t* prm, int x_cl, int y_cl,
                 int bn_code, bool pair, bool staged, void* ws, size_t ws_bytes,
                 cudaStream_t stream) {
-  const SlabPlan sp = slab_plan(N, Cin, D, H, W, KD, KH, KW, prm);
+  // fp32: bf16 hi/lo operands (three K blocks), fp32 output.
+  constexpr bool kSplit = std::is_same<TIN, float>::value;
+  using T = typename std::conditional<kSplit, __nv_bfloat16, TIN>::type;
+  using TO = TIN;
+  const SlabPlan sp = slab_plan(N, Cin, D, H, W, KD, KH, KW, prm, kSplit);
   if (!sp.ok) return fail_unsupported("conv3d slab path: geometry");
   auto encode = tensor_map_encoder();
   if (!encode) return fail_unsupported("cuTensorMapEncodeTiled unavailable");
@@ -641,6 +826,7 @@ int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bi
     max_taps = std::max(max_taps, g.tap_count);
   }
   p.n_groups = ng;
+  p.n_taps = nt;
   p.n_chunks = static_cast<int>((sp.Cp + 63) / 64);
   p.slab_rows = max_rows;
 
@@ -648,10 +834,17 @@ int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bi
   if (pair && BN > 128) BN = 128;
   const int BNl = pair ? BN / 2 : BN;
   p.a_slot_bytes = (max_rows * 128 + 1023) / 1024 * 1024;
-  p.w_slot_bytes = BNl * 128;
-  const size_t budget = kSlabSmemBudget - slab_fixed_smem(BN);
+  p.w_box_bytes = BNl * 128;
+  // Taps per W slot: a whole group when it fits in about a fifth of shared
+  // memory (one barrier round trip per group), else fewer.
+  p.w_taps = std::max(1, std::min({max_taps, static_cast<int>(44 * 1024 / p.w_box_bytes),
+                                    kSlabStageTaps}));
+  p.w_slot_bytes = p.w_taps * p.w_box_bytes;
+  const size_t budget = kSlabSmemBudget - slab_fixed_smem(BN, ng, nt);
   const int units = p.n_groups * p.n_chunks;
-  const int total_w = ng > 0 ? nt * p.n_chunks : 0;
+  int total_w = 0;
+  for (int gg = 0; gg < ng; ++gg)
+    total_w += (p.groups[gg].tap_count + p.w_taps - 1) / p.w_taps * p.n_chunks;
   p.a_slots = std::min(kSlabMaxA, std::max(2, std::min(units, 3)));
   if (units == 1) p.a_slots = 1;
   while (p.a_slots > 1 && static_cast<size_t>(p.a_slots) * p.a_slot_bytes + 2ull * p.w_slot_bytes > budget)
@@ -662,7 +855,6 @@ int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bi
                                                  static_cast<size_t>(std::max(total_w, 2))}));
   if (p.w_slots < 2 || (units > 1 && p.a_slots < 2))
     return fail_unsupported("conv3d slab path: shared memory");
-  (void)max_taps;
 
   // Stage the input (same stream; the conv overlaps its tail through PDL),
   // unless the caller staged it into the workspace already.
@@ -671,21 +863,32 @@ int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bi
     const int64_t rowsblk = sp.phases * N * sp.Dq * sp.Hq * wblocks;
     if (rowsblk > 0x7fffffffLL || (sp.Cp + 63) / 64 > 65535)
       return fail_unsupported("conv3d slab path: staging grid");
-    dim3 grid(static_cast<unsigned>(rowsblk), static_cast<unsigned>((sp.Cp + 63) / 64));
-    const T* xs = static_cast<const T*>(x);
+    const int64_t cq = kSplit ? sp.Cp / 3 : sp.Cp;   // input channels staged per block
+    dim3 grid(static_cast<unsigned>(rowsblk), static_cast<unsigned>((cq + 63) / 64));
     T* out = static_cast<T*>(ws);
     const int isd = static_cast<int>(sp.s_d), ish = static_cast<int>(sp.s_h),
               isw = static_cast<int>(sp.s_w);
     const int ipd = static_cast<int>(prm[3]), iph = static_cast<int>(prm[4]),
               ipw = static_cast<int>(prm[5]);
-    if (x_cl)
-      slab_stage_kernel<T, true><<<grid, 256, 0, stream>>>(xs, out, N, Cin, D, H, W, sp.Cp, sp.Dq,
-                                                           sp.Hq, sp.Wq, isd, ish, isw, ipd, iph,
-                                                           ipw, wblocks);
-    else
-      slab_stage_kernel<T, false><<<grid, 256, 0, stream>>>(xs, out, N, Cin, D, H, W, sp.Cp, sp.Dq,
-                                                            sp.Hq, sp.Wq, isd, ish, isw, ipd, iph,
-                                                            ipw, wblocks);
+    if constexpr (kSplit) {
+      const float* xs = static_cast<const float*>(x);
+      if (x_cl)
+        slab_stage_split_kernel<true><<<grid, 256, 0, stream>>>(
+            xs, out, N, Cin, D, H, W, cq, sp.Dq, sp.Hq, sp.Wq, isd, ish, isw, ipd, iph, ipw, wblocks);
+      else
+        slab_stage_split_kernel<false><<<grid, 256, 0, stream>>>(
+            xs, out, N, Cin, D, H, W, cq, sp.Dq, sp.Hq, sp.Wq, isd, ish, isw, ipd, iph, ipw, wblocks);
+    } else {
+      const T* xs = static_cast<const T*>(x);
+      if (x_cl)
+        slab_stage_kernel<T, true><<<grid, 256, 0, stream>>>(xs, out, N, Cin, D, H, W, sp.Cp,
+                                                             sp.Dq, sp.Hq, sp.Wq, isd, ish, isw,
+                                                             ipd, iph, ipw, wblocks);
+      else
+        slab_stage_kernel<T, false><<<grid, 256, 0, stream>>>(xs, out, N, Cin, D, H, W, sp.Cp,
+                                                              sp.Dq, sp.Hq, sp.Wq, isd, ish, isw,
+                                                              ipd, iph, ipw, wblocks);
+    }
     B200_LAUNCH_CHECK("slab_stage_kernel");
   }
 
@@ -703,7 +906,7 @@ int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bi
     if (r != CUDA_SUCCESS) return fail_unsupported("conv3d slab path: staged tensor map rejected");
   }
   {
-    const int64_t Cin_pad = (Cin + 63) / 64 * 64;
+    const int64_t Cin_pad = kSplit ? sp.Cp : (Cin + 63) / 64 * 64;   // packed K per tap
     const int64_t taps = KD * KH * KW;
     cuuint64_t dims[3] = {(cuuint64_t)Cin_pad, (cuuint64_t)Cout, (cuuint64_t)taps};
     cuuint64_t strides[2] = {(cuuint64_t)(Cin_pad * 2), (cuuint64_t)(Cout * Cin_pad * 2)};
@@ -742,7 +945,7 @@ int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bi
   p.flags = device_flags_ptr();
 
   const size_t smem = static_cast<size_t>(p.a_slots) * p.a_slot_bytes +
-                      static_cast<size_t>(p.w_slots) * p.w_slot_bytes + slab_fixed_smem(BN);
+                      static_cast<size_t>(p.w_slots) * p.w_slot_bytes + slab_fixed_smem(BN, ng, nt);
   if (smem > kSlabSmemBudget) return fail_unsupported("conv3d slab path: shared memory");
   cudaLaunchConfig_t cfg = {};
   const int sms = sm_count();
@@ -762,7 +965,7 @@ int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bi
   cfg.numAttrs = pair ? 2 : 1;
 #define B200_SLAB_LAUNCH(BNV, PR)                                                               \
   do {                                                                                         \
-    auto kern = conv3d_slab_kernel<T, BNV, PR>;                                                \
+    auto kern = conv3d_slab_kernel<T, TO, BNV, PR>;                                                \
     B200_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
                                          static_cast<int>(smem)));                             \
     B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tma, tmw, p));                              \
@@ -784,6 +987,10 @@ int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bi
   return B200_OK;
 }
 
+template int conv3d_slab<float>(const void*, const void*, const void*, void*, int, int64_t,
+                                int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                                int64_t, const int64_t*, int, int, int, bool, bool, void*,
+                                size_t, cudaStream_t);
 template int conv3d_slab<__half>(const void*, const void*, const void*, void*, int, int64_t,
                                  int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
                                  int64_t, const int64_t*, int, int, int, bool, bool, void*,

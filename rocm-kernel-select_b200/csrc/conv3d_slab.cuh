@@ -27,15 +27,23 @@ struct SlabPlan {
 
 // Plans the slab path for x [N, Cin, D, H, W] (16-bit) and a KD x KH x KW
 // filter with params9 = (stride, padding, dilation) x (d, h, w).
+// split: fp32 input staged as bf16 [hi | lo | hi] channel blocks.
 SlabPlan slab_plan(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int64_t KD,
-                   int64_t KH, int64_t KW, const int64_t* params9);
+                   int64_t KH, int64_t KW, const int64_t* params9, bool split);
 
-// Stages x into the phase grids and runs the slab kernel.  Returns
+// fp32 weights [Cout, Cin, KD, KH, KW] -> bf16 [taps][Cout][3 Cq] as
+// [hi | hi | lo] blocks (Cq = Cin rounded up to 64), the operand that pairs
+// with the split staging of an fp32 input.
+int pack_weight_split(const float* w, __nv_bfloat16* wp, int64_t Cout, int64_t Cin, int64_t KD,
+                      int64_t KH, int64_t KW, cudaStream_t stream);
+
+// Stages x into the phase grids and runs the slab kernel (TIN = float: the
+// split fp32 form with fp32 output).  Returns
 // B200_UNSUPPORTED when the problem does not fit the kernel (the caller then
 // uses the box-per-tap kernel).  `pair` selects CTA pairs (cta_group::2);
 // `staged` skips the staging pass (the workspace already holds this x
 // staged by an earlier call).
-template <typename T>
+template <typename TIN>
 int conv3d_slab(const void* x, const void* wp, const void* bias, void* y, int bias_dt,
                 int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int64_t Cout,
                 int64_t KD, int64_t KH, int64_t KW, const int64_t* params9, int x_cl, int y_cl,

@@ -860,6 +860,23 @@ struct HaloGate {
   uint32_t scale;
 };
 
+// Whether b200_conv3d_fwd takes the slab path: variant bit 20 forces it and
+// bit 21 rules it out; otherwise only strides and channel counts that are
+// not a multiple of 8, which only it handles.  (On stride-1 problems it is
+// not faster than the box kernel: with 64 output channels both are bound by
+// the operand bytes every M = 128, N = 64 MMA reads from shared memory, and
+// its staging pass and 13% of discarded rows cost more than the input bytes
+// it saves; the kernel_select contest times both where both apply.)  Never
+// with a halo gate.
+bool slab_wanted(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int64_t Cout,
+                 int64_t KD, int64_t KH, int64_t KW, const int64_t* prm9, int variant,
+                 bool gated) {
+  (void)N, (void)D, (void)H, (void)W, (void)Cout, (void)KD, (void)KH, (void)KW;
+  if (gated || ((variant >> 21) & 1) != 0) return false;
+  if (((variant >> 20) & 1) != 0) return true;
+  return prm9[0] != 1 || prm9[1] != 1 || prm9[2] != 1 || Cin % 8 != 0;
+}
+
 template <typename T>
 int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int bias_dt,
                  int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W, int64_t Cout,
@@ -873,25 +890,12 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   if (sd < 1 || sh < 1 || sw < 1) return fail_arg("bad stride");
   // Slab path (conv3d_slab.cu): strides, any channel count, and the small
   // problems where one tile per SM leaves the box kernel latency-bound.
-  // Variant bit 20 forces it, bit 21 rules it out, bit 22 runs it without
-  // CTA pairs.
-  {
-    const bool force = ((variant >> 20) & 1) != 0, never = ((variant >> 21) & 1) != 0;
-    const bool strided = sd != 1 || sh != 1 || sw != 1;
-    bool want = force || strided || Cin % 8 != 0;
-    if (!want && !never && !(gate && gate->epoch)) {
-      // One box-kernel tile (128 positions x BN) per CTA for every SM or fewer.
-      const int64_t Do1 = D + 2 * pd - dd * (KD - 1), Ho1 = H + 2 * ph - dh * (KH - 1),
-                    Wo1 = W + 2 * pw - dw * (KW - 1);
-      const int64_t tiles = N * Do1 * Ho1 * Wo1 / 128 * ((Cout + 127) / 128);
-      want = Do1 > 0 && Ho1 > 0 && Wo1 > 0 && tiles <= sm_count();
-    }
-    if (want && !never && !(gate && gate->epoch)) {
-      const int rc = conv3d_slab<T>(x, wp, bias, y, bias_dt, N, Cin, D, H, W, Cout, KD, KH, KW,
-                                    prm9, x_cl, y_cl, variant & 0xF, ((variant >> 22) & 1) == 0,
-                                    ((variant >> 23) & 1) != 0, ws, ws_bytes, stream);
-      if (rc <= 0 || force || strided || Cin % 8 != 0) return rc;
-    }
+  if (slab_wanted(N, Cin, D, H, W, Cout, KD, KH, KW, prm9, variant, gate && gate->epoch)) {
+    const bool only = ((variant >> 20) & 1) != 0 || sd != 1 || sh != 1 || sw != 1 || Cin % 8 != 0;
+    const int rc = conv3d_slab<T>(x, wp, bias, y, bias_dt, N, Cin, D, H, W, Cout, KD, KH, KW,
+                                  prm9, x_cl, y_cl, variant & 0xF, ((variant >> 22) & 1) == 0,
+                                  ((variant >> 23) & 1) != 0, ws, ws_bytes, stream);
+    if (rc <= 0 || only) return rc;
   }
   if (sd != 1 || sh != 1 || sw != 1) return fail_unsupported("conv3d tensor-core path: stride != 1");
   if (Cin % 8 != 0) return fail_unsupported("conv3d tensor-core path: Cin % 8 != 0");
@@ -1266,12 +1270,20 @@ size_t b200_conv3d_packed_weight_bytes(int64_t Cout, int64_t Cin, int64_t KD, in
   return static_cast<size_t>(KD * KH * KW * Cout * Cin_pad) * 2;
 }
 
+size_t b200_conv3d_packed_weight_bytes_for(int64_t Cout, int64_t Cin, int64_t KD, int64_t KH,
+                                           int64_t KW, int dtype) {
+  const size_t b16 = b200_conv3d_packed_weight_bytes(Cout, Cin, KD, KH, KW);
+  return dtype == B200_DTYPE_F32 ? 3 * b16 : b16;
+}
+
 int b200_conv3d_pack_weight(const void* w, void* wp, int dtype, int64_t Cout, int64_t Cin,
                             int64_t KD, int64_t KH, int64_t KW, void* stream) {
   if (!w || !wp) return fail_arg("w/wp is NULL");
-  if (dtype != B200_DTYPE_F16 && dtype != B200_DTYPE_BF16)
-    return fail_unsupported("conv3d tensor-core path: fp16/bf16 only");
   if (Cout <= 0 || Cin <= 0 || KD <= 0 || KH <= 0 || KW <= 0) return fail_arg("bad size");
+  if (dtype == B200_DTYPE_F32)
+    return pack_weight_split(static_cast<const float*>(w), static_cast<__nv_bfloat16*>(wp), Cout,
+                             Cin, KD, KH, KW, static_cast<cudaStream_t>(stream));
+  if (dtype != B200_DTYPE_F16 && dtype != B200_DTYPE_BF16) return fail_arg("bad dtype");
   const int64_t Cin_pad = (Cin + kBK - 1) / kBK * kBK;
   const int64_t taps = KD * KH * KW;
   const int64_t total = taps * Cout * Cin_pad;
@@ -1293,12 +1305,21 @@ size_t b200_conv3d_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H,
   return static_cast<size_t>(N * Cin * D * H * W) * 2;
 }
 
+int b200_conv3d_uses_slab(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
+                          int64_t Cout, int64_t KD, int64_t KH, int64_t KW,
+                          const int64_t* params9, int dtype, int variant) {
+  if (!params9) return 0;
+  if (dtype == B200_DTYPE_F32) return 1;
+  return slab_wanted(N, Cin, D, H, W, Cout, KD, KH, KW, params9, variant, false) ? 1 : 0;
+}
+
 size_t b200_conv3d_fwd_workspace_bytes(int64_t N, int64_t Cin, int64_t D, int64_t H, int64_t W,
                                        int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,
-                                       int x_channels_last) {
+                                       int dtype, int x_channels_last) {
   if (!params9 || N <= 0 || Cin <= 0 || D <= 0 || H <= 0 || W <= 0) return 0;
-  size_t need = b200_conv3d_workspace_bytes(N, Cin, D, H, W, x_channels_last);
-  const SlabPlan sp = slab_plan(N, Cin, D, H, W, KD, KH, KW, params9);
+  const bool split = dtype == B200_DTYPE_F32;
+  size_t need = split ? 0 : b200_conv3d_workspace_bytes(N, Cin, D, H, W, x_channels_last);
+  const SlabPlan sp = slab_plan(N, Cin, D, H, W, KD, KH, KW, params9, split);
   if (sp.ok && sp.staging_bytes > need) need = sp.staging_bytes;
   return need;
 }
@@ -1325,13 +1346,26 @@ int b200_conv3d_fwd_gated(const void* x, const void* wp, const void* bias, void*
   const HaloGate gate{static_cast<const uint32_t*>(gate_epoch),
                       static_cast<const uint32_t*>(gate_lo),
                       static_cast<const uint32_t*>(gate_hi), static_cast<uint32_t>(gate_scale)};
-  if (dtype != B200_DTYPE_F16 && dtype != B200_DTYPE_BF16)
-    return fail_unsupported("conv3d tensor-core path: fp16/bf16 only");
+  if (!dtype_ok(dtype)) return fail_arg("bad dtype");
   if (bias && !dtype_ok(bias_dtype)) return fail_arg("bad bias dtype");
   if (N <= 0 || Cin <= 0 || D <= 0 || H <= 0 || W <= 0 || Cout <= 0 || KD <= 0 || KH <= 0 ||
       KW <= 0)
     return fail_arg("bad size");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == B200_DTYPE_F32) {
+    // fp32: the slab kernel on bf16 hi/lo splits of x and w (packed by
+    // b200_conv3d_pack_weight with dtype fp32).
+    if (gate.epoch) return fail_unsupported("conv3d fp32: no halo gate");
+    const int64_t p9[9] = {params9[0], params9[1], params9[2], params9[3], params9[4],
+                           params9[5], params9[6], params9[7], params9[8]};
+    if (p9[3] < 0 || p9[4] < 0 || p9[5] < 0 || p9[6] < 1 || p9[7] < 1 || p9[8] < 1 || p9[0] < 1 ||
+        p9[1] < 1 || p9[2] < 1)
+      return fail_arg("bad stride/padding/dilation");
+    return conv3d_slab<float>(x, wp, bias, y, bias_dtype, N, Cin, D, H, W, Cout, KD, KH, KW, p9,
+                              x_channels_last, y_channels_last, variant & 0xF,
+                              ((variant >> 22) & 1) == 0, ((variant >> 23) & 1) != 0, workspace,
+                              workspace_bytes, s);
+  }
   if (dtype == B200_DTYPE_F16)
     return conv3d_typed<__half>(x, wp, bias, y, bias_dtype, N, Cin, D, H, W, Cout, KD, KH, KW,
                                 params9, x_channels_last, y_channels_last, variant, workspace,

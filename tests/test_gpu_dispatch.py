@@ -208,3 +208,18 @@ def test_disable_restores_stock(cuda):
     assert F.conv3d is not stock[1]
     amd_tuned_torch.disable()
     assert (F.conv1d, F.conv3d, F.group_norm) == stock
+
+
+def test_fp32_conv3d_through_patch_meets_fp32_bar(cuda, patched):
+    """Patched F.conv3d on fp32 CUDA tensors: the contest's reference runs
+    without TF32, the tensor-core candidate (bf16 hi/lo splits) passes it, and
+    the result meets the fp32 bar against stock CPU fp32."""
+    from amd_tuned_torch import kernel_select
+    g = torch.Generator().manual_seed(33)
+    x = torch.randn(1, 32, 8, 16, 16, generator=g)
+    w = torch.randn(48, 32, 3, 3, 3, generator=g) * 0.05
+    b = torch.randn(48, generator=g) * 0.1
+    y = F.conv3d(x.to(cuda), w.to(cuda), b.to(cuda), padding=1)
+    ref = oracle.stock_conv3d(x.numpy(), w.numpy(), b.numpy(), (1, 1, 1))
+    assert oracle.rel_l2(_np(y), ref) <= 1e-5
+    assert "tcgen05" in kernel_select.debug_winners().values()

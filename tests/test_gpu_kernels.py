@@ -192,10 +192,7 @@ def test_conv3d_golden(cuda, case):
     m = [int(v) for v in d["meta"]]
     p, dil = m[9:12], m[12:15]
     x, w, b = _t(d["x"], dt, cuda), _t(d["w"], dt, cuda), _t(d["b"], dt, cuda)
-    y = ops.conv3d(x, w, b, (1, 1, 1), p, dil)
-    if d["dtype"] == "f32":
-        assert y is None   # tensor-core path is fp16/bf16 only: declines
-        return
+    y = ops.conv3d(x, w, b, (1, 1, 1), p, dil)   # fp32: bf16 hi/lo splits on the slab kernel
     torch.cuda.synchronize()
     assert oracle.rel_l2(_np(y), d["y"]) <= TOL[d["dtype"]]
     _no_fault()
@@ -453,4 +450,29 @@ def test_conv3d_slab_matches_box_kernel(cuda):
     a = ops.conv3d(x, w, b, (1, 1, 1), (1, 1, 1), (1, 1, 1), variant=_SLAB)
     c = ops.conv3d(x, w, b, (1, 1, 1), (1, 1, 1), (1, 1, 1), variant=_NOSLAB)
     assert oracle.rel_l2(_np(a), _np(c)) <= 1e-3
+    _no_fault()
+
+
+@pytest.mark.parametrize("N,Cin,D,H,W,Cout,k,s,p,cl", [
+    (1, 64, 16, 32, 32, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), False),
+    (2, 24, 6, 9, 11, 40, (3, 3, 3), (1, 1, 1), (1, 1, 1), True),
+    (1, 3, 8, 16, 16, 32, (3, 3, 3), (2, 2, 2), (1, 1, 1), False),
+    (1, 96, 4, 8, 8, 130, (3, 3, 3), (1, 1, 1), (1, 1, 1), False),
+    (1, 16, 5, 12, 12, 16, (1, 3, 3), (1, 2, 2), (0, 1, 1), True),
+])
+def test_conv3d_fp32_split(cuda, N, Cin, D, H, W, Cout, k, s, p, cl):
+    """fp32 conv3d on the tensor cores: bf16 hi/lo splits of x and w with fp32
+    accumulation meet the fp32 bar (rel-L2 <= 1e-5) against stock CPU fp32."""
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(Cin + Cout + sum(s))
+    x = torch.randn(N, Cin, D, H, W, generator=g) * 2
+    w = _kaiming((Cout, Cin) + k, g)
+    b = torch.randn(Cout, generator=g) * 0.1
+    ref = torch.nn.functional.conv3d(x, w, b, stride=s, padding=p)
+    xin = x.permute(0, 2, 3, 4, 1).contiguous() if cl else x
+    y = ops.conv3d(xin.to(cuda), w.to(cuda), b.to(cuda), s, p, (1, 1, 1), x_channels_last=cl,
+                   out_channels_last=cl)
+    assert y is not None and y.dtype == torch.float32
+    got = _np(y.permute(0, 4, 1, 2, 3)) if cl else _np(y)
+    assert oracle.rel_l2(got, ref.numpy()) <= 1e-5
     _no_fault()
