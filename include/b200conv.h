@@ -61,6 +61,10 @@ int b200_sm_count(void);
  * variant: 0 auto, 1 split (stats + apply, uses workspace),
  *          2 two-pass: statistics pass, then a normalise pass that re-reads
  *            x (from L2 when the tensor fits), both 16-byte vectorised,
+ *          3 streaming: statistics on a persistent grid (next chunk's loads
+ *            in flight while the current one is reduced), a per-channel
+ *            scale/shift kernel, and a persistent normalise pass over the
+ *            whole tensor (16-byte rows required),
  *          16 + k: single-read cluster kernel with k CTAs per group
  *          (k in {1, 2, 4, 8, 16}; group slice held in shared memory). */
 size_t b200_gn_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int dtype,

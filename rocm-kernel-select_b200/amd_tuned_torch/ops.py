@@ -160,7 +160,8 @@ def clear_caches() -> None:
 
 
 # ------------------------------------------------------------ GroupNorm ---
-GN_AUTO, GN_SPLIT, GN_L2 = 0, 1, 2   # auto; stats+apply; two-pass L2-resident
+# auto; stats+apply; two-pass L2-resident; three-kernel streaming (persistent grids)
+GN_AUTO, GN_SPLIT, GN_L2, GN_STREAM = 0, 1, 2, 3
 
 
 def gn_cluster_variant(k: int) -> int:

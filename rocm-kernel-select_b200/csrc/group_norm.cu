@@ -23,7 +23,9 @@
 //    the T-sharded stack (partials are (count, mean, M2) triples).
 #include <cooperative_groups.h>
 
+#include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -803,6 +805,235 @@ int launch_l2(const T* x, const void* gamma, const void* beta, T* y, int affine_
   return B200_OK;
 }
 
+// ------------------------------------------------------ streaming path ---
+// Variant 3: three kernels on a persistent grid of 256-thread CTAs.
+//  1. gn_s_stats_kernel: chunks of kSChunk elements (4 16-byte vectors per
+//     thread) walked with a grid stride; the next chunk's loads are issued
+//     before the current chunk is reduced, so every thread keeps 8 vectors in
+//     flight.  Loads mark x evict_last (the apply pass re-reads it from L2).
+//     Per chunk: sums shifted by the group's first element -> part[g][chunk].
+//  2. gn_s_coef_kernel: one warp per (n, g) merges its chunks in fp64 and
+//     writes each channel's (scale, shift) = (rstd gamma, beta - mean rstd
+//     gamma).
+//  3. gn_s_apply_kernel: y = x * scale_c + shift_c (+ SiLU) over the whole
+//     tensor as 16-byte vectors, grid stride walked from the end (the lines
+//     pass 1 read last are the likeliest still in L2), 4 vectors in flight
+//     per thread, streaming stores.
+// 2 and 3 are launched with programmatic dependent launch; 3 issues its
+// first loads of x before waiting.
+constexpr int kSThreads = 256;
+constexpr int kSVec = 4;   // 16-byte vectors per thread per chunk / iteration
+
+template <typename T>
+constexpr int64_t s_chunk() { return static_cast<int64_t>(kSThreads) * kSVec * Vec16<T>::N; }
+
+template <typename T>
+__global__ void __launch_bounds__(kSThreads)
+gn_s_stats_kernel(const T* __restrict__ x, float2* __restrict__ part, int64_t M, int chunks,
+                  int64_t total_chunks, float keep_fraction) {
+  constexpr int V = Vec16<T>::N;
+  constexpr int64_t kChunk = s_chunk<T>();
+  __shared__ float scratch[33];
+  const uint64_t pol = l2_policy_evict_last(keep_fraction);
+  uint4 cur[kSVec], nxt[kSVec];
+  auto issue = [&](int64_t c, uint4 (&r)[kSVec]) {
+    const int64_t g = c / chunks, ch = c - (c / chunks) * chunks;
+    const T* grp = x + g * M;
+#pragma unroll
+    for (int u = 0; u < kSVec; ++u) {
+      const int64_t e = ch * kChunk + (static_cast<int64_t>(u) * kSThreads + threadIdx.x) * V;
+      r[u] = e < M ? ld16_hint(grp + e, pol) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  int64_t c = blockIdx.x;
+  if (c < total_chunks) issue(c, cur);
+  for (; c < total_chunks; c += gridDim.x) {
+    const int64_t cn = c + gridDim.x;
+    if (cn < total_chunks) issue(cn, nxt);
+    const int64_t g = c / chunks, ch = c - (c / chunks) * chunks;
+    const float shift = to_f32(x[g * M]);
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int u = 0; u < kSVec; ++u) {
+      const int64_t e = ch * kChunk + (static_cast<int64_t>(u) * kSThreads + threadIdx.x) * V;
+      if (e < M) {
+        float v[V];
+        unpack16<T>(cur[u], v);
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+          const float d = v[k] - shift;
+          s1 += d;
+          s2 = fmaf(d, d, s2);
+        }
+      }
+    }
+    s1 = block_sum<kSThreads>(s1, scratch);
+    s2 = block_sum<kSThreads>(s2, scratch);
+    if (threadIdx.x == 0) part[c] = make_float2(s1, s2);
+#pragma unroll
+    for (int u = 0; u < kSVec; ++u) cur[u] = nxt[u];
+  }
+  pdl_launch_dependents();
+}
+
+// One warp per (n, g): fixed-order fp64 merge of the group's chunk sums,
+// then per channel scale = rstd * gamma, shift = beta - mean * scale.
+__global__ void __launch_bounds__(128)
+gn_s_coef_kernel(const float2* __restrict__ part, const void* __restrict__ gamma,
+                 const void* __restrict__ beta, int affine_dt, float2* __restrict__ coef,
+                 const void* __restrict__ x, int xdt, int64_t groups, int G, int Cg, int64_t M,
+                 int chunks, float eps) {
+  pdl_wait();
+  const int64_t ng = blockIdx.x * 4LL + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (ng >= groups) return;
+  double a = 0.0, b = 0.0;
+  for (int c = lane; c < chunks; c += 32) {
+    const float2 q = part[ng * chunks + c];
+    a += q.x;
+    b += q.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  const double n = static_cast<double>(M);
+  const double mean_d = a / n;
+  const double var = fmax(b / n - mean_d * mean_d, 0.0);
+  const float mean = static_cast<float>(mean_d + static_cast<double>(load_param(x, xdt, ng * M)));
+  const float rstd = 1.0f / sqrtf(static_cast<float>(var) + eps);
+  const int64_t c0 = (ng % G) * Cg;
+  for (int j = lane; j < Cg; j += 32) {
+    const float gm = gamma ? load_param(gamma, affine_dt, c0 + j) : 1.f;
+    const float bt = beta ? load_param(beta, affine_dt, c0 + j) : 0.f;
+    const float sc = rstd * gm;
+    coef[(ng / G) * G * Cg + c0 + j] = make_float2(sc, bt - mean * sc);
+  }
+  pdl_launch_dependents();
+}
+
+// Unsigned 32-bit division by a runtime constant without a divide
+// instruction: q = (umulhi(n, m) + n) >> l with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1 (Granlund and Montgomery, "Division by
+// invariant integers using multiplication", PLDI 1994).
+struct FastDiv {
+  uint32_t m, l;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+  return FastDiv{static_cast<uint32_t>(m), l};
+}
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(__umulhi(n, f.m)) + n) >> f.l);
+}
+
+template <typename T, bool SILU>
+__global__ void __launch_bounds__(kSThreads)
+gn_s_apply_kernel(const T* __restrict__ x, const float2* __restrict__ coef, T* __restrict__ y,
+                  int nvec, FastDiv per_row) {
+  constexpr int V = Vec16<T>::N;
+  const uint64_t pol = l2_policy_evict_first();
+  const int step = static_cast<int>(gridDim.x) * kSThreads * kSVec;
+  // Walk from the end of the tensor: vector index i = last - (base + u * stride).
+  const int last = nvec - 1;
+  int base = static_cast<int>(blockIdx.x) * kSThreads * kSVec + static_cast<int>(threadIdx.x);
+  uint4 r[kSVec];
+#pragma unroll
+  for (int u = 0; u < kSVec; ++u) {
+    const int i = last - (base + u * kSThreads);
+    if (i >= 0) r[u] = ld16_hint(x + static_cast<int64_t>(i) * V, pol);
+  }
+  pdl_wait();
+  for (; base <= last; base += step) {
+    uint4 q[kSVec];
+#pragma unroll
+    for (int u = 0; u < kSVec; ++u) {   // next iteration's loads first
+      const int i = last - (base + step + u * kSThreads);
+      if (i >= 0) q[u] = ld16_hint(x + static_cast<int64_t>(i) * V, pol);
+    }
+#pragma unroll
+    for (int u = 0; u < kSVec; ++u) {
+      const int i = last - (base + u * kSThreads);
+      if (i >= 0) {
+        // (n, c) row of this vector: S / V vectors per row (S % V == 0).
+        const float2 k = coef[fast_div(static_cast<uint32_t>(i), per_row)];
+        float v[V];
+        unpack16<T>(r[u], v);
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          v[e] = fmaf(v[e], k.x, k.y);
+          if (SILU) v[e] = silu(v[e]);
+        }
+        st_stream16(y + static_cast<int64_t>(i) * V, pack16<T>(v));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kSVec; ++u) r[u] = q[u];
+  }
+}
+
+size_t s_ws_bytes(const GnShape& sh, size_t esize) {
+  const int64_t chunk = static_cast<int64_t>(kSThreads) * kSVec * (16 / static_cast<int64_t>(esize));
+  const int64_t chunks = (sh.M + chunk - 1) / chunk;
+  const size_t part = static_cast<size_t>(sh.groups * chunks) * sizeof(float2);
+  return (part + 255) / 256 * 256 + static_cast<size_t>(sh.N * sh.C) * sizeof(float2);
+}
+
+template <typename T>
+int launch_stream(const T* x, const void* gamma, const void* beta, T* y, int affine_dt,
+                  const GnShape& sh, float eps, bool silu, void* ws, size_t ws_bytes,
+                  cudaStream_t stream) {
+  if (!vec_ok<T>(x, y, sh)) return fail_unsupported("streaming GroupNorm needs 16-byte rows");
+  if (sh.S / Vec16<T>::N >= (1LL << 31)) return fail_unsupported("streaming GroupNorm: rows too long");
+  constexpr int64_t kChunk = s_chunk<T>();
+  const int64_t chunks = (sh.M + kChunk - 1) / kChunk;
+  const int64_t total = sh.groups * chunks;
+  if (ws == nullptr || ws_bytes < s_ws_bytes(sh, sizeof(T)))
+    return fail_arg("GroupNorm workspace too small");
+  if (chunks > 0x7fffffffLL || sh.groups > 0x7fffffffLL) return fail_unsupported("too large");
+  float2* part = static_cast<float2*>(ws);
+  const size_t part_bytes = (static_cast<size_t>(total) * sizeof(float2) + 255) / 256 * 256;
+  float2* coef = reinterpret_cast<float2*>(static_cast<char*>(ws) + part_bytes);
+  const double bytes = static_cast<double>(sh.N) * sh.C * sh.S * sizeof(T);
+  const float keep = static_cast<float>(std::min(1.0, kL2KeepBytes / bytes));
+  const int sms = sm_count();
+  const unsigned g1 = static_cast<unsigned>(std::min<int64_t>(total, 8LL * sms));
+  gn_s_stats_kernel<T><<<g1, kSThreads, 0, stream>>>(x, part, sh.M, (int)chunks, total, keep);
+  B200_LAUNCH_CHECK("gn_s_stats_kernel");
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((sh.groups + 3) / 4));
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int xdt = sizeof(T) == 4 ? B200_DTYPE_F32 : (std::is_same<T, __half>::value ? B200_DTYPE_F16 : B200_DTYPE_BF16);
+  const float2* cpart = part;
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gn_s_coef_kernel, cpart, gamma, beta, affine_dt, coef,
+                                     static_cast<const void*>(x), xdt, sh.groups,
+                                     static_cast<int>(sh.G), static_cast<int>(sh.Cg), sh.M,
+                                     static_cast<int>(chunks), eps));
+  constexpr int V = Vec16<T>::N;
+  const int64_t nvec = sh.N * sh.C * sh.S / V;
+  if (nvec + 2LL * kSThreads * kSVec * 8 * sms >= (1LL << 31))
+    return fail_unsupported("streaming GroupNorm: more than 2^31 vectors");
+  cudaLaunchConfig_t cfg3 = cfg;
+  cfg3.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>((nvec + kSThreads * kSVec - 1) / (kSThreads * kSVec), 8LL * sms)));
+  cfg3.blockDim = dim3(kSThreads);
+  const float2* ccoef = coef;
+  auto kern = silu ? gn_s_apply_kernel<T, true> : gn_s_apply_kernel<T, false>;
+  const FastDiv per_row = make_fastdiv(static_cast<uint32_t>(sh.S / V));
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg3, kern, x, ccoef, y, static_cast<int>(nvec), per_row));
+  return B200_OK;
+}
+
 // Smallest power-of-two cluster whose per-CTA slice fits `target` bytes.
 int auto_cluster(const GnShape& sh, size_t esize) {
   const int64_t bytes = sh.M * static_cast<int64_t>(esize);
@@ -821,6 +1052,8 @@ int gn_fwd_typed(const void* xv, const void* gamma, const void* beta, void* yv, 
   T* y = static_cast<T*>(yv);
   if (variant == 0 && l2_fits(sh, sizeof(T)) && vec_ok<T>(x, y, sh)) variant = 2;
   if (variant == 2) return launch_l2<T>(x, gamma, beta, y, affine_dt, sh, eps, false, ws, ws_bytes, stream);
+  if (variant == 3)
+    return launch_stream<T>(x, gamma, beta, y, affine_dt, sh, eps, false, ws, ws_bytes, stream);
   if (variant == 0) {
     const int k = auto_cluster(sh, sizeof(T));
     if (k > 0) {
@@ -870,7 +1103,8 @@ size_t b200_gn_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int d
   const size_t stats_bytes = ((static_cast<size_t>(sh.groups * 3) * sizeof(float) + 15) / 16) * 16;
   const size_t split = stats_bytes + stats_ws_bytes(sh, dtype);
   const size_t l2 = l2_ws_bytes(sh, dtype_size(dtype));
-  return split > l2 ? split : l2;
+  const size_t st = s_ws_bytes(sh, dtype_size(dtype));
+  return std::max(split, std::max(l2, st));
 }
 
 int b200_gn_fwd(const void* x, const void* gamma, const void* beta, void* y, int dtype,

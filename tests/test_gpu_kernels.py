@@ -34,7 +34,7 @@ def _no_fault():
 
 
 # ------------------------------------------------------------ GroupNorm ---
-GN_VARIANTS = [0, 1, 2, 17, 18, 20, 24, 32]
+GN_VARIANTS = [0, 1, 2, 3, 17, 18, 20, 24, 32]
 
 
 @pytest.mark.parametrize("variant", GN_VARIANTS)
@@ -51,7 +51,7 @@ def test_group_norm_golden(cuda, case, variant):
     if y is None:   # a cluster size that cannot be scheduled declines, and the
         # two-pass path declines rows that are not whole 16-byte vectors
         rows16 = x.numel() // (x.shape[0] * x.shape[1]) % (16 // x.element_size()) == 0
-        assert variant >= 16 or (variant == ops.GN_L2 and not rows16)
+        assert variant >= 16 or (variant in (ops.GN_L2, ops.GN_STREAM) and not rows16)
         return
     torch.cuda.synchronize()
     assert oracle.rel_l2(_np(y), d["y"]) <= TOL[d["dtype"]]
@@ -74,7 +74,7 @@ def test_group_norm_merge_ranks_matches_host_merge(cuda):
     _no_fault()
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 20, 24, 32])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 20, 24, 32])
 def test_group_norm_cfg3_full_size(cuda, variant):
     """BASELINE cfg 3: x[4,512,128,128] ~N(0,2) bf16, G=32, eps=1e-6,
     gamma ~U(0.5,1.5), beta ~N(0,0.1)."""
