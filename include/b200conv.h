@@ -235,9 +235,12 @@ int b200_to_channels_last(const void* x, void* y, int dtype, int64_t N, int64_t 
  * zero-padded transform of length nfft, nfft >= L + 2*pad, nfft in
  * 2^a 3^b 5^c).  Replaces fftconv_ops.fftconv1d_candidate -> fft_conv
  * (amd_tuned_torch/fftconv_ops.py:889-942, :603-746) for groups == C.
- * b200_fftconv1d_prepare: w [C, K] -> spectrum [C, nfft] complex fp32 in the
- *   transform's digit-reversed position order (conjugated, i.e. ready to
- *   multiply).  b200_fftconv1d_fwd consumes it. */
+ * b200_fftconv1d_prepare: w [C, K] -> spectrum [C, nfft] complex fp32,
+ *   conjugated (ready to multiply), in an order private to the kernels that
+ *   depends only on nfft: for nfft = 2048, 4096, 8192 and 16384 the
+ *   register-resident transform's per-thread order, otherwise the
+ *   shared-memory transform's digit-reversed order.  b200_fftconv1d_fwd and
+ *   b200_fftconv1d_fwd_os with the same nfft consume it. */
 int b200_fft_supported_length(int64_t n);
 size_t b200_fftconv1d_spectrum_bytes(int64_t C, int64_t nfft);
 int b200_fftconv1d_prepare(const void* w, void* spectrum, int w_dtype, int64_t C, int64_t K,
@@ -247,7 +250,7 @@ int b200_fftconv1d_fwd(const void* x, const void* spectrum, const void* bias, vo
                        int64_t pad, int64_t L_out, int64_t nfft, void* stream);
 /* Overlap-save form: the row is cut into segments of nfft - K + 1 outputs,
  * each one transform of length nfft >= K over inputs [start - pad, + nfft)
- * (one CTA per channel, row pair and segment); spectrum from
+ * (one transform per channel, row pair and segment); spectrum from
  * b200_fftconv1d_prepare with the same nfft.  L_out = L + 2*pad - K + 1.
  * Same result as b200_fftconv1d_fwd (same fft_conv semantics), with short
  * transforms that several CTAs per SM can hold. */

@@ -74,6 +74,29 @@ __device__ __forceinline__ float2 root<16>(int e) {
   }
 }
 template <>
+__device__ __forceinline__ float2 root<32>(int e) {
+  e &= 31;
+  if ((e & 1) == 0) return root<16>(e >> 1);
+  switch (e) {
+    case 1: return make_float2(0.980785280f, -0.195090322f);
+    case 3: return make_float2(0.831469612f, -0.555570233f);
+    case 5: return make_float2(0.555570233f, -0.831469612f);
+    case 7: return make_float2(0.195090322f, -0.980785280f);
+    case 9: return make_float2(-0.195090322f, -0.980785280f);
+    case 11: return make_float2(-0.555570233f, -0.831469612f);
+    case 13: return make_float2(-0.831469612f, -0.555570233f);
+    case 15: return make_float2(-0.980785280f, -0.195090322f);
+    case 17: return make_float2(-0.980785280f, 0.195090322f);
+    case 19: return make_float2(-0.831469612f, 0.555570233f);
+    case 21: return make_float2(-0.555570233f, 0.831469612f);
+    case 23: return make_float2(-0.195090322f, 0.980785280f);
+    case 25: return make_float2(0.195090322f, 0.980785280f);
+    case 27: return make_float2(0.555570233f, 0.831469612f);
+    case 29: return make_float2(0.831469612f, 0.555570233f);
+    default: return make_float2(0.980785280f, 0.195090322f);
+  }
+}
+template <>
 __device__ __forceinline__ float2 root<8>(int e) { return root<16>(2 * e); }
 template <>
 __device__ __forceinline__ float2 root<4>(int e) { return root<16>(4 * e); }
@@ -109,6 +132,19 @@ template <int R, bool INV>
 __device__ __forceinline__ float2 rootd(int e) {
   const float2 w = root<R>(e);
   return INV ? make_float2(w.x, -w.y) : w;
+}
+
+// v * W_R^{+-e} for an exponent known after unrolling: multiples of a quarter
+// turn are swaps and negations, the rest a complex multiply.
+template <int R, bool INV>
+__device__ __forceinline__ float2 twiddle_const(float2 v, int e) {
+  e %= R;
+  if (e == 0) return v;
+  if (2 * e == R) return make_float2(-v.x, -v.y);
+  if (4 * e == R)  // W_R^{R/4} = -i forward, +i inverse
+    return INV ? make_float2(-v.y, v.x) : make_float2(v.y, -v.x);
+  if (4 * e == 3 * R) return INV ? make_float2(v.y, -v.x) : make_float2(-v.y, v.x);
+  return cmul(v, rootd<R, INV>(e));
 }
 
 // R-point DFT in registers: out[k] = sum_n v[n] W_R^{+-nk}.
@@ -169,7 +205,7 @@ struct DftSplit {
       Dft<R1, INV>::run(t);
 #pragma unroll
       for (int k1 = 0; k1 < R1; ++k1)
-        y[n2 * R1 + k1] = (n2 * k1 == 0) ? t[k1] : cmul(t[k1], rootd<R, INV>(n2 * k1));
+        y[n2 * R1 + k1] = twiddle_const<R, INV>(t[k1], n2 * k1);
     }
 #pragma unroll
     for (int k1 = 0; k1 < R1; ++k1) {
@@ -189,6 +225,10 @@ struct Dft<8, INV> {
 template <bool INV>
 struct Dft<16, INV> {
   static __device__ __forceinline__ void run(float2 (&v)[16]) { DftSplit<4, 4, INV>::run(v); }
+};
+template <bool INV>
+struct Dft<32, INV> {
+  static __device__ __forceinline__ void run(float2 (&v)[32]) { DftSplit<2, 16, INV>::run(v); }
 };
 template <bool INV>
 struct Dft<9, INV> {

@@ -67,6 +67,8 @@ def test_fftconv1d_shapes(cuda, B, C, L, K, pad, dt):
 @pytest.mark.parametrize("B,C,L,K,pad,nfft,dt", [
     (3, 2, 20000, 1000, 500, 4096, "f32"), (2, 3, 9000, 257, 0, 2048, "bf16"),
     (1, 2, 5000, 100, 300, 1024, "f16"), (2, 2, 40000, 2048, 1024, 8192, "f16"),
+    (2, 3, 30000, 3000, 1500, 16384, "f32"), (3, 2, 3000, 500, 250, 2048, "f32"),
+    (5, 3, 30000, 2048, 1024, 8192, "f32"), (2, 2, 9000, 700, 0, 4096, "bf16"),
 ])
 def test_fftconv1d_overlap_save(cuda, B, C, L, K, pad, nfft, dt):
     from amd_tuned_torch import ops
@@ -81,6 +83,26 @@ def test_fftconv1d_overlap_save(cuda, B, C, L, K, pad, nfft, dt):
     tol = 1e-5 if dt == "f32" else FFT_TOL
     assert oracle.rel_l2(_np(y), ref) <= tol
     assert ops.read_device_flags() == 0
+
+
+# Whole-row transforms at the register-resident lengths (2048 ... 16384)
+# and at lengths that take the shared-memory pass-per-radix plan.
+@pytest.mark.parametrize("nfft", [2048, 4096, 8192, 16384, 6144, 10240])
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_fftconv1d_whole_row_lengths(cuda, nfft, dt):
+    from amd_tuned_torch import ops
+    g = torch.Generator().manual_seed(nfft)
+    B, C, K = 3, 2, nfft // 8 + 1
+    L, pad = nfft - 2 * (K // 2) - 5, K // 2
+    x = torch.randn(B, C, L, generator=g).to(torch_dtype(dt))
+    w = _kaiming((C, 1, K), g).to(torch_dtype(dt))
+    b = torch.randn(C, generator=g).to(torch_dtype(dt))
+    y = ops.fftconv1d(x.to(cuda), w.to(cuda), b.to(cuda), pad, nfft, segmented=False)
+    assert y is not None and tuple(y.shape) == (B, C, L + 2 * pad - K + 1)
+    ref = oracle.fft_conv_np(x.float().numpy(), w.float().numpy(), b.float().numpy(), (pad,),
+                             groups=C)
+    tol = 1e-5 if dt == "f32" else FFT_TOL
+    assert oracle.rel_l2(_np(y), ref) <= tol
 
 
 def test_fftconv1d_cfg4b_full_size(cuda):
