@@ -445,8 +445,8 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
                                        "frac": byt / (ms * 1e-3) / 1e9 / hbm,
                                        "rel_l2_slice": err, "stock_gpu_us_per_op": stock,
                                        "plan": dict(zip(("nfft", "overlap_save"),
-                                                        fftconv_ops.fftconv1d_plan(16384, 2048,
-                                                                                   1024)))}
+                                                        fftconv_ops.fftconv1d_chosen_plan(
+                                                            xs[0], wd, 1024)))}
         del xs, y
         torch.cuda.empty_cache()
 

@@ -37,8 +37,10 @@ _STOCK: dict = {}
 _ENABLED = False
 
 _GROUPNORM_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
-_CONV_TC_DTYPES = (torch.float16, torch.bfloat16)
+_CONV_TC_DTYPES = (torch.float16, torch.bfloat16)   # the torch.compile custom-op route
 _FFTCONV_CONV_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+# fp16 / bf16 natively, fp32 as bf16 hi/lo splits with fp32 accumulation.
+_CONV_NATIVE_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
 _CONV3D_KIND = "conv3d"
 
 _FFTCONV_CONV3D_ENABLED = os.environ.get("AMD_TUNED_TORCH_FFTCONV3D", "1") != "0"
@@ -187,7 +189,7 @@ class _ExactFp32:
 def _conv3d_candidates(input, weight, bias, stride, padding, dilation, groups):
     orig = _STOCK["conv3d"]
     cands = []
-    if _usable(input, weight, bias, dtypes=_FFTCONV_CONV_DTYPES) and _lib.available():
+    if _usable(input, weight, bias, dtypes=_CONV_NATIVE_DTYPES) and _lib.available():
         # fp16 / bf16, and fp32 as bf16 hi/lo splits (slab kernel).
         cands.append(("tcgen05", _conv3d_tc_thunk(input, weight, bias, stride, padding, dilation)))
         if (input.dtype != torch.float32 and _triple(stride) == (1, 1, 1)
@@ -297,10 +299,11 @@ def _patched_conv3d(input, weight, bias=None, stride=1, padding=0, dilation=1, g
 
 
 # ---------------------------------------------------------------- conv2d ---
-# F.conv2d (groups = 1, stride 1, 3-D kernels of depth 1 on the same tcgen05
-# implicit GEMM) -- the reference's _patched_conv2d (_dispatch.py:1617-1700):
-# grouped and 1x1 pointwise convs go to stock, gradients through an autograd
-# wrapper with the accelerated forward, the rest is contested per shape.
+# F.conv2d (groups = 1, as 3-D kernels of depth 1 on the same tcgen05
+# implicit GEMMs: any stride the conv3d kernels take, fp16 / bf16 / fp32) --
+# the reference's _patched_conv2d (_dispatch.py:1617-1700): grouped and 1x1
+# pointwise convs go to stock, gradients through an autograd wrapper with the
+# accelerated forward, the rest is contested per shape.
 _CONV2D_KIND = "conv2d"
 
 
@@ -311,9 +314,23 @@ def _pair(v):
     return v if len(v) == 2 else (v[0],) * 2
 
 
+def _conv2d_padding(padding, weight, dilation):
+    """Explicit (ph, pw) for F.conv2d's padding argument; None for a 'same'
+    padding that would need an extra row or column on one side."""
+    if not isinstance(padding, str):
+        return _pair(padding)
+    if padding == "valid":
+        return (0, 0)
+    total = [d * (k - 1) for d, k in zip(_pair(dilation), weight.shape[2:])]
+    if any(t % 2 for t in total):
+        return None
+    return tuple(t // 2 for t in total)
+
+
 def _conv2d_tc_thunk(input, weight, bias, stride, padding, dilation):
     def run():
-        if isinstance(padding, str) or _pair(stride) != (1, 1):
+        p2 = _conv2d_padding(padding, weight, dilation)
+        if p2 is None:
             return None
         from .conv_fusion_ops import _weight5
         if input.is_contiguous():
@@ -322,8 +339,8 @@ def _conv2d_tc_thunk(input, weight, bias, stride, padding, dilation):
             x, cl = input.permute(0, 2, 3, 1).unsqueeze(1), True     # [N, 1, H, W, C]
         else:
             return None
-        p2, d2 = _pair(padding), _pair(dilation)
-        out = ops.conv3d(x, _weight5(weight), bias, (1, 1, 1), (0,) + p2, (1,) + d2,
+        d2 = _pair(dilation)
+        out = ops.conv3d(x, _weight5(weight), bias, (1,) + _pair(stride), (0,) + p2, (1,) + d2,
                          weight_key=weight,
                          x_channels_last=cl, out_channels_last=cl)
         if out is None:
@@ -336,7 +353,8 @@ def _conv2d_accelerated_forward(input, weight, bias, stride, padding, dilation, 
     orig = _STOCK["conv2d"]
     if (groups != 1 or input.dim() != 4 or weight.dim() != 4 or input.numel() == 0
             or weight.numel() == 0 or tuple(weight.shape[2:]) == (1, 1)
-            or not _usable(input, weight, bias, dtypes=_CONV_TC_DTYPES) or not _lib.available()):
+            or not _usable(input, weight, bias, dtypes=_CONV_NATIVE_DTYPES)
+            or not _lib.available()):
         if _DEBUG:
             _debug("conv2d", "stock", "grouped, pointwise, empty or outside the dtypes",
                    input=input)
@@ -350,8 +368,14 @@ def _conv2d_accelerated_forward(input, weight, bias, stride, padding, dilation, 
             out = thunk()
             if out is not None:
                 return out
-        cands = [("tcgen05", thunk),
-                 ("stock", lambda: orig(input, weight, bias, stride, padding, dilation, groups))]
+        if input.dtype == torch.float32:
+            def stock():
+                with _ExactFp32():
+                    return orig(input, weight, bias, stride, padding, dilation, groups)
+        else:
+            def stock():
+                return orig(input, weight, bias, stride, padding, dilation, groups)
+        cands = [("tcgen05", thunk), ("stock", stock)]
         out = kernel_select.pick(_CONV2D_KIND, input, weight, stride, padding, dilation, cands)
         if out is not None:
             return out
@@ -560,5 +584,5 @@ __all__ = [
     "_grad_safe", "_usable", "_is_plain_tensor", "_patched_conv3d", "_patched_group_norm",
     "_Conv3dFn", "_GroupNormFn", "_group_norm_backward", "_conv3d_accelerated_forward",
     "_group_norm_accelerated_forward", "_GROUPNORM_DTYPES", "_CONV_TC_DTYPES",
-    "_FFTCONV_CONV_DTYPES",
+    "_FFTCONV_CONV_DTYPES", "_CONV_NATIVE_DTYPES",
 ]

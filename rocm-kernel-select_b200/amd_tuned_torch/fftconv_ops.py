@@ -153,18 +153,101 @@ def fftconv1d_plan(L: int, K: int, padding: int) -> Tuple[int, bool]:
     return full, False
 
 
+# ------------------------------------------------ transform-length contest ---
+# The reference contests smoother transform lengths against the unpadded one
+# per shape (fftconv_ops.py:381-460 policies, :546-600 `_length_contest`):
+# every length computes the same convolution, only the speed differs, and
+# no static rule picks the fastest.  Here the candidates are this package's
+# transform plans -- the whole padded row at its power-of-two or 5-smooth
+# length, or overlap-save segments at a register-resident length -- with
+# the default rule's plan last ("original", the verification reference).
+# Same switches as the reference; the contest is skipped when a gradient is
+# live, below the minimum row length, or when there is nothing to try.
+_FFTCONV_SMOOTH_LEN = _env_flag("AMD_TUNED_TORCH_FFTCONV_SMOOTH_LEN", "1")
+_FFTCONV_SMOOTH_MIN_POSITIONS = int(
+    os.environ.get("AMD_TUNED_TORCH_FFTCONV_SMOOTH_MIN_POSITIONS", "4096"))
+_ORIGINAL_LEN = "original"
+_LEN_KIND = "fftconv_len"
+# Transform lengths of the register-resident kernel (libb200conv).
+_REG_FFT_LENGTHS = (2048, 4096, 8192, 16384)
+
+
+def smooth_len_enabled() -> bool:
+    return _FFTCONV_SMOOTH_LEN
+
+
+def fftconv1d_plans(L: int, K: int, padding: int):
+    """[(name, (nfft, segmented))] worth timing for this row, distinct, the
+    default rule's plan last under the name "original"."""
+    base = fftconv1d_plan(L, K, padding)
+    n = L + 2 * padding
+    alts = {}
+    p2 = 1 << (n - 1).bit_length()
+    if p2 <= _FFT1D_MAX_N:
+        alts["pow2"] = (p2, False)
+    s5 = fft_length(n)
+    if s5 <= _FFT1D_MAX_N:
+        alts["5smooth"] = (s5, False)
+    for m in _REG_FFT_LENGTHS:
+        if 2 * K <= m < n:
+            alts[f"segments{m}"] = (m, True)
+    seen = {base}
+    out = []
+    for name, plan in alts.items():
+        if plan not in seen:
+            seen.add(plan)
+            out.append((name, plan))
+    out.append((_ORIGINAL_LEN, base))
+    return out
+
+
+def _length_contest(key, plans, run, dtype, grad_live: bool, positions: int):
+    """Runs `run(plan)` with the measured fastest plan for `key` (cached),
+    or the last ("original") plan when the contest does not apply."""
+    from . import kernel_select
+    base = plans[-1][1]
+    if (not (_FFTCONV_SMOOTH_LEN and kernel_select.enabled()) or grad_live
+            or positions < _FFTCONV_SMOOTH_MIN_POSITIONS or len(plans) == 1):
+        return run(base)
+    won = kernel_select.cached_key(_LEN_KIND, key)
+    if won is not None:
+        return run(dict(plans).get(won, base))
+    cands = [(name, (lambda p=plan: run(p))) for name, plan in plans]
+    out = kernel_select.pick_key(_LEN_KIND, key, cands, tolerance=fftconv_tolerance(dtype))
+    return out if out is not None else run(base)
+
+
+def fftconv1d_chosen_plan(input: torch.Tensor, weight: torch.Tensor, padding: int):
+    """(nfft, segmented) the next fftconv1d call on this shape runs: the
+    contest's cached winner, else the default rule."""
+    from . import kernel_select
+    L, K = input.shape[-1], weight.shape[-1]
+    plans = dict(fftconv1d_plans(L, K, padding))
+    key = ("conv1d", input.dtype, tuple(input.shape), tuple(weight.shape), int(padding))
+    won = kernel_select.cached_key(_LEN_KIND, key) if _FFTCONV_SMOOTH_LEN else None
+    return plans.get(won, plans[_ORIGINAL_LEN])
+
+
 def fftconv1d(input: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
-              padding: int, cache: bool = True) -> Optional[torch.Tensor]:
+              padding: int, cache: bool = True, plan=None) -> Optional[torch.Tensor]:
     """Depthwise y[b,c,l] = bias[c] + sum_k w[c,0,k] x[b,c,l-p+k] via the FFT
-    (no autograd graph; `fftconv1d_autograd` is the differentiable form)."""
+    (no autograd graph; `fftconv1d_autograd` is the differentiable form).
+    plan: (nfft, segmented) to use; by default the transform-length contest
+    picks it per shape."""
     B, C, L = input.shape
     K = weight.shape[-1]
     Lout = L + 2 * padding - K + 1
     if Lout <= 0:
         return None
-    nfft, segmented = fftconv1d_plan(L, K, padding)
+
     # The weight object itself (not a reshaped view) keys the spectrum cache.
-    return ops.fftconv1d(input, weight, bias, padding, nfft, segmented=segmented, cache=cache)
+    def run(p):
+        return ops.fftconv1d(input, weight, bias, padding, p[0], segmented=p[1], cache=cache)
+    if plan is not None:
+        return run(plan)
+    key = ("conv1d", input.dtype, tuple(input.shape), tuple(weight.shape), int(padding))
+    return _length_contest(key, fftconv1d_plans(L, K, padding), run, input.dtype,
+                           _grad_live(input, weight, bias), L + 2 * padding)
 
 
 def fftconv1d_backward(grad_out: torch.Tensor, input: torch.Tensor, weight: torch.Tensor,
@@ -190,13 +273,15 @@ def fftconv1d_backward(grad_out: torch.Tensor, input: torch.Tensor, weight: torc
     if need_x:
         src, back = ops._crop_for_negative_padding(dy, K, padding)
         flipped = weight.reshape(C, 1, K).flip(-1).contiguous()
-        dx = fftconv1d(src, flipped, None, back, cache=False)
+        dx = fftconv1d(src, flipped, None, back, cache=False,
+                       plan=fftconv1d_plan(src.shape[-1], K, back))
         if dx is None:   # transform length unsupported: the direct kernel is exact too
             dx = ops.depthwise_conv1d(src, weight.reshape(C, K), None, back, flip_taps=True)
     if need_w:
         rows_x = input.reshape(1, B * C, L).float()
         rows_dy = dy.reshape(B * C, 1, Lout).float()
-        part = fftconv1d(rows_x, rows_dy, None, padding, cache=False)
+        part = fftconv1d(rows_x, rows_dy, None, padding, cache=False,
+                         plan=fftconv1d_plan(L, Lout, padding))
         if part is not None:
             dw = part.reshape(B, C, K).sum(dim=0).to(weight.dtype).reshape(weight.shape)
         else:
@@ -273,5 +358,12 @@ def fft_conv3d(signal: torch.Tensor, kernel: torch.Tensor, bias: Optional[torch.
     Dp, Hp, Wp = D + 2 * pad[0], H + 2 * pad[1], W + 2 * pad[2]
     if KD > Dp or KH > Hp or KW > Wp:
         return None
-    fd, fh, fw = _next_smooth_len(Dp), _next_smooth_len(Hp), fft_length(Wp)
-    return ops.fftconv3d(signal, kernel, bias, pad, (fd, fh, fw))
+    base = (_next_smooth_len(Dp), _next_smooth_len(Hp), fft_length(Wp))
+    plans = []
+    p2 = (_next_smooth_len(Dp, (2,)), _next_smooth_len(Hp, (2,)), _next_smooth_len(Wp, (2,)))
+    if p2 != base:
+        plans.append(("pow2", p2))
+    plans.append((_ORIGINAL_LEN, base))
+    key = ("conv3d", signal.dtype, tuple(signal.shape), tuple(kernel.shape), pad)
+    return _length_contest(key, plans, lambda fs: ops.fftconv3d(signal, kernel, bias, pad, fs),
+                           signal.dtype, _grad_live(signal, kernel, bias), Dp * Hp * Wp)

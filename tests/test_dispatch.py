@@ -94,8 +94,12 @@ def test_conv2d_routes_as_depth1_conv3d(patched, force_eligible):
     assert force_eligible == [("conv3d", False), ("conv3d", True)]
     F.conv2d(x, torch.randn(8, 4, 3, 3), padding=1, groups=2)   # grouped -> stock
     F.conv2d(x, torch.randn(4, 8, 1, 1))                          # pointwise -> stock
-    F.conv2d(x, w, padding=1, stride=2)                           # stride 2 -> kernel declines
     assert force_eligible == [("conv3d", False), ("conv3d", True)]
+    F.conv2d(x, w, padding=1, stride=2)                           # strided -> the conv3d route
+    F.conv2d(x, w, padding="same")
+    F.conv2d(x, torch.randn(4, 8, 2, 2), padding="same")          # uneven 'same' -> stock
+    assert force_eligible == [("conv3d", False), ("conv3d", True), ("conv3d", False),
+                              ("conv3d", False)]
 
 
 def test_conv1d_fallback_toggle_is_independent():

@@ -143,6 +143,40 @@ def test_conv2d_through_patch(cuda, patched, monkeypatch, N, C, H, W, Co, k, p, 
     assert oracle.rel_l2(_np(y), ref.numpy()) <= (3.9e-3 if contest else 2e-3)
 
 
+@pytest.mark.parametrize("stride,padding,dt,cl", [
+    (2, 1, torch.float16, False), ((2, 1), (1, 2), torch.bfloat16, True),
+    (3, 0, torch.float16, False), (1, "same", torch.bfloat16, False),
+    (1, "valid", torch.float16, True), (1, 1, torch.float32, False),
+    (2, 1, torch.float32, True),
+])
+@pytest.mark.parametrize("contest", [False, True])
+def test_conv2d_strided_fp32_and_string_padding(cuda, patched, monkeypatch, stride, padding, dt,
+                                                cl, contest):
+    """Strided convs (VAE-encoder downsampling), fp32 (the bf16 hi/lo split
+    kernel) and string paddings through the patched F.conv2d; the fp32 bar
+    is 1e-5 against stock CPU fp32 (the contest's stock reference runs
+    without TF32)."""
+    from amd_tuned_torch import kernel_select
+    monkeypatch.setattr(kernel_select, "_ENABLED", contest)
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 48, 30, 26, generator=g).to(dt)
+    w = ((torch.rand(64, 48, 3, 3, generator=g) * 2 - 1) / math.sqrt(48 * 9)).to(dt)
+    b = (torch.randn(64, generator=g) * 0.1).to(dt)
+    xd = x.to(cuda)
+    if cl:
+        xd = xd.contiguous(memory_format=torch.channels_last)
+    y = F.conv2d(xd, w.to(cuda), b.to(cuda), stride=stride, padding=padding)
+    ref = torch.nn.functional.conv2d(x.double(), w.double(), b.double(), stride=stride,
+                                     padding=padding)
+    assert tuple(y.shape) == tuple(ref.shape)
+    tol = 1e-5 if dt == torch.float32 else (3.9e-3 if contest else 2e-3)
+    assert oracle.rel_l2(_np(y), ref.numpy()) <= tol
+    from amd_tuned_torch import _dispatch
+    native = _dispatch._conv2d_tc_thunk(xd, w.to(cuda), b.to(cuda), stride, padding, 1)()
+    assert native is not None                       # the tensor-core route takes it
+    assert oracle.rel_l2(_np(native), ref.numpy()) <= (1e-5 if dt == torch.float32 else 2e-3)
+
+
 def test_conv2d_repeated_calls_reuse_the_packed_weight(cuda, patched, monkeypatch):
     """Same weight, several calls: every call runs the tcgen05 route (the
     packed-weight cache is keyed on the 4-D weight, not on its per-call

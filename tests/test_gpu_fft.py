@@ -105,6 +105,34 @@ def test_fftconv1d_whole_row_lengths(cuda, nfft, dt):
     assert oracle.rel_l2(_np(y), ref) <= tol
 
 
+def test_fftconv1d_length_contest(cuda, monkeypatch):
+    """The transform-length contest times every plan once, caches the
+    winner, and the winner's output meets the FFT bar; a second call runs
+    the cached plan."""
+    from amd_tuned_torch import fftconv_ops, kernel_select
+    monkeypatch.setattr(kernel_select, "_ENABLED", True)
+    kernel_select.reset()
+    g = torch.Generator().manual_seed(12)
+    B, C, L, K, pad = 4, 8, 12000, 700, 350
+    x = torch.randn(B, C, L, generator=g).half()
+    w = _kaiming((C, 1, K), g).half()
+    b = torch.randn(C, generator=g).half()
+    xd, wd, bd = x.to(cuda), w.to(cuda), b.to(cuda)
+    ref = oracle.fft_conv_np(x.float().numpy(), w.float().numpy(), b.float().numpy(), (pad,),
+                             groups=C)
+    y = fftconv_ops.fftconv1d(xd, wd, bd, pad)
+    assert oracle.rel_l2(_np(y), ref) <= FFT_TOL
+    plans = dict(fftconv_ops.fftconv1d_plans(L, K, pad))
+    assert len(plans) > 1
+    won = [v for k, v in kernel_select.debug_winners().items()
+           if "fftconv_len" in str(k)]
+    assert len(won) == 1 and won[0] in plans
+    assert fftconv_ops.fftconv1d_chosen_plan(xd, wd, pad) == plans[won[0]]
+    y2 = fftconv_ops.fftconv1d(xd, wd, bd, pad)
+    assert oracle.rel_l2(_np(y2), ref) <= FFT_TOL
+    kernel_select.reset()
+
+
 def test_fftconv1d_cfg4b_full_size(cuda):
     """BASELINE cfg 4b: x[16,1024,16384] fp16 ~N(0,1), w[1024,1,2048] kaiming-U,
     bias, groups 1024, padding 1024 -> L_out 16385.  Checked on a slice of

@@ -66,3 +66,45 @@ def test_fftconv1d_plan_choice():
     assert fftconv_ops.fftconv1d_plan(60000, 257, 128)[1] is True           # too long for one
     nfft, seg = fftconv_ops.fftconv1d_plan(1000, 257, 128)
     assert not seg and nfft >= 1000 + 2 * 128
+
+
+def test_fftconv1d_length_contest_plans():
+    """The transform plans contested per shape: distinct, valid for the row
+    (whole-row lengths cover the padded signal, segments are >= 2K), the
+    default rule's plan last as the verification reference."""
+    from amd_tuned_torch import fftconv_ops
+    plans = fftconv_ops.fftconv1d_plans(16384, 2048, 1024)                 # cfg 4b
+    names = [n for n, _ in plans]
+    assert names[-1] == "original" and plans[-1][1] == (8192, True)
+    assert len({p for _, p in plans}) == len(plans)
+    assert dict(plans)["5smooth"] == (18432, False)
+    assert ("segments16384", (16384, True)) in plans and "pow2" not in names  # 32768 too long
+    for L, K, pad in [(16384, 2048, 1024), (4000, 64, 0), (1000, 257, 128), (60000, 257, 128),
+                      (5000, 999, 499)]:
+        for name, (nfft, seg) in fftconv_ops.fftconv1d_plans(L, K, pad):
+            if seg:
+                assert nfft >= K
+            else:
+                assert nfft >= L + 2 * pad and nfft <= 24576
+    # nothing else to try: a row whose only plan is the default one
+    assert [n for n, _ in fftconv_ops.fftconv1d_plans(100, 3, 1)][-1] == "original"
+
+
+def test_fftconv_length_contest_skips(monkeypatch):
+    """The contest hands straight to the default plan when off, when a
+    gradient is live, below the minimum length, or with one plan."""
+    from amd_tuned_torch import fftconv_ops, kernel_select
+    ran = []
+    plans = [("pow2", (2,)), ("original", (1,))]
+    key = ("conv1d", "probe")
+
+    def run(p):
+        ran.append(p)
+        return p
+    monkeypatch.setattr(kernel_select, "_ENABLED", True)
+    assert fftconv_ops._length_contest(key, plans, run, None, True, 10 ** 6) == (1,)
+    assert fftconv_ops._length_contest(key, plans, run, None, False, 10) == (1,)
+    assert fftconv_ops._length_contest(key, plans[-1:], run, None, False, 10 ** 6) == (1,)
+    monkeypatch.setattr(kernel_select, "_ENABLED", False)
+    assert fftconv_ops._length_contest(key, plans, run, None, False, 10 ** 6) == (1,)
+    assert ran == [(1,)] * 4
