@@ -213,7 +213,8 @@ def _length_contest(key, plans, run, dtype, grad_live: bool, positions: int):
     if won is not None:
         return run(dict(plans).get(won, base))
     cands = [(name, (lambda p=plan: run(p))) for name, plan in plans]
-    out = kernel_select.pick_key(_LEN_KIND, key, cands, tolerance=fftconv_tolerance(dtype))
+    out = kernel_select.pick_key(_LEN_KIND, key, cands, tolerance=fftconv_tolerance(dtype),
+                                 reference_competes=True)
     return out if out is not None else run(base)
 
 

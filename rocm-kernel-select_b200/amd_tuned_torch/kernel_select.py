@@ -332,10 +332,15 @@ def pick(kind: str, input, weight, stride, padding, dilation,
                     tolerance=tolerance)
 
 
-def pick_key(kind: str, key, candidates: "list[tuple[str, Callable]]", tolerance=None):
+def pick_key(kind: str, key, candidates: "list[tuple[str, Callable]]", tolerance=None,
+             reference_competes: Optional[bool] = None):
+    """Contest under an explicit key.  reference_competes: time the last
+    candidate too (default: the stock-competes setting; a contest whose
+    reference is one of this package's own plans passes True)."""
     if not _ENABLED:
         return None
-    return _contest((kind,) + tuple(key), candidates, tolerance=tolerance)
+    return _contest((kind,) + tuple(key), candidates, tolerance=tolerance,
+                    reference_competes=reference_competes)
 
 
 def _record(key, name) -> None:
@@ -353,9 +358,11 @@ def _run_guarded(thunk):
         return None, True
 
 
-def _contest(key, candidates, tolerance=None):
+def _contest(key, candidates, tolerance=None, reference_competes: Optional[bool] = None):
     if not candidates:
         return None
+    if reference_competes is None:
+        reference_competes = _REFERENCE_COMPETES
     ref_name, ref_thunk = candidates[-1]
     winner, bad = _book.state(key)
 
@@ -373,7 +380,7 @@ def _contest(key, candidates, tolerance=None):
     for name, thunk in candidates:
         if name in bad:
             continue
-        if name == ref_name and not _REFERENCE_COMPETES:
+        if name == ref_name and not reference_competes:
             continue
         ms = _measure(thunk)
         if ms is not None:

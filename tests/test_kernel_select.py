@@ -119,6 +119,18 @@ def test_reference_not_timed_by_default(monkeypatch, timings):
     assert kernel_select.cached("conv3d", x, w, s, p, d) == "stock"
 
 
+def test_pick_key_reference_competes_when_asked(monkeypatch, timings):
+    """A contest whose reference is one of this package's own plans (the
+    FFT transform-length contest) times the reference too, whatever the
+    stock-competes setting."""
+    monkeypatch.setattr(kernel_select, "_REFERENCE_COMPETES", False)
+    calls = timings({"segments4096": 5.0, "original": 3.0})
+    out = kernel_select.pick_key("fftconv_len", ("conv1d", 1), cands(["segments4096", "original"]),
+                                 reference_competes=True)
+    assert out == "out:original" and calls["original"] == 1
+    assert kernel_select.cached_key("fftconv_len", ("conv1d", 1)) == "original"
+
+
 # ------------------------------------------------------------ verification
 def test_wrong_fast_candidate_is_blacklisted(monkeypatch, timings):
     monkeypatch.setattr(kernel_select, "_VERIFY_ENABLED", True)
