@@ -1245,10 +1245,25 @@ __device__ __forceinline__ void inter_item(int t, const InterPlan& p, bool* appl
   *g = G - L + (r - 2 * (G - L));
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// Statistics word of a group before its last chunk publishes it (both
+// halves 0xffffffff, a NaN pattern no arithmetic produces).
+constexpr uint64_t kStatUnset = ~0ull;
+
+__device__ __forceinline__ uint64_t ld_acquire_gpu_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void st_release_gpu_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
 }
 
 template <typename T>
@@ -1256,7 +1271,7 @@ __global__ void __launch_bounds__(kIThreads)
 gn_inter_kernel(const T* __restrict__ x, const void* __restrict__ gamma,
                 const void* __restrict__ beta, T* __restrict__ y, int affine_dt, int M,
                 FastDiv div_s, int G, int Cg, float eps, InterPlan p, float2* part,
-                uint32_t* done, uint32_t* ticket, float keep, int* gflags) {
+                uint32_t* done, uint64_t* stat, uint32_t* ticket, float keep, int* gflags) {
   constexpr int V = Vec16<T>::N;
   constexpr int CH = kIThreads * kIVec * V;  // elements per item
   __shared__ float2 red[kIThreads / 32];
@@ -1309,39 +1324,37 @@ gn_inter_kernel(const T* __restrict__ x, const void* __restrict__ gamma,
           tot.y += red[w].y;
         }
         part[static_cast<int64_t>(g) * p.cpg + c] = tot;
-        __threadfence();
-        atomicAdd(done + g, 1u);
+        // The group's last chunk merges all of them (fp64, chunk order) and
+        // publishes (mean, rstd) as one 8-byte word: one acquire load is all
+        // a normalise item needs.
+        if (atom_add_acq_rel_gpu(done + g, 1u) == static_cast<uint32_t>(p.cpg - 1)) {
+          double a = 0.0, b = 0.0;
+          for (int j = 0; j < p.cpg; ++j) {
+            const float2 q = __ldcg(part + static_cast<int64_t>(g) * p.cpg + j);
+            a += q.x;
+            b += q.y;
+          }
+          const double n = static_cast<double>(M);
+          const double md = a / n;
+          const double var = fmax(b / n - md * md, 0.0);
+          const float mean = static_cast<float>(md + static_cast<double>(shift));
+          const float rstd = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
+          st_release_gpu_u64(stat + g, (static_cast<uint64_t>(__float_as_uint(rstd)) << 32) |
+                                           __float_as_uint(mean));
+        }
       }
     } else {
       if (tid == 0) {
         const uint64_t t0 = globaltimer_ns();
-        while (ld_acquire_gpu(done + g) < static_cast<uint32_t>(p.cpg)) {
+        uint64_t w;
+        while ((w = ld_acquire_gpu_u64(stat + g)) == kStatUnset) {
           if (globaltimer_ns() - t0 > kWaitLimitNs) {
             if (gflags) atomicExch(gflags, kFaultGnInter);
             break;
           }
         }
-      }
-      __syncthreads();
-      if (tid < 32) {
-        double a = 0.0, b = 0.0;
-        for (int j = tid; j < p.cpg; j += 32) {
-          const float2 q = __ldcg(part + static_cast<int64_t>(g) * p.cpg + j);
-          a += q.x;
-          b += q.y;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          a += __shfl_xor_sync(0xffffffffu, a, o);
-          b += __shfl_xor_sync(0xffffffffu, b, o);
-        }
-        if (tid == 0) {
-          const double n = static_cast<double>(M);
-          const double md = a / n;
-          const double var = fmax(b / n - md * md, 0.0);
-          s_stat = make_float2(static_cast<float>(md + static_cast<double>(to_f32(gx[0]))),
-                               static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps))));
-        }
+        s_stat = make_float2(__uint_as_float(static_cast<uint32_t>(w)),
+                             __uint_as_float(static_cast<uint32_t>(w >> 32)));
       }
       __syncthreads();
       const float mean = s_stat.x, rstd = s_stat.y;
@@ -1370,8 +1383,8 @@ gn_inter_kernel(const T* __restrict__ x, const void* __restrict__ gamma,
 size_t inter_ws_bytes(const GnShape& sh, size_t esize) {
   const int64_t ch = static_cast<int64_t>(kIThreads) * kIVec * (16 / static_cast<int64_t>(esize));
   const int64_t cpg = (sh.M + ch - 1) / ch;
-  return 256 + static_cast<size_t>(sh.groups) * sizeof(uint32_t) +
-         static_cast<size_t>(sh.groups * cpg) * sizeof(float2) + 256;
+  return 256 + 2 * ((static_cast<size_t>(sh.groups) * sizeof(uint64_t) + 255) / 256 * 256) +
+         static_cast<size_t>(sh.groups * cpg) * sizeof(float2);
 }
 
 template <typename T>
@@ -1384,14 +1397,19 @@ int launch_inter(const T* x, const void* gamma, const void* beta, T* y, int affi
   if (2 * sh.groups * cpg >= (1LL << 31)) return fail_unsupported("too many items");
   if (ws == nullptr || ws_bytes < inter_ws_bytes(sh, sizeof(T)))
     return fail_arg("GroupNorm workspace too small");
-  // Layout: [ticket (256 B)][done: groups x u32, padded][part: groups x cpg float2]
-  uint32_t* ticket = static_cast<uint32_t*>(ws);
-  uint32_t* done = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + 256);
-  const size_t done_bytes = (static_cast<size_t>(sh.groups) * sizeof(uint32_t) + 255) / 256 * 256;
-  float2* part = reinterpret_cast<float2*>(static_cast<char*>(ws) + 256 + done_bytes);
-  B200_CUDA_CHECK(cudaMemsetAsync(ws, 0, 256 + done_bytes, stream));
+  // Layout: [ticket (256 B)][done: groups x u32][stat: groups x u64][part: groups x cpg
+  // float2], the first two zeroed and stat set to kStatUnset before every launch.
+  const size_t arr = (static_cast<size_t>(sh.groups) * sizeof(uint64_t) + 255) / 256 * 256;
+  char* base = static_cast<char*>(ws);
+  uint32_t* ticket = reinterpret_cast<uint32_t*>(base);
+  uint32_t* done = reinterpret_cast<uint32_t*>(base + 256);
+  uint64_t* stat = reinterpret_cast<uint64_t*>(base + 256 + arr);
+  float2* part = reinterpret_cast<float2*>(base + 256 + 2 * arr);
+  B200_CUDA_CHECK(cudaMemsetAsync(base, 0, 256 + arr, stream));
+  B200_CUDA_CHECK(cudaMemsetAsync(stat, 0xff, arr, stream));
   const int sms = sm_count();
-  const int grid = static_cast<int>(std::min<int64_t>(2 * sh.groups * cpg, 3LL * sms));
+  // Four 256-thread CTAs per SM (the register limit at 64 per thread).
+  const int grid = static_cast<int>(std::min<int64_t>(2 * sh.groups * cpg, 4LL * sms));
   InterPlan plan;
   plan.groups = static_cast<int>(sh.groups);
   plan.cpg = static_cast<int>(cpg);
@@ -1401,7 +1419,7 @@ int launch_inter(const T* x, const void* gamma, const void* beta, T* y, int affi
   gn_inter_kernel<T><<<grid, kIThreads, 0, stream>>>(
       x, gamma, beta, y, affine_dt, static_cast<int>(sh.M),
       make_fastdiv(static_cast<uint32_t>(sh.S)), static_cast<int>(sh.G),
-      static_cast<int>(sh.Cg), eps, plan, part, done, ticket, keep, device_flags_ptr());
+      static_cast<int>(sh.Cg), eps, plan, part, done, stat, ticket, keep, device_flags_ptr());
   B200_LAUNCH_CHECK("gn_inter_kernel");
   return B200_OK;
 }
