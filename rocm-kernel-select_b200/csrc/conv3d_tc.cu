@@ -41,7 +41,6 @@ namespace b200 {
 namespace {
 
 constexpr int kConvThreads = 192;       // 6 warps
-constexpr int kConvThreadsFused = 320;  // + 4 transposer warps
 constexpr int kBM = 128;
 constexpr int kBK = 64;            // weight packing granule: Cin is padded to a multiple of 64
 constexpr int kMaxStages = 8;
@@ -64,11 +63,6 @@ struct ConvParams {
   int y_cl;
   int out_tma;
   int* flags;
-  // FUSE kernels: one raw box per (kd, channel chunk).  fuse_mode 1: NCDHW
-  // input, box {raw_w, rows, 1, 64, 1} starting at column ow0 - wpad8 (a
-  // multiple of 8).  fuse_mode 2: channels-last input, box {KB, raw_w, rows,
-  // 1, 1} starting at column ow0 - pw (raw_w = BW + (KW - 1) * dw).
-  int fuse_mode, raw_w, raw_bytes, raw_tx, wpad8, lbw;
   // Halo gate (T-sharded stack): output frame 0 reads input frame 0 and
   // frame Do - 1 reads frame Do + 1, which other GPUs write.  Before loading
   // a tile of such a frame the producer waits until *gate_lo / *gate_hi
@@ -147,18 +141,6 @@ __device__ bool halo_gate_wait(const ConvParams& p, int od) {
 // K-major rows, SWIZZLE_128B) or 32 (64-byte rows, SWIZZLE_64B, half the
 // stage size so that MT = 4 still leaves three stages).
 //
-// FUSE: the producer loads ONE raw box of the input per (kd, channel chunk)
-// and warps 6-9 write the swizzled K-major A tile of each kw shift from it
-// into the pipeline stage (generic stores, then a proxy fence before the
-// stage is handed to the MMA warp), so one read of the input from L2 serves
-// all KW shifts.  fuse_mode 1 (NCDHW input, MT = 1, KB = 64): the box is
-// {W span rounded to 8, rows, 1, 64 channels, 1} -- its innermost coordinate
-// rounded down to a multiple of 8 elements -- and the warps transpose it
-// with ldmatrix.trans / stmatrix.  fuse_mode 2 (channels-last input, any MT
-// and KB): the box is {KB channels, BW + (KW - 1) * dw columns, rows, 1, 1}
-// in the same swizzle as A, and the warps copy 16-byte chunks from raw row
-// r * raw_w + w + kw * dw to A row r * BW + w, re-swizzled.
-//
 // PAIR: a cluster of two CTAs on two SMs computes 2 x MT M tiles with MMAs
 // of M = 256 (tcgen05 cta_group::2): each CTA loads its own A rows and HALF
 // of the weight box (BN / 2 output channels), so the pair streams the
@@ -166,12 +148,11 @@ __device__ bool halo_gate_wait(const ConvParams& p, int od) {
 // both producers' copies count on the leader's stage barriers; the leader's
 // MMA completions are committed to both CTAs' barriers; each CTA's epilogue
 // drains its own TMEM and tells the leader (one arrival per warp).
-template <typename T, int BN, int MT, int KB, bool FUSE, bool PAIR = false>
-__global__ void __launch_bounds__(FUSE ? kConvThreadsFused : kConvThreads, 1)
+template <typename T, int BN, int MT, int KB, bool PAIR = false>
+__global__ void __launch_bounds__(kConvThreads, 1)
 conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                  const __grid_constant__ CUtensorMap tmy, const ConvParams p) {
   static_assert(KB == 64 || KB == 32, "k-block of 32 or 64 channels");
-  static_assert(!(FUSE && PAIR), "pairs use the unfused producer");
   constexpr int kRow = KB * 2;               // bytes per K-major operand row
   constexpr int kBNl = PAIR ? BN / 2 : BN;   // weight rows (output channels) this CTA loads
   constexpr int kBTap = kBNl * kRow;         // this CTA's share of one tap's weight box
@@ -194,17 +175,14 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sRaw = smem + STAGES * p.stage_bytes;                   // FUSE: 2 raw boxes
-  uint8_t* sOut = sRaw + (FUSE ? 2 * p.raw_bytes : 0);             // [BN][128] staging
+  uint8_t* sOut = smem + STAGES * p.stage_bytes;                   // [BN][128] staging
   float* sBias = reinterpret_cast<float*>(sOut + (p.out_tma ? kBM * BN * 2 : 0));  // [BN]
   uint64_t* full = reinterpret_cast<uint64_t*>(sBias + BN + 4);   // + 16-byte scratch
   uint64_t* empty = full + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;  // [2]
   uint64_t* tempty = tfull + 2;      // [2]
   uint64_t* drain = tempty + 2;      // [1]
-  uint64_t* rfull = drain + 1;       // [2] FUSE: raw box landed
-  uint64_t* rempty = rfull + 2;      // [2] FUSE: raw box consumed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -214,14 +192,8 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
     prefetch_tmap(&tmw);
     if (p.out_tma) prefetch_tmap(&tmy);
     for (int s = 0; s < kMaxStages; ++s) {
-      // FUSE: a stage is full once its weight boxes landed AND the
-      // transposer warps handed over its A tile.
-      mbar_init(&full[s], FUSE ? 2 : 1);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-    }
-    for (int r = 0; r < 2; ++r) {
-      mbar_init(&rfull[r], 1);
-      mbar_init(&rempty[r], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
@@ -249,72 +221,7 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
   // kernel; no global memory is touched before it has completed.
   pdl_wait();
 
-  if (warp == 0 && FUSE) {
-    // --------------------------------------- TMA producer, fused NCDHW input
-    // Unit u = (kd, channel chunk): one raw box, then KW k-blocks (one per kw
-    // shift) whose weight boxes go into the stages the transposer fills.
-    int stage = 0;
-    uint32_t phase = 0;
-    int ru = 0;
-    bool ok = true;
-    const int units = p.kblocks / p.KW;
-    for (int t = tile0; t < p.num_tiles && ok; t += tstep) {
-      const TileCoord tc = decode_tile(t, p, BN);
-      const int rot = p.rotate ? static_cast<int>((tc.lin * 7u) % units) : 0;
-      for (int uu = 0; uu < units && ok; ++uu, ++ru) {
-        int u = uu + rot;
-        if (u >= units) u -= units;
-        const int cc = u % p.cchunks, kd = u / p.cchunks;
-        const int r = ru & 1;
-        const uint32_t rph = static_cast<uint32_t>(ru >> 1) & 1u;
-        bool got = mbar_wait_bounded(&rempty[r], rph ^ 1u, abort, p.flags, 1);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
-          mbar_expect_tx(&rfull[r], static_cast<uint32_t>(p.raw_tx));
-          if (p.fuse_mode == 1)
-            tma_load_5d(sRaw + r * p.raw_bytes, &tmx, &rfull[r], tc.ow0 - p.wpad8, tc.oh0 - p.ph,
-                        tc.od - p.pd + kd * p.dd, cc * KB, tc.n);
-          else
-            tma_load_5d(sRaw + r * p.raw_bytes, &tmx, &rfull[r], cc * KB, tc.ow0 - p.pw,
-                        tc.oh0 - p.ph, tc.od - p.pd + kd * p.dd, tc.n);
-        }
-        __syncwarp();
-        for (int kw = 0; kw < p.KW; ++kw) {
-          got = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, p.flags, 1);
-          if (!__all_sync(0xffffffffu, got)) {
-            ok = false;
-            break;
-          }
-          if (lane == 0) {
-            uint8_t* st = smem + stage * p.stage_bytes;
-            mbar_expect_tx(&full[stage], static_cast<uint32_t>(p.khg * kBTap));
-            for (int j = 0; j < p.khg; ++j) {
-              const int tap = (kd * p.KH + j) * p.KW + kw;
-              tma_load_3d(st + p.a_bytes + j * kBTap, &tmw, &full[stage], cc * KB, tc.n0, tap);
-            }
-          }
-          __syncwarp();
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-    }
-    if (!ok && lane == 0) {
-      // Let the copies already issued land before shared memory goes away.
-      const int last = (stage + STAGES - 1) % STAGES;
-      mbar_wait_bounded(&full[last], (stage == 0 ? phase ^ 1u : phase), nullptr, nullptr, 0);
-      if (ru > 0) {
-        const int lr = (ru - 1) & 1;
-        mbar_wait_bounded(&rfull[lr], static_cast<uint32_t>((ru - 1) >> 1) & 1u, nullptr, nullptr, 0);
-      }
-    }
-    __syncwarp();
-  } else if (warp == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     // The whole warp walks the loop (waits included) so it stays converged;
     // one lane issues the copies.
@@ -491,104 +398,6 @@ conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant_
       __syncwarp();
       mbar_wait_bounded(drain, 0, nullptr, nullptr, 0);
       __syncwarp();
-    }
-  } else if (FUSE && warp >= 6) {
-    // ------------------------------------------------ transposer (FUSE only)
-    // Raw box [64 channels][rows][raw_w] (16-bit) -> A tile of each kw shift:
-    // position q = row * BW + w is a 128-byte K-major row whose channel group
-    // cg (8 channels, 16 bytes) sits at chunk cg ^ (q & 7) (SWIZZLE_128B).
-    // Work item = (row, block of 8 raw columns, 32 channels): ldmatrix.trans
-    // turns four [8 channels x 8 columns] blocks into per-column channel rows
-    // and stmatrix writes each column's row to the A row of the output
-    // position that column feeds for this kw (rows outside the tile go to a
-    // scratch slot).  The unaligned kw shift only moves store addresses.
-    const int tt = threadIdx.x - 192;
-    const int twarp = tt >> 5;
-    const int rows = MT * p.BH + (p.khg - 1) * p.dh;
-    const int plane = rows * p.raw_w;   // elements between two channels of the raw box (mode 1)
-    const int BWm = p.BW;
-    const uint32_t dummy = smem_u32(sBias + BN);   // 16 scratch bytes past the bias (see fixed_smem)
-    const int m = lane >> 3, i = lane & 7;      // this lane's matrix and row
-    int stage = 0;
-    uint32_t phase = 0;
-    int ru = 0;
-    bool ok = true;
-    const int units = p.kblocks / p.KW;
-    for (int t = tile0; t < p.num_tiles && ok; t += tstep) {
-      for (int uu = 0; uu < units && ok; ++uu, ++ru) {
-        const int r = ru & 1;
-        const uint32_t rph = static_cast<uint32_t>(ru >> 1) & 1u;
-        bool got = mbar_wait_bounded(&rfull[r], rph, abort, p.flags, 1);
-        if (!tp_bar_and(got)) {
-          ok = false;
-          break;
-        }
-        const uint32_t raw = smem_u32(sRaw + r * p.raw_bytes);
-        for (int kw = 0; kw < p.KW; ++kw) {
-          got = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort, p.flags, 1);
-          if (!tp_bar_and(got)) {
-            ok = false;
-            break;
-          }
-          const uint32_t A = smem_u32(smem + stage * p.stage_bytes);
-          if (p.fuse_mode == 2) {
-            // Shift copy: A row q = r * BW + w <- raw row r * raw_w + w + kw * dw,
-            // chunk c of a kRow-byte row stored at c ^ swz(row) in both.
-            constexpr int kCh = KB / 8;                 // 16-byte chunks per row
-            const int total = (rows << p.lbw) * kCh;
-            for (int idx = tt; idx < total; idx += 128) {
-              const int q = idx / kCh, c = idx % kCh;
-              const int rr = q >> p.lbw, w = q & (BWm - 1);
-              const int src = rr * p.raw_w + w + kw * p.dw;
-              const int sw_s = KB == 64 ? (src & 7) : ((src >> 1) & 3);
-              const int sw_d = KB == 64 ? (q & 7) : ((q >> 1) & 3);
-              uint4 v;
-              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                           : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                           : "r"(raw + static_cast<uint32_t>(src * kRow + ((c ^ sw_s) << 4))));
-              asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(
-                               A + static_cast<uint32_t>(q * kRow + ((c ^ sw_d) << 4))),
-                           "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                           : "memory");
-            }
-            fence_proxy_async();
-            tp_bar();
-            if (tt == 0) mbar_arrive(&full[stage]);
-            if (++stage == STAGES) {
-              stage = 0;
-              phase ^= 1u;
-            }
-            continue;
-          }
-          const int xs = p.wpad8 - p.pw + kw * p.dw;   // raw column feeding output w = 0
-          const int j0 = xs >> 3, j1 = (xs + BWm - 1) >> 3;
-          const int nblk = j1 - j0 + 1;
-          const int items = rows * nblk * 2;           // (row, column block, 32-channel half)
-          for (int it = twarp; it < items; it += 4) {
-            const int half = it & 1;
-            const int rb = it >> 1;
-            const int rr = rb / nblk, j = j0 + rb % nblk;
-            const int c = half * 32 + m * 8 + i;       // channel of this lane's source row
-            uint32_t v[4];
-            ldsm_x4_trans(raw + static_cast<uint32_t>(((c * rows + rr) * p.raw_w + 8 * j) * 2), v);
-            const int w = 8 * j + i - xs;              // output position fed by raw column 8j + i
-            const int q = rr * BWm + w;
-            const int cg = half * 4 + m;
-            const uint32_t dst = (w >= 0 && w < BWm)
-                                     ? A + static_cast<uint32_t>(q * 128 + ((cg ^ (q & 7)) << 4))
-                                     : dummy;
-            stsm_x4(dst, v);
-          }
-          fence_proxy_async();   // generic stores -> visible to the tensor-core reads
-          tp_bar();
-          if (tt == 0) mbar_arrive(&full[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (ok && tt == 0) mbar_arrive(&rempty[r]);   // every read of this raw box is done
-      }
     }
   } else {
     // ---------------------------------------------------------- epilogue
@@ -813,14 +622,13 @@ constexpr size_t fixed_smem(int BN, bool staging) {
 }
 constexpr size_t kSmemBudget = 232448;  // sm_100 opt-in maximum per CTA
 
-template <typename T, int BN, int MT, int KB, bool FUSE = false, bool PAIR = false>
+template <typename T, int BN, int MT, int KB, bool PAIR = false>
 int launch_conv(const CUtensorMap& tmx, const CUtensorMap& tmw, const CUtensorMap& tmy,
                 const ConvParams& prm, bool staging, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(prm.stages) * prm.stage_bytes + fixed_smem(BN, staging) +
-                      (FUSE ? 2 * static_cast<size_t>(prm.raw_bytes) : 0);
+  const size_t smem = static_cast<size_t>(prm.stages) * prm.stage_bytes + fixed_smem(BN, staging);
   if (smem > kSmemBudget) return fail_unsupported("conv3d stage geometry exceeds shared memory");
   if (prm.out_tma && !staging) return fail_arg("conv3d TMA output without staging");
-  auto kern = conv3d_tc_kernel<T, BN, MT, KB, FUSE, PAIR>;
+  auto kern = conv3d_tc_kernel<T, BN, MT, KB, PAIR>;
   B200_CUDA_CHECK(
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   // Pairs: clusters of two CTAs, one tile per cluster per turn.
@@ -828,7 +636,7 @@ int launch_conv(const CUtensorMap& tmx, const CUtensorMap& tmw, const CUtensorMa
                         : std::min(prm.num_tiles, sm_count());
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(FUSE ? kConvThreadsFused : kConvThreads);
+  cfg.blockDim = dim3(kConvThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -911,6 +719,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
 
   if (!aligned16(wp)) return fail_unsupported("operands not 16-byte aligned");
 
+  if (((variant >> 14) & 3) != 0) return fail_arg("conv3d variant bits 14-15 are not defined");
   const int BN = pick_bn(Cout, variant & 0xF);
   int BW;
   const int bw_code = (variant >> 4) & 0xF;
@@ -929,8 +738,7 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   // Variant bit 16: CTA pairs (cta_group::2 MMAs of M = 256; each CTA of the
   // pair loads half of the weight box).  A pair tile is 2 x MT M tiles.
   const bool pair = ((variant >> 16) & 1) != 0;
-  if (pair && (BN > 128 || ((variant >> 14) & 3) != 0))
-    return fail_unsupported("conv3d CTA pairs: Cout tiles <= 128, unfused producer");
+  if (pair && BN > 128) return fail_unsupported("conv3d CTA pairs: Cout tiles <= 128");
   const int BNl = pair ? BN / 2 : BN;   // weight rows one CTA loads
   const int prow = pair ? 2 : 1;
   auto tiles_for = [&](int mt) {
@@ -1012,77 +820,10 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   }
   if (!planned) return fail_unsupported("conv3d tile does not fit in shared memory");
 
-  // NCDHW input: by default transpose into the workspace first (a separate
-  // bandwidth-bound kernel).  Variant bit 14 instead fuses the transposition
-  // into the conv kernel (one M tile, kh-grouped, two raw boxes in shared
-  // memory) when TMA can address x (16-byte aligned, rows of W elements a
-  // multiple of 16 bytes).  Measured on the cfg2 shape the fused kernel is
-  // slower (21 us vs 13 us for transpose + conv): the raw boxes leave room
-  // for only two pipeline stages.  It stays selectable for other shapes.
-  bool fuse = false;
-  int raw_w = 0, raw_tx = 0, raw_bytes = 0, wpad8 = 0;
-  if (!x_cl && ((variant >> 14) & 1) == 1 && aligned16(x) && (W % 8) == 0 && g.mt == 1 &&
-      kgmode != 1) {
-    wpad8 = static_cast<int>((pw + 7) / 8 * 8);
-    const int64_t rw = ((wpad8 - pw) + BW + (KW - 1) * dw + 7) / 8 * 8;
-    const int64_t rows = BH + (KH - 1) * dh;
-    if (rw <= 256 && rows <= 256) {
-      raw_w = static_cast<int>(rw);
-      raw_tx = static_cast<int>(kBK * rows * rw * 2);
-      raw_bytes = (raw_tx + 1023) / 1024 * 1024;
-      Geo f;
-      f.mt = 1;
-      f.kb = kBK;
-      f.khg = static_cast<int>(KH);
-      f.a_bytes = static_cast<int>(rows * BW * kBK * 2);
-      f.stage_bytes = f.a_bytes + f.khg * BN * kBK * 2;
-      for (int pass = 0; pass < 2 && !fuse; ++pass) {
-        f.staging = tma_out_ok && pass == 0;
-        if (pass == 0 && !tma_out_ok) continue;
-        const size_t fixed = fixed_smem(BN, f.staging) + 2 * static_cast<size_t>(raw_bytes);
-        if (fixed >= kSmemBudget) continue;
-        f.stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemBudget - fixed) / f.stage_bytes));
-        if (f.stages >= 2) fuse = true;
-      }
-      if (fuse) g = f;
-    }
-  }
-  int fuse_mode = fuse ? 1 : 0;
-  // Channels-last input, variant bit 15 (opt-in): one raw box {KB, BW +
-  // (KW-1) dw, rows, 1, 1} per (kd, chunk) serves all KW shifts (the copier
-  // warps build each shift's A tile in shared memory), instead of one A box
-  // per (kd, kw): the input crosses L2 -> SM once instead of KW times.
-  // Measured slower on cfg2 (13.9 vs 11.0 us) and on the cfg5 conv (1406 vs
-  // 778 us): the raw boxes cost pipeline stages and the copy adds a hand-off
-  // per k-block, which matter more here than the saved L2 traffic.
-  if (x_cl && ((variant >> 15) & 1) == 1 && g.khg == KH && KW > 1) {
-    const int64_t rw = BW + (KW - 1) * dw;
-    const int64_t rows = static_cast<int64_t>(g.mt) * BH + (KH - 1) * dh;
-    if (rw <= 256 && rows <= 256) {
-      const int tx = static_cast<int>(g.kb * 2 * rw * rows);
-      const int rb = (tx + 1023) / 1024 * 1024;
-      Geo f = g;
-      bool ok = false;
-      for (int pass = 0; pass < 2 && !ok; ++pass) {
-        f.staging = tma_out_ok && pass == 0;
-        if (pass == 0 && !tma_out_ok) continue;
-        const size_t fixed = fixed_smem(BN, f.staging) + 2 * static_cast<size_t>(rb);
-        if (fixed >= kSmemBudget) continue;
-        f.stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemBudget - fixed) / f.stage_bytes));
-        if (f.stages >= (pass == 0 ? 3 : 2)) ok = true;
-      }
-      if (ok) {
-        g = f;
-        fuse = true;
-        fuse_mode = 2;
-        raw_w = static_cast<int>(rw);
-        raw_tx = tx;
-        raw_bytes = rb;
-      }
-    }
-  }
+  // NCDHW input: transposed into the workspace first (a separate
+  // bandwidth-bound kernel that triggers this kernel's dependent launch).
   const void* xcl = x;
-  if (!x_cl && !fuse) {
+  if (!x_cl) {
     const size_t need = static_cast<size_t>(N * D * H * W * Cin) * sizeof(T);
     if (ws == nullptr || ws_bytes < need) return fail_arg("conv3d workspace too small");
     const int64_t S = D * H * W;
@@ -1106,25 +847,12 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   const CUtensorMapSwizzle swz = KB == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUtensorMapDataType dt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  if (fuse_mode == 1) {
-    // NCDHW: dims (W, H, D, C, N); one raw box {raw_w, rows, 1, 64, 1}, no swizzle.
-    cuuint64_t dims[5] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)Cin, (cuuint64_t)N};
-    cuuint64_t strides[4] = {(cuuint64_t)(W * 2), (cuuint64_t)(H * W * 2),
-                             (cuuint64_t)(D * H * W * 2), (cuuint64_t)(Cin * D * H * W * 2)};
-    cuuint32_t box[5] = {(cuuint32_t)raw_w, (cuuint32_t)a_rows_h, 1, (cuuint32_t)kBK, 1};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    CUresult r = encode(&tmx, dt, 5, const_cast<void*>(xcl), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail_unsupported("NCDHW input tensor map rejected");
-  } else {
+  {
     cuuint64_t dims[5] = {(cuuint64_t)Cin, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)D, (cuuint64_t)N};
     cuuint64_t strides[4] = {(cuuint64_t)(Cin * 2), (cuuint64_t)(W * Cin * 2),
                              (cuuint64_t)(H * W * Cin * 2), (cuuint64_t)(D * H * W * Cin * 2)};
-    // Channels-last: one A box {KB, BW, rows, 1, 1} per (kd, kw), or in fuse
-    // mode 2 one raw box {KB, BW + (KW - 1) dw, rows, 1, 1} per kd.
-    cuuint32_t box[5] = {(cuuint32_t)KB, (cuuint32_t)(fuse_mode == 2 ? raw_w : BW),
-                         (cuuint32_t)a_rows_h, 1, 1};
+    // Channels-last: one A box {KB, BW, rows, 1, 1} per (kd, kw).
+    cuuint32_t box[5] = {(cuuint32_t)KB, (cuuint32_t)BW, (cuuint32_t)a_rows_h, 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = encode(&tmx, dt, 5, const_cast<void*>(xcl), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
@@ -1179,22 +907,15 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
   prm.bias_dt = bias_dt;
   prm.y_cl = y_cl;
   prm.flags = device_flags_ptr();
-  prm.fuse_mode = fuse_mode;
-  prm.raw_w = raw_w;
-  prm.raw_bytes = raw_bytes;
-  prm.raw_tx = raw_tx;
-  prm.wpad8 = wpad8;
-  prm.lbw = 0;
-  while ((1 << prm.lbw) < BW) ++prm.lbw;
   prm.Nb = (int)N;
   prm.gate_epoch = nullptr;
   prm.gate_lo = prm.gate_hi = nullptr;
   prm.gate_scale = 0;
   if (gate && gate->epoch) {
     // The gate assumes one halo frame each side read only by the edge
-    // output frames: KD = 3, no T padding, no T dilation, unfused producer.
-    if (KD != 3 || pd != 0 || dd != 1 || fuse_mode != 0)
-      return fail_unsupported("halo gate: needs KD = 3, T padding 0, T dilation 1, unfused");
+    // output frames: KD = 3, no T padding, no T dilation.
+    if (KD != 3 || pd != 0 || dd != 1)
+      return fail_unsupported("halo gate: needs KD = 3, T padding 0, T dilation 1");
     prm.gate_epoch = gate->epoch;
     prm.gate_lo = gate->lo;
     prm.gate_hi = gate->hi;
@@ -1220,27 +941,14 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     prm.out_tma = (r == CUDA_SUCCESS) ? 1 : 0;
   }
   const bool stg = g.staging;
-  if (fuse) {
+  if (pair) {
     if (MT == 1) {
       if (BN == 64) return launch_conv<T, 64, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
-      if (BN == 128) return launch_conv<T, 128, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
-      return launch_conv<T, 256, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
+      return launch_conv<T, 128, 1, 64, true>(tmx, tmw, tmy, prm, stg, stream);
     }
     if (MT == 2) {
       if (BN == 64) return launch_conv<T, 64, 2, 32, true>(tmx, tmw, tmy, prm, stg, stream);
       return launch_conv<T, 128, 2, 32, true>(tmx, tmw, tmy, prm, stg, stream);
-    }
-    if (BN == 64) return launch_conv<T, 64, 4, 32, true>(tmx, tmw, tmy, prm, stg, stream);
-    return launch_conv<T, 128, 4, 32, true>(tmx, tmw, tmy, prm, stg, stream);
-  }
-  if (pair) {
-    if (MT == 1) {
-      if (BN == 64) return launch_conv<T, 64, 1, 64, false, true>(tmx, tmw, tmy, prm, stg, stream);
-      return launch_conv<T, 128, 1, 64, false, true>(tmx, tmw, tmy, prm, stg, stream);
-    }
-    if (MT == 2) {
-      if (BN == 64) return launch_conv<T, 64, 2, 32, false, true>(tmx, tmw, tmy, prm, stg, stream);
-      return launch_conv<T, 128, 2, 32, false, true>(tmx, tmw, tmy, prm, stg, stream);
     }
     return fail_unsupported("conv3d CTA pairs: MT <= 2");
   }

@@ -144,35 +144,6 @@ __device__ __forceinline__ void bulk_wait_all0() {
 }
 // Named barrier 1 over the 128 epilogue threads (warps 2-5).
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-// Four 8 x 8 16-bit matrices: ldmatrix .trans from shared memory (lane l
-// gives the row address of matrix l / 8, row l % 8), and stmatrix of the same
-// fragments (lane l gives the destination row address the same way).
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr)
-               : "memory");
-}
-__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
-  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr),
-               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3])
-               : "memory");
-}
-// Named barrier 2 over 128 threads (the conv kernel's transposer warps), and
-// its AND-vote form.
-__device__ __forceinline__ void tp_bar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
-__device__ __forceinline__ bool tp_bar_and(bool pred) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 2, 128, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(out)
-      : "r"(static_cast<uint32_t>(pred))
-      : "memory");
-  return out != 0;
-}
 // Same barrier as epi_bar, returning the AND of `pred` over the 128 threads
 // (a uniform decision for all of them).
 __device__ __forceinline__ bool epi_bar_and(bool pred) {

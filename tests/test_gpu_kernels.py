@@ -361,69 +361,6 @@ def test_conv3d_cta_pairs(cuda, dt, N, Cin, D, H, W, Cout, k, p, dil, variant, c
     _no_fault()
 
 
-# NCDHW input with the channels-last transposition fused into the kernel
-# (variant bit 14; the default is a separate transposition): same results on
-# shapes with W % 8 == 0, padding / dilation along W, a partial channel chunk,
-# a partial last W tile and KW = 1.
-_FUSE = 1 << 14
-
-
-@pytest.mark.parametrize("dt,N,Cin,D,H,W,Cout,k,p,dil", [
-    ("f16", 1, 64, 6, 12, 32, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1)),
-    ("bf16", 2, 40, 3, 7, 24, 48, (3, 3, 3), (1, 1, 1), (1, 1, 1)),
-    ("f16", 1, 64, 4, 9, 40, 80, (3, 3, 3), (0, 2, 3), (1, 2, 2)),
-    ("bf16", 1, 128, 3, 5, 16, 128, (3, 3, 1), (1, 1, 0), (1, 1, 1)),
-    ("f16", 1, 32, 3, 4, 136, 64, (1, 3, 5), (0, 1, 2), (1, 1, 1)),
-    ("bf16", 1, 64, 3, 6, 8, 256, (2, 2, 2), (1, 0, 1), (1, 1, 1)),
-])
-def test_conv3d_fused_ncdhw(cuda, dt, N, Cin, D, H, W, Cout, k, p, dil):
-    from amd_tuned_torch import ops
-    g = torch.Generator().manual_seed(Cin + W + Cout)
-    x = torch.randn(N, Cin, D, H, W, generator=g).to(torch_dtype(dt))
-    w = _kaiming((Cout, Cin) + k, g).to(torch_dtype(dt))
-    b = torch.randn(Cout, generator=g).to(torch_dtype(dt)) * 0.1
-    ref = torch.nn.functional.conv3d(x.float(), w.float(), b.float(), padding=p, dilation=dil)
-    xd, wd, bd = x.to(cuda), w.to(cuda), b.to(cuda)
-    y = ops.conv3d(xd, wd, bd, (1, 1, 1), p, dil, variant=_FUSE)
-    y_split = ops.conv3d(xd, wd, bd, (1, 1, 1), p, dil)
-    assert y is not None and y_split is not None
-    assert tuple(y.shape) == tuple(ref.shape)
-    assert oracle.rel_l2(_np(y), ref.numpy()) <= TOL[dt]
-    assert oracle.rel_l2(_np(y), _np(y_split)) <= 1e-3   # same sums, another k-block order
-    _no_fault()
-
-
-# Channels-last input with one raw box per (kd, chunk) shared by the KW shifts
-# (variant bit 15): same results as one A box per (kd, kw), for one M tile
-# (64-channel k-blocks) and two / four M tiles (32-channel k-blocks),
-# dilation, padding, partial channel chunks and partial W tiles.
-_CL_RAW = 1 << 15
-
-
-@pytest.mark.parametrize("dt,N,Cin,D,H,W,Cout,k,p,dil,mt", [
-    ("f16", 1, 64, 5, 12, 32, 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), 0),
-    ("bf16", 1, 128, 4, 12, 128, 128, (3, 3, 3), (1, 1, 1), (1, 1, 1), _MT2),
-    ("f16", 2, 40, 3, 7, 24, 48, (3, 3, 3), (1, 1, 1), (1, 1, 1), _MT4),
-    ("bf16", 1, 64, 5, 10, 40, 64, (3, 3, 3), (2, 2, 2), (2, 2, 2), _MT2),
-    ("f16", 1, 32, 3, 6, 16, 64, (1, 3, 5), (0, 1, 2), (1, 1, 1), 0),
-])
-def test_conv3d_cl_raw_box(cuda, dt, N, Cin, D, H, W, Cout, k, p, dil, mt):
-    from amd_tuned_torch import ops
-    g = torch.Generator().manual_seed(Cin + 3 * W + Cout)
-    x = torch.randn(N, Cin, D, H, W, generator=g).to(torch_dtype(dt))
-    w = _kaiming((Cout, Cin) + k, g).to(torch_dtype(dt))
-    b = torch.randn(Cout, generator=g).to(torch_dtype(dt)) * 0.1
-    ref = torch.nn.functional.conv3d(x.float(), w.float(), b.float(), padding=p, dilation=dil)
-    xcl = x.permute(0, 2, 3, 4, 1).contiguous().to(cuda)
-    wd, bd = w.to(cuda), b.to(cuda)
-    y = ops.conv3d(xcl, wd, bd, (1, 1, 1), p, dil, variant=mt | _CL_RAW, x_channels_last=True)
-    y0 = ops.conv3d(xcl, wd, bd, (1, 1, 1), p, dil, variant=mt, x_channels_last=True)
-    assert y is not None and y0 is not None
-    assert oracle.rel_l2(_np(y), ref.numpy()) <= TOL[dt]
-    assert oracle.rel_l2(_np(y), _np(y0)) <= 1e-3
-    _no_fault()
-
-
 def test_conv3d_channels_last_io(cuda):
     from amd_tuned_torch import ops
     g = torch.Generator().manual_seed(9)
