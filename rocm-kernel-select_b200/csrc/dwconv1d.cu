@@ -136,6 +136,9 @@ dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
   // the neighbouring vector outside the warp -- are requested before any is
   // used, so a warp waits for one memory round trip, not two.
   float cur[kDwSubTiles][V], edge[kDwSubTiles][V];
+  // Launched with programmatic stream serialisation: the CTA is scheduled
+  // while the previous kernel drains, and reads nothing before it is done.
+  pdl_wait();
 #pragma unroll
   for (int u = 0; u < kDwSubTiles; ++u) load_vec(base + u * kSub, cur[u]);
   if (lane == 0 || lane == 31) {
@@ -143,6 +146,7 @@ dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
 #pragma unroll
     for (int u = 0; u < kDwSubTiles; ++u) load_vec(base + u * kSub + off, edge[u]);
   }
+  pdl_launch_dependents();  // the next kernel may start its own set-up now
   float wk[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) wk[k] = load_param(w, wdt, c * K + (flip ? K - 1 - k : k));
@@ -182,6 +186,23 @@ dwconv1d_reg_kernel(const T* __restrict__ x, const void* __restrict__ w,
   }
 }
 
+// Launch with programmatic stream serialisation (the kernel calls pdl_wait
+// before its first global read).
+template <typename... P, typename... A>
+int launch_pdl(void (*kern)(P...), unsigned grid, cudaStream_t stream, A... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kDwThreads);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, static_cast<P>(args)...));
+  return B200_OK;
+}
+
 template <typename T>
 int launch(const void* xv, const void* w, const void* bias, void* yv, int wdt, int64_t B,
            int64_t C, int64_t L, int64_t K, int64_t pad, int64_t Lout, bool flip,
@@ -199,7 +220,8 @@ int launch(const void* xv, const void* w, const void* bias, void* yv, int wdt, i
       T* y = static_cast<T*>(yv);
       const unsigned grid = static_cast<unsigned>(blocks);
       const int mode = pad == (K - 1) / 2 ? 0 : (pad == 0 ? 1 : 2);
-#define B200_DWR(KK, PP) dwconv1d_reg_kernel<T, KK, PP><<<grid, kDwThreads, 0, stream>>>( \
+      int rc = B200_OK;
+#define B200_DWR(KK, PP) rc = launch_pdl(dwconv1d_reg_kernel<T, KK, PP>, grid, stream, \
     x, w, bias, y, wdt, C, L, Lout, tiles, flip)
 #define B200_DWK(KK)                                                     \
   case KK:                                                               \
@@ -215,8 +237,7 @@ int launch(const void* xv, const void* w, const void* bias, void* yv, int wdt, i
       }
 #undef B200_DWK
 #undef B200_DWR
-      B200_LAUNCH_CHECK("dwconv1d_reg_kernel");
-      return B200_OK;
+      return rc;
     }
   }
   const T* x = static_cast<const T*>(xv);
