@@ -222,6 +222,21 @@ int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, in
                     int64_t Cout, int64_t KD, int64_t KH, int64_t KW, const int64_t* params9,
                     int x_channels_last, int y_channels_last, int variant, void* workspace,
                     size_t workspace_bytes, void* stream);
+/* The same call with the per-problem arguments packed once: hosts that call
+ * one conv shape repeatedly (the patched F.conv3d after its contest) build a
+ * B200Conv3dProblem per shape and pass only the per-call pointers, which
+ * keeps the per-call binding cost of a foreign-function interface (ctypes:
+ * ~8 us for the 22-argument form) to a few arguments.  Fields mean what the
+ * b200_conv3d_fwd arguments of the same names mean; workspace_bytes is the
+ * size of `workspace`.  Replaces the same reference call as b200_conv3d_fwd. */
+typedef struct B200Conv3dProblem {
+  int64_t N, Cin, D, H, W, Cout, KD, KH, KW;
+  int64_t params9[9];
+  int32_t dtype, bias_dtype, x_channels_last, y_channels_last, variant, reserved;
+  uint64_t workspace_bytes;
+} B200Conv3dProblem;
+int b200_conv3d_fwd_call(const B200Conv3dProblem* problem, const void* x, const void* wp,
+                         const void* bias, void* y, void* workspace, void* stream);
 /* b200_conv3d_fwd with a halo gate for the T-sharded stack (no reference
  * counterpart): x is a haloed operand whose first and last frames other GPUs
  * write (b200_peer_halo_push).  Tiles of output frame 0 / Do - 1 are

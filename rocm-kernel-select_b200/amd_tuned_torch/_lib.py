@@ -27,6 +27,16 @@ c_int, c_int64, c_float, c_size_t, c_vp = (ctypes.c_int, ctypes.c_int64, ctypes.
 c_i64p = ctypes.POINTER(ctypes.c_int64)
 c_intp = ctypes.POINTER(ctypes.c_int)
 
+class Conv3dProblem(ctypes.Structure):
+    """Mirror of B200Conv3dProblem (include/b200conv.h)."""
+    _fields_ = ([(n, ctypes.c_int64) for n in ("N", "Cin", "D", "H", "W", "Cout", "KD", "KH",
+                                                 "KW")]
+                + [("params9", ctypes.c_int64 * 9)]
+                + [(n, ctypes.c_int32) for n in ("dtype", "bias_dtype", "x_channels_last",
+                                                 "y_channels_last", "variant", "reserved")]
+                + [("workspace_bytes", ctypes.c_uint64)])
+
+
 # name -> (restype, argtypes).  Mirrors include/b200conv.h one to one; the CPU
 # test suite checks that every function declared there is exported and listed.
 SIGNATURES = {
@@ -62,6 +72,7 @@ SIGNATURES = {
     "b200_conv3d_packed_weight_bytes_for": (c_size_t, [c_int64] * 5 + [c_int]),
     "b200_conv3d_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 9
                         + [c_i64p, c_int, c_int, c_int, c_vp, c_size_t, c_vp]),
+    "b200_conv3d_fwd_call": (c_int, [c_vp] * 7),
     "b200_conv3d_fwd_gated": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int] + [c_int64] * 9
                               + [c_i64p, c_int, c_int, c_int, c_vp, c_size_t, c_vp, c_vp, c_vp,
                                  c_int64, c_vp]),

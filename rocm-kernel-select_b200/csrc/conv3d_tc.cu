@@ -543,6 +543,9 @@ __global__ void __launch_bounds__(256)
 to_cl16_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t C, int64_t S) {
   static_assert(sizeof(T) == 2, "16-bit elements");
   __shared__ uint32_t tile[64 * 33];
+  // Launched with programmatic serialisation behind the previous kernel
+  // (which may still read the workspace this copy writes): wait for it first.
+  pdl_wait();
   pdl_launch_dependents();  // the conv kernel's prologue may overlap this copy
   const int64_t n = blockIdx.z;
   const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 64;
@@ -596,6 +599,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 to_cl_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t C, int64_t S) {
   __shared__ T tile[64][66];
+  pdl_wait();  // as to_cl16_kernel
   pdl_launch_dependents();
   const int64_t n = blockIdx.z;
   const int64_t c0 = static_cast<int64_t>(blockIdx.y) * 64;
@@ -832,10 +836,23 @@ int conv3d_typed(const void* x, const void* wp, const void* bias, void* y, int b
     if ((S + 63) / 64 > 0x7fffffffLL || (Cin + 63) / 64 > 65535)
       return fail_unsupported("transpose grid too large");
     if (aligned16(x) && aligned16(ws))
-      to_cl16_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
-    else
-      to_cl_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(x), static_cast<T*>(ws), Cin, S);
-    B200_LAUNCH_CHECK("to_cl_kernel");
+    {
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      at[0].val.programmaticStreamSerializationAllowed = 1;
+      cudaLaunchConfig_t lc = {};
+      lc.gridDim = grid;
+      lc.blockDim = dim3(256);
+      lc.stream = stream;
+      lc.attrs = at;
+      lc.numAttrs = 1;
+      const T* xs = static_cast<const T*>(x);
+      T* wsd = static_cast<T*>(ws);
+      if (aligned16(x) && aligned16(ws))
+        B200_CUDA_CHECK(cudaLaunchKernelEx(&lc, to_cl16_kernel<T>, xs, wsd, Cin, S));
+      else
+        B200_CUDA_CHECK(cudaLaunchKernelEx(&lc, to_cl_kernel<T>, xs, wsd, Cin, S));
+    }
     xcl = ws;
   }
   if (!aligned16(xcl)) return fail_unsupported("operands not 16-byte aligned");
@@ -1040,6 +1057,16 @@ int b200_conv3d_fwd(const void* x, const void* wp, const void* bias, void* y, in
   return b200_conv3d_fwd_gated(x, wp, bias, y, dtype, bias_dtype, N, Cin, D, H, W, Cout, KD, KH,
                                KW, params9, x_channels_last, y_channels_last, variant, workspace,
                                workspace_bytes, nullptr, nullptr, nullptr, 0, stream);
+}
+
+int b200_conv3d_fwd_call(const B200Conv3dProblem* pr, const void* x, const void* wp,
+                         const void* bias, void* y, void* workspace, void* stream) {
+  if (!pr) return fail_arg("NULL problem");
+  return b200_conv3d_fwd_gated(x, wp, bias, y, pr->dtype, pr->bias_dtype, pr->N, pr->Cin, pr->D,
+                               pr->H, pr->W, pr->Cout, pr->KD, pr->KH, pr->KW, pr->params9,
+                               pr->x_channels_last, pr->y_channels_last, pr->variant, workspace,
+                               static_cast<size_t>(pr->workspace_bytes), nullptr, nullptr,
+                               nullptr, 0, stream);
 }
 
 int b200_conv3d_fwd_gated(const void* x, const void* wp, const void* bias, void* y, int dtype,

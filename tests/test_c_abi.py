@@ -3,6 +3,7 @@ function include/b200conv.h declares, with a ctypes signature for each.
 No kernel is launched here (CPU only)."""
 from __future__ import annotations
 
+import ctypes
 import re
 from pathlib import Path
 
@@ -61,3 +62,12 @@ def test_argument_errors_are_reported_without_a_gpu():
     with pytest.raises(_lib.NativeError):
         _lib.check(-1, "b200_dwconv1d_fwd")
     assert _lib.check(1, "declined") is False
+
+
+def test_conv3d_problem_struct_layout():
+    """The ctypes mirror of B200Conv3dProblem has the C layout: 18 int64,
+    6 int32, one uint64 -- 176 bytes, workspace_bytes at offset 168."""
+    from amd_tuned_torch import _lib
+    P = _lib.Conv3dProblem
+    assert ctypes.sizeof(P) == 176
+    assert P.params9.offset == 72 and P.dtype.offset == 144 and P.workspace_bytes.offset == 168
