@@ -1126,6 +1126,9 @@ constexpr int kSVec = 4;   // 16-byte vectors per thread per chunk / iteration
 
 template <typename T>
 constexpr int64_t s_chunk() { return static_cast<int64_t>(kSThreads) * kSVec * Vec16<T>::N; }
+inline int64_t s_chunk_elems(size_t esize) {
+  return static_cast<int64_t>(kSThreads) * kSVec * (16 / static_cast<int64_t>(esize));
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kSThreads)
@@ -1482,6 +1485,75 @@ int launch_inter(const T* x, const void* gamma, const void* beta, T* y, int affi
   return B200_OK;
 }
 
+// (count, mean, M2) per group from the streaming statistics pass's shifted
+// chunk sums (one warp per group, fixed-order fp64 merge): the
+// b200_gn_partial_stats output for 16-byte rows.
+__global__ void __launch_bounds__(128)
+gn_s_triples_kernel(const float2* __restrict__ part, const void* __restrict__ x, int xdt,
+                    float* __restrict__ out, int64_t groups, int64_t M, int chunks) {
+  pdl_wait();
+  const int64_t ng = blockIdx.x * 4LL + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (ng >= groups) return;
+  double a = 0.0, b = 0.0;
+  for (int c = lane; c < chunks; c += 32) {
+    const float2 q = part[ng * chunks + c];
+    a += q.x;
+    b += q.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if (lane == 0) {
+    const double n = static_cast<double>(M);
+    const double md = a / n;
+    out[ng * 3 + 0] = static_cast<float>(n);
+    out[ng * 3 + 1] = static_cast<float>(md + static_cast<double>(load_param(x, xdt, ng * M)));
+    out[ng * 3 + 2] = static_cast<float>(fmax(b - a * md, 0.0));
+  }
+}
+
+// b200_gn_partial_stats for 16-byte rows: the persistent streaming
+// statistics kernel (two chunks of loads in flight per thread), then the
+// triples.  Declines (> 0) for other shapes.
+template <typename T>
+int launch_stats_stream(const T* x, float* stats_out, const GnShape& sh, void* ws,
+                        size_t ws_bytes, cudaStream_t stream) {
+  if (!vec_ok<T>(x, nullptr, sh)) return fail_unsupported("streaming statistics need 16-byte rows");
+  constexpr int64_t kChunk = s_chunk<T>();
+  const int64_t chunks = (sh.M + kChunk - 1) / kChunk;
+  const int64_t total = sh.groups * chunks;
+  if (chunks > 0x7fffffffLL || total > 0x7fffffffLL) return fail_unsupported("too many chunks");
+  if (ws == nullptr || ws_bytes < static_cast<size_t>(total) * sizeof(float2))
+    return fail_unsupported("workspace too small for the streaming statistics");
+  float2* part = static_cast<float2*>(ws);
+  const double bytes = static_cast<double>(sh.N) * sh.C * sh.S * sizeof(T);
+  const float keep = static_cast<float>(std::min(1.0, kL2KeepBytes / bytes));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t c1 = {};
+  c1.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(total, 8LL * sm_count())));
+  c1.blockDim = dim3(kSThreads);
+  c1.stream = stream;
+  c1.attrs = attr;
+  c1.numAttrs = 1;
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&c1, gn_s_stats_kernel<T>, x, part, sh.M,
+                                     static_cast<int>(chunks), total, keep));
+  cudaLaunchConfig_t c2 = c1;
+  c2.gridDim = dim3(static_cast<unsigned>((sh.groups + 3) / 4));
+  c2.blockDim = dim3(128);
+  const int xdt = sizeof(T) == 4 ? B200_DTYPE_F32
+                                 : (std::is_same<T, __half>::value ? B200_DTYPE_F16 : B200_DTYPE_BF16);
+  const float2* cpart = part;
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&c2, gn_s_triples_kernel, cpart,
+                                     static_cast<const void*>(x), xdt, stats_out, sh.groups,
+                                     sh.M, static_cast<int>(chunks)));
+  return B200_OK;
+}
+
 size_t s_ws_bytes(const GnShape& sh, size_t esize) {
   const int64_t chunk = static_cast<int64_t>(kSThreads) * kSVec * (16 / static_cast<int64_t>(esize));
   const int64_t chunks = (sh.M + chunk - 1) / chunk;
@@ -1651,7 +1723,10 @@ int b200_gn_fwd(const void* x, const void* gamma, const void* beta, void* y, int
 size_t b200_gn_stats_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int dtype) {
   GnShape sh;
   if (check_shape(N, C, S, G, &sh) != B200_OK) return 0;
-  return stats_ws_bytes(sh, dtype);
+  const int64_t ck = s_chunk_elems(dtype_size(dtype));
+  const size_t stream_bytes =
+      static_cast<size_t>(sh.groups * ((sh.M + ck - 1) / ck)) * sizeof(float2);
+  return std::max(stats_ws_bytes(sh, dtype), stream_bytes);
 }
 
 int b200_gn_partial_stats(const void* x, float* partial_out, int dtype, int64_t N, int64_t C,
@@ -1663,6 +1738,18 @@ int b200_gn_partial_stats(const void* x, float* partial_out, int dtype, int64_t 
   int rc = check_shape(N, C, S, G, &sh);
   if (rc != B200_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // 16-byte rows: the persistent streaming pass; otherwise (or when the
+  // caller's workspace is sized for the chunked pass only) the chunked one.
+  if (dtype == B200_DTYPE_F32)
+    rc = launch_stats_stream<float>(static_cast<const float*>(x), partial_out, sh, workspace,
+                                    workspace_bytes, s);
+  else if (dtype == B200_DTYPE_F16)
+    rc = launch_stats_stream<__half>(static_cast<const __half*>(x), partial_out, sh, workspace,
+                                     workspace_bytes, s);
+  else
+    rc = launch_stats_stream<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x), partial_out,
+                                            sh, workspace, workspace_bytes, s);
+  if (rc <= 0) return rc;
   if (dtype == B200_DTYPE_F32)
     return launch_stats<float>(static_cast<const float*>(x), partial_out, sh, workspace,
                                workspace_bytes, s);
