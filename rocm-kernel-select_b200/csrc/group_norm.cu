@@ -774,7 +774,9 @@ gn_apply_clt_kernel(const T* __restrict__ x, const float* __restrict__ stats,
       k.y = gamma ? rstd * load_param(gamma, affine_dt, c) : rstd;
       k.z = beta ? load_param(beta, affine_dt, c) : 0.f;
     }
-    coef[threadIdx.x] = k;
+    // Stored channel-within-group major, so that the lanes of a warp (one
+    // channel group each) read consecutive entries below.
+    coef[(threadIdx.x & 7) * CGW + (threadIdx.x >> 3)] = k;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -783,7 +785,7 @@ gn_apply_clt_kernel(const T* __restrict__ x, const float* __restrict__ stats,
   if (c0 >= C) return;
   float4 k[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) k[i] = coef[8 * cg + i];
+  for (int i = 0; i < 8; ++i) k[i] = coef[i * CGW + cg];
   const T* xr = x + (n * C + c0) * S;
   T* yn = y + n * S * C + c0;
   auto pos = [&](int t) {
@@ -1136,7 +1138,7 @@ gn_s_stats_kernel(const T* __restrict__ x, float2* __restrict__ part, int64_t M,
                   int64_t total_chunks, float keep_fraction) {
   constexpr int V = Vec16<T>::N;
   constexpr int64_t kChunk = s_chunk<T>();
-  __shared__ float scratch[33];
+  __shared__ float2 red[kSThreads / 32];
   const uint64_t pol = l2_policy_evict_last(keep_fraction);
   uint4 cur[kSVec], nxt[kSVec];
   auto issue = [&](int64_t c, uint4 (&r)[kSVec]) {
@@ -1171,11 +1173,23 @@ gn_s_stats_kernel(const T* __restrict__ x, float2* __restrict__ part, int64_t M,
         }
       }
     }
-    s1 = block_sum<kSThreads>(s1, scratch);
-    s2 = block_sum<kSThreads>(s2, scratch);
-    if (threadIdx.x == 0) part[c] = make_float2(s1, s2);
+    // One block reduction of the (sum, sum of squares) pair.
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(s1, s2);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float2 tot = red[0];
+#pragma unroll
+      for (int w = 1; w < kSThreads / 32; ++w) {
+        tot.x += red[w].x;
+        tot.y += red[w].y;
+      }
+      part[c] = tot;
+    }
 #pragma unroll
     for (int u = 0; u < kSVec; ++u) cur[u] = nxt[u];
+    __syncthreads();  // red[] is rewritten by the next chunk
   }
   pdl_launch_dependents();
 }
