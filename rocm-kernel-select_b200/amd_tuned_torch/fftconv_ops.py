@@ -341,6 +341,12 @@ def fftconv1d_autograd(input: torch.Tensor, weight: torch.Tensor, bias: Optional
     return FFTConv1dFn.apply(input, weight, bias, padding)
 
 
+def _bins(fsize) -> int:
+    """Frequency bins of a real 3-D transform of extents fsize (last axis halved)."""
+    fd, fh, fw = fsize
+    return fd * fh * (fw // 2 + 1)
+
+
 def fft_conv3d(signal: torch.Tensor, kernel: torch.Tensor, bias: Optional[torch.Tensor] = None,
                padding=0, stride=1, dilation=1, groups: int = 1) -> Optional[torch.Tensor]:
     """F.conv3d-equivalent through the FFT kernels (groups 1, stride 1,
@@ -362,7 +368,9 @@ def fft_conv3d(signal: torch.Tensor, kernel: torch.Tensor, bias: Optional[torch.
     base = (_next_smooth_len(Dp), _next_smooth_len(Hp), fft_length(Wp))
     plans = []
     p2 = (_next_smooth_len(Dp, (2,)), _next_smooth_len(Hp, (2,)), _next_smooth_len(Wp, (2,)))
-    if p2 != base:
+    # The cached weight spectrum grows with the transform volume: a power-of-
+    # two plan is only tried when it costs at most a quarter more bins.
+    if p2 != base and _bins(p2) <= 1.25 * _bins(base):
         plans.append(("pow2", p2))
     plans.append((_ORIGINAL_LEN, base))
     key = ("conv3d", signal.dtype, tuple(signal.shape), tuple(kernel.shape), pad)

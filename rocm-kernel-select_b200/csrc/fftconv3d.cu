@@ -77,6 +77,28 @@ __device__ __forceinline__ int qdiv(int a, int d, float inv_d) {
   return q;
 }
 
+// Gathers total elements into shared memory with kGather independent global
+// loads in flight per thread: load(i) returns element i, slot(i) its
+// shared-memory index.  (A plain loop leaves one load in flight per thread,
+// and these kernels then wait out one memory latency per element.)
+constexpr int kGather = 8;
+template <typename LoadF, typename SlotF>
+__device__ __forceinline__ void gather_smem(float2* buf, int total, LoadF load, SlotF slot) {
+  for (int base = threadIdx.x; base < total; base += blockDim.x * kGather) {
+    float2 v[kGather];
+#pragma unroll
+    for (int u = 0; u < kGather; ++u) {
+      const int i = base + u * static_cast<int>(blockDim.x);
+      v[u] = i < total ? load(i) : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kGather; ++u) {
+      const int i = base + u * static_cast<int>(blockDim.x);
+      if (i < total) buf[slot(i)] = v[u];
+    }
+  }
+}
+
 // One pass over nseq sequences; element j of sequence s at buf[s*ss + j*es].
 template <int R, bool INV>
 __device__ __forceinline__ void bpass(float2* buf, int n, int span, int nseq, int ss, int es,
@@ -168,14 +190,19 @@ plane_fwd_kernel(const T* __restrict__ x, float2* __restrict__ G, int64_t n_item
   build_small_tw(twh, Fh);
   build_small_tw(tww, Fw);
   const float inv_fw0 = 1.0f / static_cast<float>(Fw);
-  for (int idx = threadIdx.x; idx < Fh * Fw; idx += blockDim.x) {
-    const int hh = qdiv(idx, Fw, inv_fw0), ww = idx - hh * Fw;
-    const int h = hh - oh, w = ww - ow;
-    const bool in = h >= 0 && h < H && w >= 0 && w < W;
-    const float re = in ? to_f32(x0[h * W + w]) : 0.f;
-    const float im = (in && has1) ? to_f32(x1[h * W + w]) : 0.f;
-    buf[hh * RS + ww] = make_float2(re, im);
-  }
+  gather_smem(
+      buf, Fh * Fw,
+      [&](int idx) {
+        const int hh = qdiv(idx, Fw, inv_fw0), ww = idx - hh * Fw;
+        const int h = hh - oh, w = ww - ow;
+        const bool in = h >= 0 && h < H && w >= 0 && w < W;
+        return make_float2(in ? to_f32(x0[h * W + w]) : 0.f,
+                           (in && has1) ? to_f32(x1[h * W + w]) : 0.f);
+      },
+      [&](int idx) {
+        const int hh = qdiv(idx, Fw, inv_fw0);
+        return hh * RS + (idx - hh * Fw);
+      });
   __syncthreads();
   int* posh = reinterpret_cast<int*>(buf + Fh * RS);
   int* posw = posh + Fh;
@@ -209,16 +236,23 @@ depth_fwd_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, in
   build_pos(posd, pl.d);
   const int fk = Fd * kCols;
   const float inv_fk = 1.0f / static_cast<float>(fk);
-  for (int idx = threadIdx.x; idx < nseq * Fd; idx += blockDim.x) {
-    const int c = qdiv(idx, fk, inv_fk);
-    const int r = idx - c * fk;
-    const int j = r / kCols, q = r - j * kCols;   // q fastest: contiguous columns
-    const int d = j - od, col = col0 + q;
-    float2 v = make_float2(0.f, 0.f);
-    if (d >= 0 && d < Dz && col < cols)
-      v = G[((static_cast<int64_t>(p) * C + c) * Dz + d) * cols + col];
-    buf[(c * kCols + q) * SS + j] = v;
-  }
+  gather_smem(
+      buf, nseq * Fd,
+      [&](int idx) {
+        const int c = qdiv(idx, fk, inv_fk);
+        const int r = idx - c * fk;
+        const int j = r / kCols, q = r - j * kCols;   // q fastest: contiguous columns
+        const int d = j - od, col = col0 + q;
+        return (d >= 0 && d < Dz && col < cols)
+                   ? G[((static_cast<int64_t>(p) * C + c) * Dz + d) * cols + col]
+                   : make_float2(0.f, 0.f);
+      },
+      [&](int idx) {
+        const int c = qdiv(idx, fk, inv_fk);
+        const int r = idx - c * fk;
+        const int j = r / kCols, q = r - j * kCols;
+        return (c * kCols + q) * SS + j;
+      });
   __syncthreads();
   bfft<false>(buf, pl.d, nseq, SS, 1, twd);
   const float inv_c = 1.0f / static_cast<float>(C);
@@ -240,7 +274,10 @@ depth_fwd_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, in
 // load.  The input-channel loop runs in steps of 8 with every load of a step
 // issued first.  H is stored scaled by `hscale` (a power of two, see the
 // spectrum header); the sums are scaled back before they are written.
-constexpr int kCi = 8;
+// Input-channel pairs per step: as many weight loads in flight as the
+// registers hold (16 for fp16-complex weights, 8 for fp32-complex).
+template <typename S>
+constexpr int ci_step() { return sizeof(S) == 4 ? 16 : 8; }
 
 __device__ __forceinline__ void cmac(float2& acc, float2 z, float2 h) {
   acc.x = fmaf(z.x, h.x, fmaf(-z.y, h.y, acc.x));
@@ -280,6 +317,11 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
   // Half-warp `par` takes input channels of parity par; lane q of a half owns
   // output channels 4q .. 4q + 3 of each 64-channel block (one 16-byte load
   // of fp16 complex, two of fp32 complex).  The halves are added at the end.
+  // The bin's input spectrum (f and -f) is staged per 64-channel block in
+  // the warp's shared memory, so the registers hold kCi weight loads in flight.
+  constexpr int kCi = ci_step<S>();
+  __shared__ float2 zs_all[kThreads / 32][2][64];
+  float2 (*zs)[64] = zs_all[threadIdx.x >> 5];
   const int par = lane >> 4, q = lane & 15;
   constexpr int kPer = 16 / static_cast<int>(sizeof(S));   // values per 16-byte load
   const bool vec = (Cout % 4) == 0;
@@ -291,39 +333,49 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
       float2 a[4], bsum[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) a[j] = bsum[j] = make_float2(0.f, 0.f);
-      for (int ci0 = 0; ci0 < Cin; ci0 += 2 * kCi) {
-        float2 z[kCi], zz[kCi];
-        S hv[kCi][4];
+      for (int cb = 0; cb < Cin; cb += 64) {
+        __syncwarp();   // the previous block's values are no longer read
 #pragma unroll
-        for (int k = 0; k < kCi; ++k) {
-          const int ci = ci0 + 2 * k + par;
-          const bool in = ci < Cin;
-          z[k] = in ? __ldg(zf + ci) : make_float2(0.f, 0.f);
-          zz[k] = (in && neg) ? __ldg(zn + ci) : make_float2(0.f, 0.f);
-          const S* hr = h + static_cast<int64_t>(in ? ci : 0) * Cout + c0;
-          if (in && vec && c0 + 3 < Cout) {
+        for (int u = 0; u < 2; ++u) {
+          const int ci = cb + lane + 32 * u;
+          zs[0][lane + 32 * u] = ci < Cin ? __ldg(zf + ci) : make_float2(0.f, 0.f);
+          zs[1][lane + 32 * u] = (ci < Cin && neg) ? __ldg(zn + ci) : make_float2(0.f, 0.f);
+        }
+        __syncwarp();
+        const int cend = min(Cin, cb + 64);
+        for (int ci0 = cb; ci0 < cend; ci0 += 2 * kCi) {
+          S hv[kCi][4];
 #pragma unroll
-            for (int v = 0; v < 4; v += kPer) {
-              const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(hr + v));
-              const S* e = reinterpret_cast<const S*>(&w4);
+          for (int k = 0; k < kCi; ++k) {
+            const int ci = ci0 + 2 * k + par;
+            const bool in = ci < cend;
+            const S* hr = h + static_cast<int64_t>(in ? ci : 0) * Cout + c0;
+            if (in && vec && c0 + 3 < Cout) {
 #pragma unroll
-              for (int u = 0; u < kPer; ++u) hv[k][v + u] = e[u];
-            }
-          } else {
+              for (int v = 0; v < 4; v += kPer) {
+                const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(hr + v));
+                const S* e = reinterpret_cast<const S*>(&w4);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (in && c0 + j < Cout) hv[k][j] = __ldg(hr + j);
-              else spec_zero(hv[k][j]);
+                for (int u = 0; u < kPer; ++u) hv[k][v + u] = e[u];
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                if (in && c0 + j < Cout) hv[k][j] = __ldg(hr + j);
+                else spec_zero(hv[k][j]);
+              }
             }
           }
-        }
 #pragma unroll
-        for (int k = 0; k < kCi; ++k) {
+          for (int k = 0; k < kCi; ++k) {
+            const int cl = ci0 - cb + 2 * k + par;          // < 64; zero past cend
+            const float2 z = zs[0][cl & 63], zz = zs[1][cl & 63];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 g = spec_f2(hv[k][j]);
-            cmac(a[j], z[k], g);
-            cmac_conj(bsum[j], zz[k], g);
+            for (int j = 0; j < 4; ++j) {
+              const float2 g = spec_f2(hv[k][j]);
+              cmac(a[j], z, g);
+              cmac_conj(bsum[j], zz, g);
+            }
           }
         }
       }
@@ -367,15 +419,21 @@ depth_inv_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int P, i
   build_pos(posd, pl.d);
   __syncthreads();
   const float inv_c = 1.0f / static_cast<float>(C);
-  for (int idx = threadIdx.x; idx < nseq * Fd; idx += blockDim.x) {
-    const int r = qdiv(idx, C, inv_c);
-    const int c = idx - r * C;
-    const int q = r % kCols, fd = r / kCols;
-    const int col = col0 + q;
-    float2 v = make_float2(0.f, 0.f);
-    if (col < cols) v = U[((static_cast<int64_t>(fd) * cols + col) * P + p) * C + c];
-    buf[(c * kCols + q) * SS + posd[fd]] = v;
-  }
+  gather_smem(
+      buf, nseq * Fd,
+      [&](int idx) {
+        const int r = qdiv(idx, C, inv_c);
+        const int c = idx - r * C;
+        const int q = r % kCols, fd = r / kCols;
+        const int col = col0 + q;
+        return col < cols ? U[((static_cast<int64_t>(fd) * cols + col) * P + p) * C + c]
+                          : make_float2(0.f, 0.f);
+      },
+      [&](int idx) {
+        const int r = qdiv(idx, C, inv_c);
+        const int c = idx - r * C;
+        return (c * kCols + r % kCols) * SS + posd[r / kCols];
+      });
   __syncthreads();
   bfft<true>(buf, pl.d, nseq, SS, 1, twd);
   const int dk = Do * kCols;
@@ -416,10 +474,12 @@ plane_inv_kernel(const float2* __restrict__ G2, T* __restrict__ y, const void* _
   build_pos(posw, pl.w);
   __syncthreads();
   const float inv_fw = 1.0f / static_cast<float>(Fw);
-  for (int idx = threadIdx.x; idx < Fh * Fw; idx += blockDim.x) {
-    const int fh = qdiv(idx, Fw, inv_fw), fw = idx - fh * Fw;
-    buf[posh[fh] * RS + posw[fw]] = g[idx];
-  }
+  gather_smem(
+      buf, Fh * Fw, [&](int idx) { return g[idx]; },
+      [&](int idx) {
+        const int fh = qdiv(idx, Fw, inv_fw);
+        return posh[fh] * RS + posw[idx - fh * Fw];
+      });
   __syncthreads();
   bfft<true>(buf, pl.h, Fw, 1, RS, twh);
   bfft<true>(buf, pl.w, Fh, RS, 1, tww);
