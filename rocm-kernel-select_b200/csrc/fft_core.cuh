@@ -97,6 +97,45 @@ __device__ __forceinline__ float2 root<32>(int e) {
   }
 }
 template <>
+__device__ __forceinline__ float2 root<30>(int e) {
+  switch (((e % 30) + 30) % 30) {
+    case 0: return make_float2(1.000000000f, 0.f);
+    case 1: return make_float2(0.978147601f, -0.207911691f);
+    case 2: return make_float2(0.913545458f, -0.406736643f);
+    case 3: return make_float2(0.809016994f, -0.587785252f);
+    case 4: return make_float2(0.669130606f, -0.743144825f);
+    case 5: return make_float2(0.500000000f, -0.866025404f);
+    case 6: return make_float2(0.309016994f, -0.951056516f);
+    case 7: return make_float2(0.104528463f, -0.994521895f);
+    case 8: return make_float2(-0.104528463f, -0.994521895f);
+    case 9: return make_float2(-0.309016994f, -0.951056516f);
+    case 10: return make_float2(-0.500000000f, -0.866025404f);
+    case 11: return make_float2(-0.669130606f, -0.743144825f);
+    case 12: return make_float2(-0.809016994f, -0.587785252f);
+    case 13: return make_float2(-0.913545458f, -0.406736643f);
+    case 14: return make_float2(-0.978147601f, -0.207911691f);
+    case 15: return make_float2(-1.000000000f, 0.f);
+    case 16: return make_float2(-0.978147601f, 0.207911691f);
+    case 17: return make_float2(-0.913545458f, 0.406736643f);
+    case 18: return make_float2(-0.809016994f, 0.587785252f);
+    case 19: return make_float2(-0.669130606f, 0.743144825f);
+    case 20: return make_float2(-0.500000000f, 0.866025404f);
+    case 21: return make_float2(-0.309016994f, 0.951056516f);
+    case 22: return make_float2(-0.104528463f, 0.994521895f);
+    case 23: return make_float2(0.104528463f, 0.994521895f);
+    case 24: return make_float2(0.309016994f, 0.951056516f);
+    case 25: return make_float2(0.500000000f, 0.866025404f);
+    case 26: return make_float2(0.669130606f, 0.743144825f);
+    case 27: return make_float2(0.809016994f, 0.587785252f);
+    case 28: return make_float2(0.913545458f, 0.406736643f);
+    default: return make_float2(0.978147601f, 0.207911691f);
+  }
+}
+template <>
+__device__ __forceinline__ float2 root<15>(int e) { return root<30>(2 * e); }
+template <>
+__device__ __forceinline__ float2 root<6>(int e) { return root<30>(5 * e); }
+template <>
 __device__ __forceinline__ float2 root<8>(int e) { return root<16>(2 * e); }
 template <>
 __device__ __forceinline__ float2 root<4>(int e) { return root<16>(4 * e); }
@@ -229,6 +268,18 @@ struct Dft<16, INV> {
 template <bool INV>
 struct Dft<32, INV> {
   static __device__ __forceinline__ void run(float2 (&v)[32]) { DftSplit<2, 16, INV>::run(v); }
+};
+template <bool INV>
+struct Dft<6, INV> {
+  static __device__ __forceinline__ void run(float2 (&v)[6]) { DftSplit<2, 3, INV>::run(v); }
+};
+template <bool INV>
+struct Dft<15, INV> {
+  static __device__ __forceinline__ void run(float2 (&v)[15]) { DftSplit<3, 5, INV>::run(v); }
+};
+template <bool INV>
+struct Dft<30, INV> {
+  static __device__ __forceinline__ void run(float2 (&v)[30]) { DftSplit<2, 15, INV>::run(v); }
 };
 template <bool INV>
 struct Dft<9, INV> {

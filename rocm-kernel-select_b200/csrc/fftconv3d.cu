@@ -267,6 +267,93 @@ depth_fwd_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, in
   }
 }
 
+// ------------------------------------------------ K2 / K4, in registers ---
+// Depth transforms of a compile-time length FD (30 for the cfg 4a shapes)
+// with each sequence in one thread's registers (fft::Dft<FD>, natural order
+// in and out).  A CTA takes 16 columns x 16 channels of one pair: the loads
+// read 16 consecutive columns (128 bytes) per (channel, depth); the switch to
+// the channel-fastest spectrum layout goes through shared memory, so the
+// stores (K2) / loads (K4) move 16 consecutive channels per (bin, column).
+// ~10x fewer instructions per point than the shared-memory pass engine.
+constexpr int kDCols = 16, kDCh = 16;
+
+template <int FD>
+size_t depth_reg_smem() { return static_cast<size_t>(FD) * kDCols * (kDCh + 1) * sizeof(float2); }
+
+template <int FD>
+__global__ void __launch_bounds__(kDCols * kDCh, 2)
+depth_fwd_reg_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, int C, int Dz,
+                     int od, int cols) {
+  extern __shared__ float2 sm[];   // [FD][kDCols][kDCh + 1]
+  const int tcol = threadIdx.x % kDCols, tch = threadIdx.x / kDCols;
+  const int ctiles = (cols + kDCols - 1) / kDCols, chtiles = (C + kDCh - 1) / kDCh;
+  int b = blockIdx.x;
+  const int coltile = b % ctiles;
+  b /= ctiles;
+  const int chtile = b % chtiles, p = b / chtiles;
+  const int col = coltile * kDCols + tcol, c = chtile * kDCh + tch;
+  float2 v[FD];
+#pragma unroll
+  for (int j = 0; j < FD; ++j) v[j] = make_float2(0.f, 0.f);
+  if (col < cols && c < C) {
+    const float2* g = G + (static_cast<int64_t>(p) * C + c) * Dz * cols + col;
+#pragma unroll
+    for (int j = 0; j < FD; ++j) {
+      const int d = j - od;
+      if (d >= 0 && d < Dz) v[j] = g[static_cast<int64_t>(d) * cols];
+    }
+  }
+  fft::Dft<FD, false>::run(v);
+#pragma unroll
+  for (int f = 0; f < FD; ++f) sm[(f * kDCols + tcol) * (kDCh + 1) + tch] = v[f];
+  __syncthreads();
+  for (int i = threadIdx.x; i < FD * kDCols * kDCh; i += kDCols * kDCh) {
+    const int cc = i % kDCh, r = i / kDCh, q = r % kDCols, f = r / kDCols;
+    const int colw = coltile * kDCols + q, cw = chtile * kDCh + cc;
+    if (colw < cols && cw < C)
+      Z[((static_cast<int64_t>(f) * cols + colw) * P + p) * C + cw] =
+          sm[(f * kDCols + q) * (kDCh + 1) + cc];
+  }
+}
+
+template <int FD>
+__global__ void __launch_bounds__(kDCols * kDCh, 2)
+depth_inv_reg_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int P, int C, int Do,
+                     int cols) {
+  extern __shared__ float2 sm[];   // [FD][kDCols][kDCh + 1]
+  const int tcol = threadIdx.x % kDCols, tch = threadIdx.x / kDCols;
+  const int ctiles = (cols + kDCols - 1) / kDCols, chtiles = (C + kDCh - 1) / kDCh;
+  int b = blockIdx.x;
+  const int coltile = b % ctiles;
+  b /= ctiles;
+  const int chtile = b % chtiles, p = b / chtiles;
+  gather_smem(
+      sm, FD * kDCols * kDCh,
+      [&](int i) {
+        const int cc = i % kDCh, r = i / kDCh, q = r % kDCols, f = r / kDCols;
+        const int colr = coltile * kDCols + q, cr = chtile * kDCh + cc;
+        return (colr < cols && cr < C)
+                   ? U[((static_cast<int64_t>(f) * cols + colr) * P + p) * C + cr]
+                   : make_float2(0.f, 0.f);
+      },
+      [&](int i) {
+        const int cc = i % kDCh, r = i / kDCh;
+        return r * (kDCh + 1) + cc;
+      });
+  __syncthreads();
+  const int col = coltile * kDCols + tcol, c = chtile * kDCh + tch;
+  float2 v[FD];
+#pragma unroll
+  for (int f = 0; f < FD; ++f) v[f] = sm[(f * kDCols + tcol) * (kDCh + 1) + tch];
+  fft::Dft<FD, true>::run(v);
+  if (col < cols && c < C) {
+    float2* g = G2 + (static_cast<int64_t>(p) * C + c) * Do * cols + col;
+#pragma unroll
+    for (int o = 0; o < FD; ++o)
+      if (o < Do) g[static_cast<int64_t>(o) * cols] = v[o];
+  }
+}
+
 // --------------------------------------------------------------- K3 -----
 // U[f][p][co] = sum_ci Z[f][p][ci] H[hb][ci][co], and the partner -f with
 // conj(H).  One warp per stored bin; lane l owns output channels 2l, 2l + 1
@@ -613,6 +700,16 @@ int forward_volume(const T* x, float2* G, float2* Z, int64_t n_items, int64_t it
                                                          ow, pl);
   B200_LAUNCH_CHECK("plane_fwd_kernel");
   const int cols = pl.h.n * pl.w.n;
+  if (pl.d.n == 30) {
+    const size_t rs = depth_reg_smem<30>();
+    if ((rc = set_smem(depth_fwd_reg_kernel<30>, rs)) != B200_OK) return rc;
+    const int64_t g2 = npairs * ((C + kDCh - 1) / kDCh) * ((cols + kDCols - 1) / kDCols);
+    if (g2 > 0x7fffffffLL) return fail_unsupported("grid too large");
+    depth_fwd_reg_kernel<30><<<(unsigned)g2, kDCols * kDCh, rs, s>>>(G, Z, (int)npairs, C, Dz,
+                                                                      od, cols);
+    B200_LAUNCH_CHECK("depth_fwd_reg_kernel");
+    return B200_OK;
+  }
   const int64_t g2 = npairs * ((cols + kCols - 1) / kCols);
   depth_fwd_kernel<<<(unsigned)g2, kThreads, ds, s>>>(G, Z, (int)npairs, C, Dz, od, pl);
   B200_LAUNCH_CHECK("depth_fwd_kernel");
@@ -679,9 +776,19 @@ int fwd_typed(const void* xv, const void* spec, const void* bias, int bias_dt, v
   if ((rc = set_smem(plane_inv_kernel<T>, ps)) != B200_OK) return rc;
   const int cols = pl.h.n * pl.w.n;
   float2* G2 = G;   // G is dead once Z is built
-  depth_inv_kernel<<<(unsigned)(sz.P * ((cols + kCols - 1) / kCols)), kThreads, ds, s>>>(
-      U, G2, (int)sz.P, (int)Cout, (int)Do, pl);
-  B200_LAUNCH_CHECK("depth_inv_kernel");
+  if (pl.d.n == 30) {
+    const size_t rs = depth_reg_smem<30>();
+    if ((rc = set_smem(depth_inv_reg_kernel<30>, rs)) != B200_OK) return rc;
+    const int64_t g4 = sz.P * ((Cout + kDCh - 1) / kDCh) * ((cols + kDCols - 1) / kDCols);
+    if (g4 > 0x7fffffffLL) return fail_unsupported("grid too large");
+    depth_inv_reg_kernel<30><<<(unsigned)g4, kDCols * kDCh, rs, s>>>(U, G2, (int)sz.P,
+                                                                      (int)Cout, (int)Do, cols);
+    B200_LAUNCH_CHECK("depth_inv_reg_kernel");
+  } else {
+    depth_inv_kernel<<<(unsigned)(sz.P * ((cols + kCols - 1) / kCols)), kThreads, ds, s>>>(
+        U, G2, (int)sz.P, (int)Cout, (int)Do, pl);
+    B200_LAUNCH_CHECK("depth_inv_kernel");
+  }
   const float scale = 1.0f / static_cast<float>(static_cast<double>(pl.d.n) * pl.h.n * pl.w.n);
   const int64_t g5 = sz.P * Cout * Do;
   if (g5 > 0x7fffffffLL) return fail_unsupported("grid too large");

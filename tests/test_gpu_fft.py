@@ -189,6 +189,10 @@ def test_fftconv3d_golden(cuda, case):
     (3, 5, 7, 9, 10, 3, (5, 6, 7), (2, 3, 3), "f32"),
     (1, 16, 8, 12, 12, 70, (7, 7, 7), (3, 3, 3), "bf16"),
     (2, 8, 6, 20, 6, 8, (6, 9, 6), (0, 4, 2), "f16"),
+    # depth transform of 30 points (the register depth kernels): channel
+    # counts that are not multiples of the 16-channel tile, an odd batch
+    (3, 20, 16, 12, 12, 24, (15, 5, 5), (7, 2, 2), "f16"),
+    (1, 6, 10, 8, 8, 10, (21, 3, 3), (10, 1, 1), "f32"),
 ])
 def test_fftconv3d_shapes(cuda, N, Cin, D, H, W, Cout, k, p, dt):
     from amd_tuned_torch import fftconv_ops
