@@ -300,8 +300,7 @@ def per_shape(dev, peaks, only=None, small=False) -> dict:
         byt = 134219776
         best = None
         stock = _stock_us(lambda i: torch.group_norm(xs[i % nbuf], 32, wd, bd, 1e-6), 50, stream)
-        for name, var in (("auto", ops.GN_AUTO), ("l2", ops.GN_L2), ("stream", ops.GN_STREAM),
-                          ("pipe", ops.GN_PIPE), ("inter", ops.GN_INTER)):
+        for name, var in (("auto", ops.GN_AUTO), ("l2", ops.GN_L2), ("stream", ops.GN_STREAM)):
             y = ops.group_norm(xs[0], 32, wd, bd, 1e-6, variant=var)
             if y is None:
                 continue

@@ -58,25 +58,15 @@ int b200_sm_count(void);
  * (src/main_rocm.cpp:556-599) and its kernel group_norm_kernel
  * (src/cuda/group_norm.cu:40-104).  x, y: contiguous [N, C, S] with
  * S = product of spatial dims; gamma/beta: [C] of `affine_dtype` or NULL.
- * variant: 0 auto, 1 split (stats + apply, uses workspace),
+ * variant: 0 auto (streaming for 16-byte rows that fit the L2 keep budget,
+ *            else the cluster kernel for small groups, else split),
+ *          1 split (stats + apply, uses workspace),
  *          2 two-pass: statistics pass, then a normalise pass that re-reads
  *            x (from L2 when the tensor fits), both 16-byte vectorised,
  *          3 streaming: statistics on a persistent grid (next chunk's loads
  *            in flight while the current one is reduced), a per-channel
  *            scale/shift kernel, and a persistent normalise pass over the
  *            whole tensor (16-byte rows required),
- *          4 pipelined clusters: persistent 8-CTA clusters each owning
- *            whole groups in turn; each CTA's slice arrives by bulk copy
- *            (later groups' copies in flight), statistics are exchanged
- *            through distributed shared memory, the normalised slice leaves
- *            by bulk store -- one read and one write of the tensor (declines
- *            unless rows are whole 16-byte vectors, a group splits into 8
- *            slices of whole vectors, and two slices fit in shared memory),
- *          5 interleaved: one persistent kernel taking tickets from a list
- *            that interleaves the statistics chunks of group g + lag with
- *            the normalise chunks of group g (the re-read hits L2, reads of
- *            later groups overlap writes of earlier ones; 16-byte rows
- *            required; uses workspace),
  *          16 + k: single-read cluster kernel with k CTAs per group
  *          (k in {1, 2, 4, 8, 16}; group slice held in shared memory). */
 size_t b200_gn_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int dtype,

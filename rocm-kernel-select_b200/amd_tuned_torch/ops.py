@@ -161,7 +161,7 @@ def clear_caches() -> None:
 
 # ------------------------------------------------------------ GroupNorm ---
 # auto; stats+apply; two-pass L2-resident; three-kernel streaming (persistent grids)
-GN_AUTO, GN_SPLIT, GN_L2, GN_STREAM, GN_PIPE, GN_INTER = 0, 1, 2, 3, 4, 5
+GN_AUTO, GN_SPLIT, GN_L2, GN_STREAM = 0, 1, 2, 3
 
 
 def gn_cluster_variant(k: int) -> int:

@@ -28,7 +28,6 @@
 #include <type_traits>
 
 #include "common.cuh"
-#include "sm100_ptx.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -188,177 +187,6 @@ inline FastDiv make_fastdiv(uint32_t d) {
 
 __device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f) {
   return static_cast<uint32_t>((static_cast<uint64_t>(__umulhi(n, f.m)) + n) >> f.l);
-}
-
-// --------------------------------------------------- pipelined clusters ----
-// Variant 4: persistent clusters of kPipeCluster CTAs.  A cluster owns whole
-// groups in turn (cluster c takes groups c, c + clusters, ...), each CTA one
-// contiguous 1/kPipeCluster slice of the group.  Per group: the slice lands
-// in shared memory by one bulk copy, issued NBUF - 1 groups ahead; the CTA
-// sums it shifted by the group's first element (fp32 per thread, fp64
-// across the cluster); one cluster barrier publishes the partial sums, which
-// every warp reads from the peers' shared memory (DSMEM) and merges in the
-// same fixed order, so all CTAs hold bit-identical statistics; the slice is
-// normalised in place and written back by one bulk store.  HBM traffic: one
-// read and one write of the tensor, with the reads of later groups in flight
-// during the arithmetic and the barrier of the current one.
-constexpr int kPipeThreads = 512;
-constexpr int kPipeMaxBuf = 3;
-constexpr int kPipeMaxChannels = 256;  // channels one slice may touch
-constexpr int kFaultGnPipe = 5;
-
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
-               ::"l"(dst), "r"(smem_u32(src)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ float2 ld_dsmem_f2(uint32_t cluster_addr) {
-  float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];"
-               : "=f"(v.x), "=f"(v.y)
-               : "r"(cluster_addr)
-               : "memory");
-  return v;
-}
-
-// csize CTAs per cluster (8, or 16 with the non-portable cluster size).
-template <typename T>
-__global__ void __launch_bounds__(kPipeThreads, 1)
-gn_pipe_kernel(const T* __restrict__ x, const void* __restrict__ gamma,
-               const void* __restrict__ beta, T* __restrict__ y, int affine_dt, int S,
-               FastDiv div_s, int G, int Cg, int64_t groups, float eps, int slice, int nbuf,
-               int csize, int* gflags) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ __align__(8) uint64_t bars[kPipeMaxBuf];
-  __shared__ float2 part[2];      // (sum, sum of squares) of this CTA's slice, by parity
-  __shared__ float2 red[kPipeThreads / 32];
-  __shared__ float2 ab[kPipeMaxChannels];  // per channel of the slice: rstd * gamma, beta
-  constexpr int V = Vec16<T>::N;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t rank = cluster_ctarank();
-  const int64_t cid = cluster_id_x(), ncl = nclusters_x();
-  const int64_t M = static_cast<int64_t>(Cg) * S;
-  const uint32_t bytes = static_cast<uint32_t>(slice) * sizeof(T);
-  T* buf0 = reinterpret_cast<T*>(smem_raw);
-  const int64_t iters = cid < groups ? (groups - cid + ncl - 1) / ncl : 0;
-  const int nv = slice / V;
-  const int e0 = static_cast<int>(rank) * slice;       // slice start within the group
-  const int cl0 = static_cast<int>(fast_div(static_cast<uint32_t>(e0), div_s));
-  const int nch = static_cast<int>(fast_div(static_cast<uint32_t>(e0 + slice - 1), div_s)) -
-                  cl0 + 1;
-
-  if (tid == 0) {
-    for (int b = 0; b < nbuf; ++b) mbar_init(&bars[b], 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  auto issue = [&](int64_t it) {
-    const int b = static_cast<int>(it % nbuf);
-    mbar_expect_tx(&bars[b], bytes);
-    bulk_load(buf0 + static_cast<int64_t>(b) * slice, x + (cid + it * ncl) * M + e0, bytes,
-              &bars[b]);
-  };
-  if (tid == 0)
-    for (int64_t it = 0; it < iters && it < nbuf - 1; ++it) issue(it);
-
-  for (int64_t it = 0; it < iters; ++it) {
-    const int b = static_cast<int>(it % nbuf);
-    const int64_t grp = cid + it * ncl;
-    T* sb = buf0 + static_cast<int64_t>(b) * slice;
-    const float shift = to_f32(x[grp * M]);  // the same in every CTA of the cluster
-    // A wait that runs out leaves garbage in the slice but keeps the control
-    // flow (and so the cluster barriers) identical in every CTA.
-    mbar_wait_bounded(&bars[b], static_cast<uint32_t>((it / nbuf) & 1), nullptr, gflags,
-                      kFaultGnPipe);
-
-    // Shifted sums of the slice.
-    float s = 0.f, q = 0.f;
-    const uint4* v4 = reinterpret_cast<const uint4*>(sb);
-    for (int i = tid; i < nv; i += kPipeThreads) {
-      float v[V];
-      unpack16<T>(v4[i], v);
-#pragma unroll
-      for (int e = 0; e < V; ++e) {
-        const float d = v[e] - shift;
-        s += d;
-        q = fmaf(d, d, q);
-      }
-    }
-    s = warp_sum(s);
-    q = warp_sum(q);
-    if (lane == 0) red[warp] = make_float2(s, q);
-    __syncthreads();
-    if (warp == 0) {
-      float2 t = lane < kPipeThreads / 32 ? red[lane] : make_float2(0.f, 0.f);
-      t.x = warp_sum(t.x);
-      t.y = warp_sum(t.y);
-      if (lane == 0) part[it & 1] = t;
-    }
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    // Two buffers: the next load fills the buffer the previous group was
-    // stored from, so it is issued here, once that store has read it.
-    if (nbuf == 2 && tid == 0 && it + 1 < iters) {
-      bulk_wait_read0();
-      issue(it + 1);
-    }
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-
-    // Every warp merges the csize partials in the same order.
-    double ds = 0.0, dq = 0.0;
-    if (lane < csize) {
-      const float2 p = ld_dsmem_f2(mapa_u32(&part[it & 1], static_cast<uint32_t>(lane)));
-      ds = p.x;
-      dq = p.y;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {  // every lane ends with the totals
-      ds += __shfl_xor_sync(0xffffffffu, ds, o);
-      dq += __shfl_xor_sync(0xffffffffu, dq, o);
-    }
-    const double md = ds / static_cast<double>(M);
-    const double var = fmax(dq / static_cast<double>(M) - md * md, 0.0);
-    const float mean = static_cast<float>(static_cast<double>(shift) + md);
-    const float rstd = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
-    const int c0 = static_cast<int>(grp % G) * Cg + cl0;
-    if (tid < nch) {
-      ab[tid] = make_float2(gamma ? rstd * load_param(gamma, affine_dt, c0 + tid) : rstd,
-                            beta ? load_param(beta, affine_dt, c0 + tid) : 0.f);
-    }
-    __syncthreads();
-
-    // (x - mean) * (rstd gamma) + beta in place, then one bulk store.
-    uint4* w4 = reinterpret_cast<uint4*>(sb);
-    for (int i = tid; i < nv; i += kPipeThreads) {
-      const float2 f = ab[fast_div(static_cast<uint32_t>(e0 + i * V), div_s) - cl0];
-      float v[V];
-      unpack16<T>(w4[i], v);
-#pragma unroll
-      for (int e = 0; e < V; ++e) v[e] = fmaf(v[e] - mean, f.x, f.y);
-      w4[i] = pack16<T>(v);
-    }
-    fence_proxy_async();
-    __syncthreads();
-    if (tid == 0) {
-      bulk_store(y + grp * M + e0, sb, bytes);
-      bulk_commit();
-      // Three buffers: the load of group it + 2 reuses the buffer of group
-      // it - 1, whose store (one group older than the one just issued) has
-      // long finished reading it, so this wait does not stall.
-      if (nbuf == 3 && it + 2 < iters) {
-        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-        issue(it + 2);
-      }
-    }
-  }
-  if (tid == 0) bulk_wait_all0();
-  cluster_sync();  // peers may still be reading this CTA's part[]
 }
 
 // ------------------------------------------------------- split: stats ----
@@ -906,58 +734,6 @@ int launch_cluster(const T* x, const void* gamma, const void* beta, T* y, int af
   return B200_OK;
 }
 
-// Variant 4 (csize = 8 CTAs per cluster; 16-CTA clusters measured slower:
-// fewer of them can be resident).  Declines (> 0) unless x / y
-// are 16-byte aligned, a slice is a whole number of 16-byte vectors, the
-// group has fewer than 2^31 elements, a slice touches at most
-// kPipeMaxChannels channels and two slices fit in shared memory.
-template <typename T>
-int launch_pipe(const T* x, const void* gamma, const void* beta, T* y, int affine_dt,
-                const GnShape& sh, float eps, int csize, cudaStream_t stream) {
-  constexpr int V = Vec16<T>::N;
-  if (!vec_ok<T>(x, y, sh) || sh.M % (csize * V) != 0 || sh.M >= (1LL << 31))
-    return fail_unsupported("GroupNorm pipelined clusters: unaligned or oversized groups");
-  const int64_t slice = sh.M / csize;
-  if (slice / sh.S + 2 > kPipeMaxChannels)
-    return fail_unsupported("GroupNorm pipelined clusters: a slice spans too many channels");
-  const size_t sbytes = static_cast<size_t>(slice) * sizeof(T);
-  const size_t room = static_cast<size_t>(max_smem_optin()) - 4096;
-  const int nbuf = 3 * sbytes <= room ? 3 : 2;
-  if (2 * sbytes > room) return fail_unsupported("GroupNorm slice exceeds shared memory");
-  const size_t smem = nbuf * sbytes;
-  auto kern = gn_pipe_kernel<T>;
-  B200_CUDA_CHECK(
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  if (csize > 8)
-    B200_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-  cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(kPipeThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = csize;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cfg.gridDim = dim3(static_cast<unsigned>(csize * std::min<int64_t>(sh.groups, 1024)));
-  int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
-    cudaGetLastError();
-    return fail_unsupported("cluster configuration cannot be scheduled");
-  }
-  const int64_t ncl = std::min<int64_t>(sh.groups, clusters);
-  cfg.gridDim = dim3(static_cast<unsigned>(csize * ncl));
-  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, x, gamma, beta, y, affine_dt,
-                                     static_cast<int>(sh.S),
-                                     make_fastdiv(static_cast<uint32_t>(sh.S)),
-                                     static_cast<int>(sh.G), static_cast<int>(sh.Cg), sh.groups,
-                                     eps, static_cast<int>(slice), nbuf, csize,
-                                     device_flags_ptr()));
-  return B200_OK;
-}
-
 template <typename T>
 int launch_stats(const T* x, float* stats_out, const GnShape& sh, void* ws, size_t ws_bytes,
                  cudaStream_t stream) {
@@ -1276,229 +1052,6 @@ gn_s_apply_kernel(const T* __restrict__ x, const float2* __restrict__ coef, T* _
   }
 }
 
-// ---------------------------------------------------- interleaved passes ---
-// Variant 5: one persistent kernel walks a ticket list that interleaves the
-// two passes group by group -- the statistics chunks of group g + lag come
-// right before the normalise chunks of group g -- so the reads of later
-// groups overlap the writes of earlier ones and the re-read of a group hits
-// L2 (it was read lag groups, a few MB, earlier).  A statistics item reads
-// its chunk (16-byte vectors, all in flight, marked evict_last), stores the
-// chunk's sums shifted by the group's first element and counts itself into
-// done[g] (release).  A normalise item issues its chunk's loads first, then
-// waits (acquire, bounded) until done[g] holds every chunk of the group,
-// merges the group's sums in fp64 in chunk order (the same in every item of
-// the group) and streams y out.  Tickets come from an atomic counter, so a
-// CTA only ever waits on items that running CTAs took before it: no
-// residency assumption, no deadlock.
-constexpr int kIThreads = 256;
-constexpr int kIVec = 8;  // 16-byte vectors per thread per item
-constexpr int kFaultGnInter = 6;
-
-struct InterPlan {
-  int groups, cpg, lag;  // groups (N * G), chunks per group, lag in groups
-};
-
-// Ticket -> (normalise item?, group, chunk).  Blocks of cpg tickets: S(0) ..
-// S(lag - 1), then S(lag), A(0), S(lag + 1), A(1), ..., then the last lag A's.
-__device__ __forceinline__ void inter_item(int t, const InterPlan& p, bool* apply, int* g,
-                                           int* c) {
-  const int blk = t / p.cpg;
-  *c = t - blk * p.cpg;
-  const int L = p.lag, G = p.groups;
-  if (blk < L) {
-    *apply = false;
-    *g = blk;
-    return;
-  }
-  const int r = blk - L;
-  if (r < 2 * (G - L)) {
-    *apply = (r & 1) != 0;
-    *g = (r & 1) ? (r >> 1) : L + (r >> 1);
-    return;
-  }
-  *apply = true;
-  *g = G - L + (r - 2 * (G - L));
-}
-
-// Statistics word of a group before its last chunk publishes it (both
-// halves 0xffffffff, a NaN pattern no arithmetic produces).
-constexpr uint64_t kStatUnset = ~0ull;
-
-__device__ __forceinline__ uint64_t ld_acquire_gpu_u64(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_gpu_u64(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
-               : "=r"(old)
-               : "l"(p), "r"(v)
-               : "memory");
-  return old;
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kIThreads)
-gn_inter_kernel(const T* __restrict__ x, const void* __restrict__ gamma,
-                const void* __restrict__ beta, T* __restrict__ y, int affine_dt, int M,
-                FastDiv div_s, int G, int Cg, float eps, InterPlan p, float2* part,
-                uint32_t* done, uint64_t* stat, uint32_t* ticket, float keep, int* gflags) {
-  constexpr int V = Vec16<T>::N;
-  constexpr int CH = kIThreads * kIVec * V;  // elements per item
-  __shared__ float2 red[kIThreads / 32];
-  __shared__ int s_ticket;
-  __shared__ float2 s_stat;  // mean, rstd
-  const int tid = threadIdx.x;
-  const uint64_t keep_pol = l2_policy_evict_last(keep);
-  const uint64_t first_pol = l2_policy_evict_first();
-  const int total = 2 * p.groups * p.cpg;
-  if (tid == 0) s_ticket = static_cast<int>(atomicAdd(ticket, 1u));
-  __syncthreads();
-  int t = s_ticket;
-  while (t < total) {
-    __syncthreads();  // every thread has read s_ticket
-    if (tid == 0) s_ticket = static_cast<int>(atomicAdd(ticket, 1u));  // next, in flight
-    bool apply;
-    int g, c;
-    inter_item(t, p, &apply, &g, &c);
-    const T* gx = x + static_cast<int64_t>(g) * M;
-    uint4 r[kIVec];
-#pragma unroll
-    for (int u = 0; u < kIVec; ++u) {
-      const int e = c * CH + (u * kIThreads + tid) * V;
-      r[u] = e < M ? ld16_hint(gx + e, apply ? first_pol : keep_pol) : make_uint4(0, 0, 0, 0);
-    }
-    if (!apply) {
-      const float shift = to_f32(gx[0]);
-      float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-      for (int u = 0; u < kIVec; ++u) {
-        if (c * CH + (u * kIThreads + tid) * V < M) {
-          float v[V];
-          unpack16<T>(r[u], v);
-#pragma unroll
-          for (int k = 0; k < V; ++k) {
-            const float d = v[k] - shift;
-            s1 += d;
-            s2 = fmaf(d, d, s2);
-          }
-        }
-      }
-      s1 = warp_sum(s1);
-      s2 = warp_sum(s2);
-      if ((tid & 31) == 0) red[tid >> 5] = make_float2(s1, s2);
-      __syncthreads();
-      if (tid == 0) {
-        float2 tot = red[0];
-        for (int w = 1; w < kIThreads / 32; ++w) {
-          tot.x += red[w].x;
-          tot.y += red[w].y;
-        }
-        part[static_cast<int64_t>(g) * p.cpg + c] = tot;
-        // The group's last chunk merges all of them (fp64, chunk order) and
-        // publishes (mean, rstd) as one 8-byte word: one acquire load is all
-        // a normalise item needs.
-        if (atom_add_acq_rel_gpu(done + g, 1u) == static_cast<uint32_t>(p.cpg - 1)) {
-          double a = 0.0, b = 0.0;
-          for (int j = 0; j < p.cpg; ++j) {
-            const float2 q = __ldcg(part + static_cast<int64_t>(g) * p.cpg + j);
-            a += q.x;
-            b += q.y;
-          }
-          const double n = static_cast<double>(M);
-          const double md = a / n;
-          const double var = fmax(b / n - md * md, 0.0);
-          const float mean = static_cast<float>(md + static_cast<double>(shift));
-          const float rstd = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
-          st_release_gpu_u64(stat + g, (static_cast<uint64_t>(__float_as_uint(rstd)) << 32) |
-                                           __float_as_uint(mean));
-        }
-      }
-    } else {
-      if (tid == 0) {
-        const uint64_t t0 = globaltimer_ns();
-        uint64_t w;
-        while ((w = ld_acquire_gpu_u64(stat + g)) == kStatUnset) {
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            if (gflags) atomicExch(gflags, kFaultGnInter);
-            break;
-          }
-        }
-        s_stat = make_float2(__uint_as_float(static_cast<uint32_t>(w)),
-                             __uint_as_float(static_cast<uint32_t>(w >> 32)));
-      }
-      __syncthreads();
-      const float mean = s_stat.x, rstd = s_stat.y;
-      const int c0 = (g % G) * Cg;
-      T* gy = y + static_cast<int64_t>(g) * M;
-#pragma unroll
-      for (int u = 0; u < kIVec; ++u) {
-        const int e = c * CH + (u * kIThreads + tid) * V;
-        if (e < M) {
-          const int ch = c0 + static_cast<int>(fast_div(static_cast<uint32_t>(e), div_s));
-          const float a = gamma ? rstd * load_param(gamma, affine_dt, ch) : rstd;
-          const float b = beta ? load_param(beta, affine_dt, ch) : 0.f;
-          float v[V];
-          unpack16<T>(r[u], v);
-#pragma unroll
-          for (int k = 0; k < V; ++k) v[k] = fmaf(v[k] - mean, a, b);
-          st_stream16(gy + e, pack16<T>(v));
-        }
-      }
-    }
-    __syncthreads();  // s_ticket written; scratch / s_stat reads done
-    t = s_ticket;
-  }
-}
-
-size_t inter_ws_bytes(const GnShape& sh, size_t esize) {
-  const int64_t ch = static_cast<int64_t>(kIThreads) * kIVec * (16 / static_cast<int64_t>(esize));
-  const int64_t cpg = (sh.M + ch - 1) / ch;
-  return 256 + 2 * ((static_cast<size_t>(sh.groups) * sizeof(uint64_t) + 255) / 256 * 256) +
-         static_cast<size_t>(sh.groups * cpg) * sizeof(float2);
-}
-
-template <typename T>
-int launch_inter(const T* x, const void* gamma, const void* beta, T* y, int affine_dt,
-                 const GnShape& sh, float eps, void* ws, size_t ws_bytes, cudaStream_t stream) {
-  constexpr int64_t CH = static_cast<int64_t>(kIThreads) * kIVec * Vec16<T>::N;
-  if (!vec_ok<T>(x, y, sh)) return fail_unsupported("interleaved GroupNorm needs 16-byte rows");
-  if (sh.M + CH >= (1LL << 31)) return fail_unsupported("interleaved GroupNorm: group too large");
-  const int64_t cpg = (sh.M + CH - 1) / CH;
-  if (2 * sh.groups * cpg >= (1LL << 31)) return fail_unsupported("too many items");
-  if (ws == nullptr || ws_bytes < inter_ws_bytes(sh, sizeof(T)))
-    return fail_arg("GroupNorm workspace too small");
-  // Layout: [ticket (256 B)][done: groups x u32][stat: groups x u64][part: groups x cpg
-  // float2], the first two zeroed and stat set to kStatUnset before every launch.
-  const size_t arr = (static_cast<size_t>(sh.groups) * sizeof(uint64_t) + 255) / 256 * 256;
-  char* base = static_cast<char*>(ws);
-  uint32_t* ticket = reinterpret_cast<uint32_t*>(base);
-  uint32_t* done = reinterpret_cast<uint32_t*>(base + 256);
-  uint64_t* stat = reinterpret_cast<uint64_t*>(base + 256 + arr);
-  float2* part = reinterpret_cast<float2*>(base + 256 + 2 * arr);
-  B200_CUDA_CHECK(cudaMemsetAsync(base, 0, 256 + arr, stream));
-  B200_CUDA_CHECK(cudaMemsetAsync(stat, 0xff, arr, stream));
-  const int sms = sm_count();
-  // Four 256-thread CTAs per SM (the register limit at 64 per thread).
-  const int grid = static_cast<int>(std::min<int64_t>(2 * sh.groups * cpg, 4LL * sms));
-  InterPlan plan;
-  plan.groups = static_cast<int>(sh.groups);
-  plan.cpg = static_cast<int>(cpg);
-  plan.lag = static_cast<int>(std::min<int64_t>(sh.groups, (grid + cpg - 1) / cpg + 4));
-  const double bytes = static_cast<double>(sh.N) * sh.C * sh.S * sizeof(T);
-  const float keep = static_cast<float>(std::min(1.0, kL2KeepBytes / bytes));
-  gn_inter_kernel<T><<<grid, kIThreads, 0, stream>>>(
-      x, gamma, beta, y, affine_dt, static_cast<int>(sh.M),
-      make_fastdiv(static_cast<uint32_t>(sh.S)), static_cast<int>(sh.G),
-      static_cast<int>(sh.Cg), eps, plan, part, done, stat, ticket, keep, device_flags_ptr());
-  B200_LAUNCH_CHECK("gn_inter_kernel");
-  return B200_OK;
-}
-
 // (count, mean, M2) per group from the streaming statistics pass's shifted
 // chunk sums (one warp per group, fixed-order fp64 merge): the
 // b200_gn_partial_stats output for 16-byte rows.
@@ -1657,9 +1210,6 @@ int gn_fwd_typed(const void* xv, const void* gamma, const void* beta, void* yv, 
   if (variant == 2) return launch_l2<T>(x, gamma, beta, y, affine_dt, sh, eps, false, ws, ws_bytes, stream);
   if (variant == 3)
     return launch_stream<T>(x, gamma, beta, y, affine_dt, sh, eps, false, ws, ws_bytes, stream);
-  if (variant == 4) return launch_pipe<T>(x, gamma, beta, y, affine_dt, sh, eps, 8, stream);
-  if (variant == 5)
-    return launch_inter<T>(x, gamma, beta, y, affine_dt, sh, eps, ws, ws_bytes, stream);
   if (variant == 0) {
     const int k = auto_cluster(sh, sizeof(T));
     if (k > 0) {
@@ -1709,8 +1259,7 @@ size_t b200_gn_workspace_bytes(int64_t N, int64_t C, int64_t S, int64_t G, int d
   const size_t stats_bytes = ((static_cast<size_t>(sh.groups * 3) * sizeof(float) + 15) / 16) * 16;
   const size_t split = stats_bytes + stats_ws_bytes(sh, dtype);
   const size_t l2 = l2_ws_bytes(sh, dtype_size(dtype));
-  const size_t st = std::max(s_ws_bytes(sh, dtype_size(dtype)),
-                             inter_ws_bytes(sh, dtype_size(dtype)));
+  const size_t st = s_ws_bytes(sh, dtype_size(dtype));
   return std::max(split, std::max(l2, st));
 }
 
