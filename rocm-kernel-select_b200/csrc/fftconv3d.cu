@@ -217,7 +217,16 @@ plane_fwd_kernel(const T* __restrict__ x, float2* __restrict__ G, int64_t n_item
   int* posw = posh + Fh;
   build_pos(posh, pl.h);
   build_pos(posw, pl.w);
-  bfft<false>(buf, pl.w, Fh, RS, 1, tww);   // rows (its barriers also publish posh / posw)
+  // Rows (their barriers also publish posh / posw); rows outside the data are
+  // zero and stay zero, so only the H data rows are transformed.
+  {
+    const int r0 = oh > 0 ? oh : 0, r1 = oh + H < Fh ? oh + H : Fh;
+    if (r1 > r0) {
+      bfft<false>(buf + r0 * RS, pl.w, r1 - r0, RS, 1, tww);
+    } else {
+      __syncthreads();
+    }
+  }
   bfft<false>(buf, pl.h, Fw, 1, RS, twh);   // columns
   float2* g = G + ((p * C + c) * Dz + dz) * static_cast<int64_t>(Fh) * Fw;
   const float inv_fw = 1.0f / static_cast<float>(Fw);
@@ -578,7 +587,7 @@ plane_inv_kernel(const float2* __restrict__ G2, T* __restrict__ y, const void* _
       });
   __syncthreads();
   bfft<true>(buf, pl.h, Fw, 1, RS, twh);
-  bfft<true>(buf, pl.w, Fh, RS, 1, tww);
+  bfft<true>(buf, pl.w, Ho < Fh ? Ho : Fh, RS, 1, tww);   // only the rows that are output
   const float bv = bias ? load_param(bias, bias_dt, c) : 0.f;
   const int64_t n0 = 2 * p, n1 = n0 + 1;
   const int64_t vol = static_cast<int64_t>(Do) * Ho * Wo;
