@@ -402,8 +402,19 @@ __device__ __forceinline__ void spec_zero(__half2& v) { v = __floats2half2_rn(0.
 __device__ __forceinline__ void spec_put(float2* o, float a, float b) { *o = make_float2(a, b); }
 __device__ __forceinline__ void spec_put(__half2* o, float a, float b) { *o = __floats2half2_rn(a, b); }
 
-template <typename S>
-__global__ void __launch_bounds__(kThreads, 2)
+// 8-byte global -> shared copy; bytes past src_bytes are zero-filled.
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem, int src_bytes) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(sa), "l"(gmem),
+               "r"(src_bytes) : "memory");
+}
+
+// NARROW: Cout <= 16, where NG >= 8 lane groups cover a 64-channel block in a
+// few short steps; a quarter of the weight registers lets three CTAs share an
+// SM instead of two, so more bins' loads are in flight (at such channel counts
+// a bin is ~2 KB of weights and the kernel is latency-bound, not HBM-bound).
+template <typename S, bool NARROW>
+__global__ void __launch_bounds__(kThreads, NARROW ? 3 : 2)
 contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
                 const float* __restrict__ hdr, float2* __restrict__ U, int P, int Cin, int Cout,
                 int Fd, int Fh, int Fw, int64_t hbins) {
@@ -419,43 +430,55 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
   const bool neg = fw > 0 && 2 * fw != Fw;
   const int64_t fn = (static_cast<int64_t>((Fd - fd) % Fd) * Fh + (Fh - fh) % Fh) * Fw + (Fw - fw);
   const S* h = Hs + hb * Cin * Cout;
-  // Half-warp `par` takes input channels of parity par; lane q of a half owns
-  // output channels 4q .. 4q + 3 of each 64-channel block (one 16-byte load
-  // of fp16 complex, two of fp32 complex).  The halves are added at the end.
+  // The warp splits into NG groups of LPG lanes (LPG = 16 for Cout >= 64;
+  // fewer for narrow outputs, e.g. a rank's slice of a channel-sharded conv,
+  // so that no lane idles): group g takes input channels ci = g (mod NG),
+  // lane q of a group owns output channels 4q .. 4q + 3 of each 4 * LPG
+  // channel block (one 16-byte load of fp16 complex, two of fp32 complex).
+  // The groups' sums are added at the end.
   // The bin's input spectrum (f and -f) is staged per 64-channel block in
   // the warp's shared memory, so the registers hold kCi weight loads in flight.
-  constexpr int kCi = ci_step<S>();
+  constexpr int kCi = NARROW ? ci_step<S>() / 4 : ci_step<S>();
   __shared__ float2 zs_all[kThreads / 32][2][64];
   float2 (*zs)[64] = zs_all[threadIdx.x >> 5];
-  const int par = lane >> 4, q = lane & 15;
+  const int LPG = Cout > 32 ? 16 : (Cout > 16 ? 8 : (Cout > 8 ? 4 : (Cout > 4 ? 2 : 1)));
+  const int NG = 32 / LPG;
+  const int grp = lane / LPG, q = lane % LPG;
   constexpr int kPer = 16 / static_cast<int>(sizeof(S));   // values per 16-byte load
   const bool vec = (Cout % 4) == 0;
   for (int p = 0; p < P; ++p) {
     const float2* zf = Z + (f * P + p) * Cin;
     const float2* zn = Z + (fn * P + p) * Cin;
-    for (int co0 = 0; co0 < Cout; co0 += 64) {
+    for (int co0 = 0; co0 < Cout; co0 += 4 * LPG) {
       const int c0 = co0 + 4 * q;
       float2 a[4], bsum[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) a[j] = bsum[j] = make_float2(0.f, 0.f);
       for (int cb = 0; cb < Cin; cb += 64) {
+        const int cend = min(Cin, cb + 64);
+        // The block's input spectrum is copied straight into shared memory
+        // while the first step's weight loads are in flight (one memory
+        // round trip per step, not two; no registers held by the copy).
         __syncwarp();   // the previous block's values are no longer read
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int ci = cb + lane + 32 * u;
-          zs[0][lane + 32 * u] = ci < Cin ? __ldg(zf + ci) : make_float2(0.f, 0.f);
-          zs[1][lane + 32 * u] = (ci < Cin && neg) ? __ldg(zn + ci) : make_float2(0.f, 0.f);
+          const bool in = ci < Cin;
+          cp_async8(&zs[0][lane + 32 * u], in ? zf + ci : zf, in ? 8 : 0);
+          cp_async8(&zs[1][lane + 32 * u], (in && neg) ? zn + ci : zf, (in && neg) ? 8 : 0);
         }
-        __syncwarp();
-        const int cend = min(Cin, cb + 64);
-        for (int ci0 = cb; ci0 < cend; ci0 += 2 * kCi) {
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        for (int ci0 = cb; ci0 < cend; ci0 += NG * kCi) {
           S hv[kCi][4];
 #pragma unroll
           for (int k = 0; k < kCi; ++k) {
-            const int ci = ci0 + 2 * k + par;
+            const int ci = ci0 + NG * k + grp;
             const bool in = ci < cend;
             const S* hr = h + static_cast<int64_t>(in ? ci : 0) * Cout + c0;
-            if (in && vec && c0 + 3 < Cout) {
+            if (!in) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) spec_zero(hv[k][j]);
+            } else if (vec && c0 + 3 < Cout) {
 #pragma unroll
               for (int v = 0; v < 4; v += kPer) {
                 const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(hr + v));
@@ -466,14 +489,19 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
             } else {
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
-                if (in && c0 + j < Cout) hv[k][j] = __ldg(hr + j);
+                if (c0 + j < Cout) hv[k][j] = __ldg(hr + j);
                 else spec_zero(hv[k][j]);
               }
             }
           }
+          if (ci0 == cb) {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+            __syncwarp();
+          }
 #pragma unroll
           for (int k = 0; k < kCi; ++k) {
-            const int cl = ci0 - cb + 2 * k + par;          // < 64; zero past cend
+            if (ci0 + NG * k >= cend) break;   // warp-uniform: no group has channels left
+            const int cl = ci0 - cb + NG * k + grp;         // weights are zero past cend
             const float2 z = zs[0][cl & 63], zz = zs[1][cl & 63];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -484,14 +512,16 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
           }
         }
       }
+      for (int o = LPG; o < 32; o <<= 1) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        a[j].x += __shfl_xor_sync(0xffffffffu, a[j].x, 16);
-        a[j].y += __shfl_xor_sync(0xffffffffu, a[j].y, 16);
-        bsum[j].x += __shfl_xor_sync(0xffffffffu, bsum[j].x, 16);
-        bsum[j].y += __shfl_xor_sync(0xffffffffu, bsum[j].y, 16);
+        for (int j = 0; j < 4; ++j) {
+          a[j].x += __shfl_xor_sync(0xffffffffu, a[j].x, o);
+          a[j].y += __shfl_xor_sync(0xffffffffu, a[j].y, o);
+          bsum[j].x += __shfl_xor_sync(0xffffffffu, bsum[j].x, o);
+          bsum[j].y += __shfl_xor_sync(0xffffffffu, bsum[j].y, o);
+        }
       }
-      if (par == 0) {
+      if (grp == 0) {
         float2* uf = U + (f * P + p) * Cout;
         float2* un = U + (fn * P + p) * Cout;
 #pragma unroll
@@ -786,8 +816,13 @@ int fwd_typed(const void* xv, const void* spec, const void* bias, int bias_dt, v
   const float* hdr = static_cast<const float*>(spec);
   const SpecT<T>* Hs =
       reinterpret_cast<const SpecT<T>*>(static_cast<const char*>(spec) + kSpecHeader);
-  contract_kernel<SpecT<T>><<<(unsigned)((warps * 32 + kThreads - 1) / kThreads), kThreads, 0, s>>>(
-      Z, Hs, hdr, U, (int)sz.P, (int)Cin, (int)Cout, pl.d.n, pl.h.n, pl.w.n, sz.hbins);
+  const unsigned cgrid = (unsigned)((warps * 32 + kThreads - 1) / kThreads);
+  if (Cout <= 16)
+    contract_kernel<SpecT<T>, true><<<cgrid, kThreads, 0, s>>>(
+        Z, Hs, hdr, U, (int)sz.P, (int)Cin, (int)Cout, pl.d.n, pl.h.n, pl.w.n, sz.hbins);
+  else
+    contract_kernel<SpecT<T>, false><<<cgrid, kThreads, 0, s>>>(
+        Z, Hs, hdr, U, (int)sz.P, (int)Cin, (int)Cout, pl.d.n, pl.h.n, pl.w.n, sz.hbins);
   B200_LAUNCH_CHECK("contract_kernel");
   const size_t ds = depth_smem(pl, (int)Cout), ps = plane_smem(pl);
   if ((rc = set_smem(depth_inv_kernel, ds)) != B200_OK) return rc;

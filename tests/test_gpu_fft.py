@@ -193,6 +193,11 @@ def test_fftconv3d_golden(cuda, case):
     # counts that are not multiples of the 16-channel tile, an odd batch
     (3, 20, 16, 12, 12, 24, (15, 5, 5), (7, 2, 2), "f16"),
     (1, 6, 10, 8, 8, 10, (21, 3, 3), (10, 1, 1), "f32"),
+    # input channels past one 64-channel block, narrow (Cout <= 16) and wide
+    # contraction variants, output-channel counts off the lane-group widths
+    (1, 70, 6, 8, 8, 16, (3, 3, 3), (1, 1, 1), "bf16"),
+    (2, 72, 5, 6, 6, 13, (3, 3, 3), (1, 1, 1), "f32"),
+    (1, 130, 4, 6, 6, 40, (3, 3, 3), (1, 1, 1), "f16"),
 ])
 def test_fftconv3d_shapes(cuda, N, Cin, D, H, W, Cout, k, p, dt):
     from amd_tuned_torch import fftconv_ops
