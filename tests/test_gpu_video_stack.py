@@ -89,6 +89,46 @@ def test_stack_cfg5_full_size_one_gpu(cuda):
     assert oracle.rel_l2(_np(yb[:, :, 11:15]), ref.numpy()) <= 2e-3
 
 
+def test_stack_cfg5_full_size_chain_matches_stock(cuda):
+    """BASELINE cfg 5 end to end at full size: the 4-block chain on this
+    package's kernels against the same chain in stock torch on the GPU (fp32
+    math, no TF32, activations rounded to bf16 at the same op boundaries),
+    each side feeding its own outputs forward.  Block 1 meets the per-op bar
+    of 2e-3; the chained bound grows with depth because a bf16 rounding that
+    flips in one block is carried (and mixed by the next conv) into the
+    following blocks."""
+    import amd_tuned_torch
+    params = vs.make_params(channels=128, blocks=4, groups=32, dtype=torch.bfloat16, seed=5,
+                            device=cuda)
+    x = torch.randn(1, 128, 64, 128, 128, generator=torch.Generator().manual_seed(6))
+    x = x.bfloat16().to(cuda)
+    stack = vs.VideoStack(params)
+    was = amd_tuned_torch.is_enabled()
+    amd_tuned_torch.disable()
+    tf32 = (torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32)
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    errs = []
+    try:
+        h, r = x, x.float()
+        for i in range(4):
+            h = stack.block(h, i)
+            one = vs.StackParams(params.gn_weight[i:i + 1], params.gn_bias[i:i + 1],
+                                 params.conv_weight[i:i + 1], params.conv_bias[i:i + 1],
+                                 params.groups, params.eps)
+            with torch.no_grad():
+                r = vs.reference_forward(r, one, round_dtype=torch.bfloat16)
+            errs.append(float((h.float() - r).norm() / r.norm()))
+    finally:
+        torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32 = tf32
+        if was:
+            amd_tuned_torch.enable()
+    print("cfg5 full-size chain rel-L2 per block:", errs)
+    assert all(e == e for e in errs), errs
+    assert errs[0] <= 2e-3, errs
+    assert max(errs) <= 6e-3, errs
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
