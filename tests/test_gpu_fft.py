@@ -198,6 +198,10 @@ def test_fftconv3d_golden(cuda, case):
     (1, 70, 6, 8, 8, 16, (3, 3, 3), (1, 1, 1), "bf16"),
     (2, 72, 5, 6, 6, 13, (3, 3, 3), (1, 1, 1), "f32"),
     (1, 130, 4, 6, 6, 40, (3, 3, 3), (1, 1, 1), "f16"),
+    # Cout a multiple of 64 with even input rows: the bulk-copy contraction
+    (2, 24, 5, 8, 8, 64, (3, 3, 3), (1, 1, 1), "f16"),
+    (3, 10, 4, 6, 6, 128, (3, 3, 3), (1, 1, 1), "bf16"),
+    (2, 16, 5, 6, 8, 64, (3, 3, 3), (1, 1, 1), "f32"),
 ])
 def test_fftconv3d_shapes(cuda, N, Cin, D, H, W, Cout, k, p, dt):
     from amd_tuned_torch import fftconv_ops
