@@ -174,16 +174,98 @@ __device__ __forceinline__ void bfft(float2* buf, const fft::Plan& p, int nseq, 
   }
 }
 
+// Two-pass transforms of a compile-time plan RA x RB (the 80-point plane
+// rows and columns of cfg 4a: 16 x 5): the pass geometry and the index
+// divisions become constants (bpass divides by runtime pass sizes through
+// qdiv and picks the radix with a switch per pass).
+template <int R, bool INV, int N, int SPAN>
+__device__ __forceinline__ void bpass_ct(float2* buf, int nseq, int ss, int es,
+                                         const float2* tw) {
+  constexpr int stride = SPAN / R, per = N / R, tscale = N / SPAN;
+  const int total = nseq * per;
+  for (int b = threadIdx.x; b < total; b += blockDim.x) {
+    const int s = b / per, bb = b - s * per;
+    const int g = bb / stride, k = bb - g * stride;
+    float2* base = buf + s * ss + (g * SPAN + k) * es;
+    float2 v[R];
+#pragma unroll
+    for (int m = 0; m < R; ++m) v[m] = base[m * stride * es];
+    if (!INV) {
+      fft::Dft<R, false>::run(v);
+      if (k != 0) {
+#pragma unroll
+        for (int m = 1; m < R; ++m) v[m] = fft::cmul(v[m], tw[k * m * tscale]);
+      }
+    } else {
+      if (k != 0) {
+#pragma unroll
+        for (int m = 1; m < R; ++m) v[m] = fft::cmulc(v[m], tw[k * m * tscale]);
+      }
+      fft::Dft<R, true>::run(v);
+    }
+#pragma unroll
+    for (int m = 0; m < R; ++m) base[m * stride * es] = v[m];
+  }
+}
+
+// bfft for a plan of exactly two passes RA, RB (same order and output as
+// bfft with that plan).
+template <bool INV, int RA, int RB>
+__device__ __forceinline__ void bfft2_ct(float2* buf, int nseq, int ss, int es,
+                                         const float2* tw) {
+  constexpr int N = RA * RB;
+  if (!INV) {
+    bpass_ct<RA, false, N, N>(buf, nseq, ss, es, tw);
+    __syncthreads();
+    bpass_ct<RB, false, N, RB>(buf, nseq, ss, es, tw);
+    __syncthreads();
+  } else {
+    bpass_ct<RB, true, N, RB>(buf, nseq, ss, es, tw);
+    __syncthreads();
+    bpass_ct<RA, true, N, N>(buf, nseq, ss, es, tw);
+    __syncthreads();
+  }
+}
+
+// Plane transforms: NP = 80 is the 80 x 80 plane with the 16 x 5 plan in
+// both directions (compile-time), NP = 0 any plan.
+template <bool INV, int NP>
+__device__ __forceinline__ void plane_fft(float2* buf, const fft::Plan& p, int nseq, int ss,
+                                          int es, const float2* tw) {
+  if constexpr (NP == 80) {
+    bfft2_ct<INV, 16, 5>(buf, nseq, ss, es, tw);
+  } else {
+    bfft<INV>(buf, p, nseq, ss, es, tw);
+  }
+}
+
+template <int NP>
+__device__ __forceinline__ int div_np(int a, int n, float inv_n) {
+  if constexpr (NP != 0) {
+    return a / NP;
+  } else {
+    return qdiv(a, n, inv_n);
+  }
+}
+
+// Whether both plane plans are 80 = 16 x 5 (the NP = 80 plane kernels).
+inline bool plane80(const fft::Plan& h, const fft::Plan& w) {
+  auto is80 = [](const fft::Plan& p) {
+    return p.n == 80 && p.passes == 2 && p.radix[0] == 16 && p.radix[1] == 5;
+  };
+  return is80(h) && is80(w);
+}
+
 // --------------------------------------------------------------- K1 -----
 // items [n_items][C][Dz][H][W] real (T); pair p packs items item0+2p, +2p+1.
 // Output G[p][c][dz][Fh][Fw] complex, natural order.  Placement offset
 // (oh, ow) of the real data inside the transform plane.
-template <typename T>
+template <typename T, int NP>
 __global__ void __launch_bounds__(kThreads, 3)
 plane_fwd_kernel(const T* __restrict__ x, float2* __restrict__ G, int64_t n_items, int64_t item0,
                  int C, int Dz, int H, int W, int oh, int ow, const Plan3 pl) {
   extern __shared__ float2 sm[];
-  const int Fh = pl.h.n, Fw = pl.w.n, RS = plane_row_stride(Fw);
+  const int Fh = NP ? NP : pl.h.n, Fw = NP ? NP : pl.w.n, RS = plane_row_stride(Fw);
   float2* twh = sm;
   float2* tww = twh + Fh;
   float2* buf = tww + Fw;
@@ -202,14 +284,14 @@ plane_fwd_kernel(const T* __restrict__ x, float2* __restrict__ G, int64_t n_item
   gather_smem(
       buf, Fh * Fw,
       [&](int idx) {
-        const int hh = qdiv(idx, Fw, inv_fw0), ww = idx - hh * Fw;
+        const int hh = div_np<NP>(idx, Fw, inv_fw0), ww = idx - hh * Fw;
         const int h = hh - oh, w = ww - ow;
         const bool in = h >= 0 && h < H && w >= 0 && w < W;
         return make_float2(in ? to_f32(x0[h * W + w]) : 0.f,
                            (in && has1) ? to_f32(x1[h * W + w]) : 0.f);
       },
       [&](int idx) {
-        const int hh = qdiv(idx, Fw, inv_fw0);
+        const int hh = div_np<NP>(idx, Fw, inv_fw0);
         return hh * RS + (idx - hh * Fw);
       });
   __syncthreads();
@@ -222,16 +304,16 @@ plane_fwd_kernel(const T* __restrict__ x, float2* __restrict__ G, int64_t n_item
   {
     const int r0 = oh > 0 ? oh : 0, r1 = oh + H < Fh ? oh + H : Fh;
     if (r1 > r0) {
-      bfft<false>(buf + r0 * RS, pl.w, r1 - r0, RS, 1, tww);
+      plane_fft<false, NP>(buf + r0 * RS, pl.w, r1 - r0, RS, 1, tww);
     } else {
       __syncthreads();
     }
   }
-  bfft<false>(buf, pl.h, Fw, 1, RS, twh);   // columns
+  plane_fft<false, NP>(buf, pl.h, Fw, 1, RS, twh);   // columns
   float2* g = G + ((p * C + c) * Dz + dz) * static_cast<int64_t>(Fh) * Fw;
   const float inv_fw = 1.0f / static_cast<float>(Fw);
   for (int idx = threadIdx.x; idx < Fh * Fw; idx += blockDim.x) {
-    const int fh = qdiv(idx, Fw, inv_fw), fw = idx - fh * Fw;
+    const int fh = div_np<NP>(idx, Fw, inv_fw), fw = idx - fh * Fw;
     g[idx] = buf[posh[fh] * RS + posw[fw]];
   }
 }
@@ -586,13 +668,13 @@ depth_inv_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int P, i
 // --------------------------------------------------------------- K5 -----
 // G2[p][co][od][Fh*Fw] -> y[n][co][od][Ho][Wo] (inverse plane FFT, crop,
 // scale, bias).
-template <typename T>
+template <typename T, int NP>
 __global__ void __launch_bounds__(kThreads, 3)
 plane_inv_kernel(const float2* __restrict__ G2, T* __restrict__ y, const void* __restrict__ bias,
                  int bias_dt, int64_t N, int C, int Do, int Ho, int Wo, float scale,
                  const Plan3 pl) {
   extern __shared__ float2 sm[];
-  const int Fh = pl.h.n, Fw = pl.w.n, RS = plane_row_stride(Fw);
+  const int Fh = NP ? NP : pl.h.n, Fw = NP ? NP : pl.w.n, RS = plane_row_stride(Fw);
   float2* twh = sm;
   float2* tww = twh + Fh;
   float2* buf = tww + Fw;
@@ -612,12 +694,12 @@ plane_inv_kernel(const float2* __restrict__ G2, T* __restrict__ y, const void* _
   gather_smem(
       buf, Fh * Fw, [&](int idx) { return g[idx]; },
       [&](int idx) {
-        const int fh = qdiv(idx, Fw, inv_fw);
+        const int fh = div_np<NP>(idx, Fw, inv_fw);
         return posh[fh] * RS + posw[idx - fh * Fw];
       });
   __syncthreads();
-  bfft<true>(buf, pl.h, Fw, 1, RS, twh);
-  bfft<true>(buf, pl.w, Ho < Fh ? Ho : Fh, RS, 1, tww);   // only the rows that are output
+  plane_fft<true, NP>(buf, pl.h, Fw, 1, RS, twh);
+  plane_fft<true, NP>(buf, pl.w, Ho < Fh ? Ho : Fh, RS, 1, tww);   // only the output rows
   const float bv = bias ? load_param(bias, bias_dt, c) : 0.f;
   const int64_t n0 = 2 * p, n1 = n0 + 1;
   const int64_t vol = static_cast<int64_t>(Do) * Ho * Wo;
@@ -740,12 +822,13 @@ int forward_volume(const T* x, float2* G, float2* Z, int64_t n_items, int64_t it
                    const Plan3& pl, cudaStream_t s) {
   int rc;
   const size_t ps = plane_smem(pl), ds = depth_smem(pl, C);
-  if ((rc = set_smem(plane_fwd_kernel<T>, ps)) != B200_OK) return rc;
+  const bool p80 = plane80(pl.h, pl.w);
+  auto plane_fwd = p80 ? plane_fwd_kernel<T, 80> : plane_fwd_kernel<T, 0>;
+  if ((rc = set_smem(plane_fwd, ps)) != B200_OK) return rc;
   if ((rc = set_smem(depth_fwd_kernel, ds)) != B200_OK) return rc;
   const int64_t g1 = npairs * C * Dz;
   if (g1 > 0x7fffffffLL) return fail_unsupported("grid too large");
-  plane_fwd_kernel<T><<<(unsigned)g1, kThreads, ps, s>>>(x, G, n_items, item0, C, Dz, H, W, oh,
-                                                         ow, pl);
+  plane_fwd<<<(unsigned)g1, kThreads, ps, s>>>(x, G, n_items, item0, C, Dz, H, W, oh, ow, pl);
   B200_LAUNCH_CHECK("plane_fwd_kernel");
   const int cols = pl.h.n * pl.w.n;
   if (pl.d.n == 30) {
@@ -826,7 +909,8 @@ int fwd_typed(const void* xv, const void* spec, const void* bias, int bias_dt, v
   B200_LAUNCH_CHECK("contract_kernel");
   const size_t ds = depth_smem(pl, (int)Cout), ps = plane_smem(pl);
   if ((rc = set_smem(depth_inv_kernel, ds)) != B200_OK) return rc;
-  if ((rc = set_smem(plane_inv_kernel<T>, ps)) != B200_OK) return rc;
+  auto plane_inv = plane80(pl.h, pl.w) ? plane_inv_kernel<T, 80> : plane_inv_kernel<T, 0>;
+  if ((rc = set_smem(plane_inv, ps)) != B200_OK) return rc;
   const int cols = pl.h.n * pl.w.n;
   float2* G2 = G;   // G is dead once Z is built
   if (pl.d.n == 30) {
@@ -845,9 +929,8 @@ int fwd_typed(const void* xv, const void* spec, const void* bias, int bias_dt, v
   const float scale = 1.0f / static_cast<float>(static_cast<double>(pl.d.n) * pl.h.n * pl.w.n);
   const int64_t g5 = sz.P * Cout * Do;
   if (g5 > 0x7fffffffLL) return fail_unsupported("grid too large");
-  plane_inv_kernel<T><<<(unsigned)g5, kThreads, ps, s>>>(G2, static_cast<T*>(yv), bias, bias_dt,
-                                                         N, (int)Cout, (int)Do, (int)Ho, (int)Wo,
-                                                         scale, pl);
+  plane_inv<<<(unsigned)g5, kThreads, ps, s>>>(G2, static_cast<T*>(yv), bias, bias_dt, N,
+                                               (int)Cout, (int)Do, (int)Ho, (int)Wo, scale, pl);
   B200_LAUNCH_CHECK("plane_inv_kernel");
   return B200_OK;
 }
