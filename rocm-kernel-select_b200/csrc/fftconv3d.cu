@@ -491,12 +491,13 @@ __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, int src_
                "r"(src_bytes) : "memory");
 }
 
-// NARROW: Cout <= 16, where NG >= 8 lane groups cover a 64-channel block in a
-// few short steps; a quarter of the weight registers lets three CTAs share an
-// SM instead of two, so more bins' loads are in flight (at such channel counts
-// a bin is ~2 KB of weights and the kernel is latency-bound, not HBM-bound).
-template <typename S, bool NARROW>
-__global__ void __launch_bounds__(kThreads, NARROW ? 3 : 2)
+// KDIV: the step holds ci_step / KDIV weight loads per lane.  KDIV = 1 runs
+// two CTAs per SM at 128 registers; KDIV = 2 and 4 run three at <= 85, which
+// keeps more bins in flight per SM: KDIV = 4 for Cout <= 16 (NG >= 8 lane
+// groups cover a 64-channel block in a few short steps; a bin is ~2 KB of
+// weights and the kernel latency-bound), KDIV = 2 for wider fp16 spectra.
+template <typename S, int KDIV>
+__global__ void __launch_bounds__(kThreads, KDIV == 1 ? 2 : 3)
 contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
                 const float* __restrict__ hdr, float2* __restrict__ U, int P, int Cin, int Cout,
                 int Fd, int Fh, int Fw, int64_t hbins) {
@@ -520,7 +521,7 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
   // The groups' sums are added at the end.
   // The bin's input spectrum (f and -f) is staged per 64-channel block in
   // the warp's shared memory, so the registers hold kCi weight loads in flight.
-  constexpr int kCi = NARROW ? ci_step<S>() / 4 : ci_step<S>();
+  constexpr int kCi = ci_step<S>() / KDIV;
   __shared__ float2 zs_all[kThreads / 32][2][64];
   float2 (*zs)[64] = zs_all[threadIdx.x >> 5];
   const int LPG = Cout > 32 ? 16 : (Cout > 16 ? 8 : (Cout > 8 ? 4 : (Cout > 4 ? 2 : 1)));
@@ -900,11 +901,18 @@ int fwd_typed(const void* xv, const void* spec, const void* bias, int bias_dt, v
   const SpecT<T>* Hs =
       reinterpret_cast<const SpecT<T>*>(static_cast<const char*>(spec) + kSpecHeader);
   const unsigned cgrid = (unsigned)((warps * 32 + kThreads - 1) / kThreads);
-  if (Cout <= 16)
-    contract_kernel<SpecT<T>, true><<<cgrid, kThreads, 0, s>>>(
+  // Weight loads in flight per lane against CTAs per SM (measured at cfg 4a,
+  // Cout = 64, fp16 spectrum: kCi 16 at two CTAs 597 us per op, kCi 8 at
+  // three 572 us, kCi 4 at three 598 us).
+  const int kd = Cout <= 16 ? 4 : (sizeof(SpecT<T>) == 4 ? 2 : 1);
+  if (kd == 4)
+    contract_kernel<SpecT<T>, 4><<<cgrid, kThreads, 0, s>>>(
+        Z, Hs, hdr, U, (int)sz.P, (int)Cin, (int)Cout, pl.d.n, pl.h.n, pl.w.n, sz.hbins);
+  else if (kd == 2)
+    contract_kernel<SpecT<T>, 2><<<cgrid, kThreads, 0, s>>>(
         Z, Hs, hdr, U, (int)sz.P, (int)Cin, (int)Cout, pl.d.n, pl.h.n, pl.w.n, sz.hbins);
   else
-    contract_kernel<SpecT<T>, false><<<cgrid, kThreads, 0, s>>>(
+    contract_kernel<SpecT<T>, 1><<<cgrid, kThreads, 0, s>>>(
         Z, Hs, hdr, U, (int)sz.P, (int)Cin, (int)Cout, pl.d.n, pl.h.n, pl.w.n, sz.hbins);
   B200_LAUNCH_CHECK("contract_kernel");
   const size_t ds = depth_smem(pl, (int)Cout), ps = plane_smem(pl);
