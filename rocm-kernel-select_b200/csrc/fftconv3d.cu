@@ -502,13 +502,17 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
                 const float* __restrict__ hdr, float2* __restrict__ U, int P, int Cin, int Cout,
                 int Fd, int Fh, int Fw, int64_t hbins) {
   const int lane = threadIdx.x & 31;
-  const int64_t hb = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-  if (hb >= hbins) return;
+  // Bin indices fit 32 bits (extents <= 256, so hbins < 2^24): 32-bit
+  // division here, not the 64-bit routine (~10% of this kernel's instructions).
+  const int hbi = static_cast<int>((blockIdx.x * static_cast<unsigned>(kThreads) + threadIdx.x) >> 5);
+  if (hbi >= hbins) return;
+  const int64_t hb = hbi;
   const float inv = 1.0f / __ldg(hdr);
   const int Fw2 = Fw / 2 + 1;
-  const int fw = static_cast<int>(hb % Fw2);
-  const int fh = static_cast<int>((hb / Fw2) % Fh);
-  const int fd = static_cast<int>(hb / (static_cast<int64_t>(Fw2) * Fh));
+  const int q2 = hbi / Fw2;
+  const int fw = hbi - q2 * Fw2;
+  const int fd = q2 / Fh;
+  const int fh = q2 - fd * Fh;
   const int64_t f = (static_cast<int64_t>(fd) * Fh + fh) * Fw + fw;
   const bool neg = fw > 0 && 2 * fw != Fw;
   const int64_t fn = (static_cast<int64_t>((Fd - fd) % Fd) * Fh + (Fh - fh) % Fh) * Fw + (Fw - fw);
@@ -529,6 +533,7 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
   const int grp = lane / LPG, q = lane % LPG;
   constexpr int kPer = 16 / static_cast<int>(sizeof(S));   // values per 16-byte load
   const bool vec = (Cout % 4) == 0;
+  const bool dense = Cout % (4 * LPG) == 0;   // every lane's 4 channels exist
   for (int p = 0; p < P; ++p) {
     const float2* zf = Z + (f * P + p) * Cin;
     const float2* zn = Z + (fn * P + p) * Cin;
@@ -553,6 +558,37 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
         asm volatile("cp.async.commit_group;" ::: "memory");
         for (int ci0 = cb; ci0 < cend; ci0 += NG * kCi) {
           S hv[kCi][4];
+          if (dense && ci0 + NG * kCi <= cend) {
+            // Whole step in range (warp-uniform): plain strided 16-byte loads.
+            const S* hp = h + static_cast<int64_t>(ci0 + grp) * Cout + c0;
+            const int st = NG * Cout;
+#pragma unroll
+            for (int k = 0; k < kCi; ++k) {
+#pragma unroll
+              for (int v = 0; v < 4; v += kPer) {
+                const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(hp + k * st + v));
+                const S* e = reinterpret_cast<const S*>(&w4);
+#pragma unroll
+                for (int u = 0; u < kPer; ++u) hv[k][v + u] = e[u];
+              }
+            }
+            if (ci0 == cb) {
+              asm volatile("cp.async.wait_group 0;" ::: "memory");
+              __syncwarp();
+            }
+#pragma unroll
+            for (int k = 0; k < kCi; ++k) {
+              const int cl = ci0 - cb + NG * k + grp;
+              const float2 z = zs[0][cl], zz = zs[1][cl];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 g = spec_f2(hv[k][j]);
+                cmac(a[j], z, g);
+                cmac_conj(bsum[j], zz, g);
+              }
+            }
+            continue;
+          }
 #pragma unroll
           for (int k = 0; k < kCi; ++k) {
             const int ci = ci0 + NG * k + grp;
