@@ -938,8 +938,8 @@ int fwd_typed(const void* xv, const void* spec, const void* bias, int bias_dt, v
       reinterpret_cast<const SpecT<T>*>(static_cast<const char*>(spec) + kSpecHeader);
   const unsigned cgrid = (unsigned)((warps * 32 + kThreads - 1) / kThreads);
   // Weight loads in flight per lane against CTAs per SM (measured at cfg 4a,
-  // Cout = 64, fp16 spectrum: kCi 16 at two CTAs 597 us per op, kCi 8 at
-  // three 572 us, kCi 4 at three 598 us).
+  // Cout = 64, fp16 spectrum, whole op: kCi 16 at two CTAs 541 us, kCi 8 at
+  // three 530 us, kCi 4 at three 554 us).
   const int kd = Cout <= 16 ? 4 : (sizeof(SpecT<T>) == 4 ? 2 : 1);
   if (kd == 4)
     contract_kernel<SpecT<T>, 4><<<cgrid, kThreads, 0, s>>>(
