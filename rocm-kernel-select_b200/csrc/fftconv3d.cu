@@ -466,6 +466,24 @@ depth_inv_reg_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int 
 template <typename S>
 constexpr int ci_step() { return sizeof(S) == 4 ? 16 : 8; }
 
+// Packed fp32 pairs (sm_100 fma.rn.f32x2: two fp32 FMAs per instruction).
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 up2(unsigned long long v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b,
+                                                   unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 __device__ __forceinline__ void cmac(float2& acc, float2 z, float2 h) {
   acc.x = fmaf(z.x, h.x, fmaf(-z.y, h.y, acc.x));
   acc.y = fmaf(z.x, h.y, fmaf(z.y, h.x, acc.y));
@@ -576,16 +594,32 @@ contract_kernel(const float2* __restrict__ Z, const S* __restrict__ Hs,
               asm volatile("cp.async.wait_group 0;" ::: "memory");
               __syncwarp();
             }
+            // Packed pairs: a += (hx, hy) (zx, zx) + (hy, hx) (-zy, zy) is z h;
+            // b += (hx, hy) (zzx, -zzx) + (hy, hx) (zzy, zzy) is zz conj(h).
+            unsigned long long A[4], B[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              A[j] = pk2(a[j].x, a[j].y);
+              B[j] = pk2(bsum[j].x, bsum[j].y);
+            }
 #pragma unroll
             for (int k = 0; k < kCi; ++k) {
               const int cl = ci0 - cb + NG * k + grp;
               const float2 z = zs[0][cl], zz = zs[1][cl];
+              const unsigned long long zxx = pk2(z.x, z.x), zyn = pk2(-z.y, z.y);
+              const unsigned long long wxn = pk2(zz.x, -zz.x), wyy = pk2(zz.y, zz.y);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const float2 g = spec_f2(hv[k][j]);
-                cmac(a[j], z, g);
-                cmac_conj(bsum[j], zz, g);
+                const unsigned long long hp = pk2(g.x, g.y), hs = pk2(g.y, g.x);
+                A[j] = fma2(hs, zyn, fma2(hp, zxx, A[j]));
+                B[j] = fma2(hs, wyy, fma2(hp, wxn, B[j]));
               }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              a[j] = up2(A[j]);
+              bsum[j] = up2(B[j]);
             }
             continue;
           }
