@@ -82,17 +82,17 @@ __device__ __forceinline__ int qdiv(int a, int d, float inv_d) {
 // shared-memory index.  (A plain loop leaves one load in flight per thread,
 // and these kernels then wait out one memory latency per element.)
 constexpr int kGather = 8;
-template <typename LoadF, typename SlotF>
+template <int GD = kGather, typename LoadF, typename SlotF>
 __device__ __forceinline__ void gather_smem(float2* buf, int total, LoadF load, SlotF slot) {
-  for (int base = threadIdx.x; base < total; base += blockDim.x * kGather) {
-    float2 v[kGather];
+  for (int base = threadIdx.x; base < total; base += blockDim.x * GD) {
+    float2 v[GD];
 #pragma unroll
-    for (int u = 0; u < kGather; ++u) {
+    for (int u = 0; u < GD; ++u) {
       const int i = base + u * static_cast<int>(blockDim.x);
       v[u] = i < total ? load(i) : make_float2(0.f, 0.f);
     }
 #pragma unroll
-    for (int u = 0; u < kGather; ++u) {
+    for (int u = 0; u < GD; ++u) {
       const int i = base + u * static_cast<int>(blockDim.x);
       if (i < total) buf[slot(i)] = v[u];
     }
@@ -427,7 +427,9 @@ depth_inv_reg_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int 
   const int coltile = b % ctiles;
   b /= ctiles;
   const int chtile = b % chtiles, p = b / chtiles;
-  gather_smem(
+  // All FD loads of a thread in flight at once (the registers are free until
+  // the transform).
+  gather_smem<FD>(
       sm, FD * kDCols * kDCh,
       [&](int i) {
         const int cc = i % kDCh, r = i / kDCh, q = r % kDCols, f = r / kDCols;
@@ -762,7 +764,7 @@ plane_inv_kernel(const float2* __restrict__ G2, T* __restrict__ y, const void* _
   build_pos(posw, pl.w);
   __syncthreads();
   const float inv_fw = 1.0f / static_cast<float>(Fw);
-  gather_smem(
+  gather_smem<16>(
       buf, Fh * Fw, [&](int idx) { return g[idx]; },
       [&](int idx) {
         const int fh = div_np<NP>(idx, Fw, inv_fw);
