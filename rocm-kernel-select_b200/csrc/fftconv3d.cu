@@ -382,8 +382,10 @@ constexpr int kDCols = 16, kDCh = 16;
 template <int FD>
 size_t depth_reg_smem() { return static_cast<size_t>(FD) * kDCols * (kDCh + 1) * sizeof(float2); }
 
+// Three CTAs per SM (80 registers, no spills; cfg 4a op 484 -> 479 us); the
+// inverse, with all FD loads in flight, needs 128 registers and runs two.
 template <int FD>
-__global__ void __launch_bounds__(kDCols * kDCh, 2)
+__global__ void __launch_bounds__(kDCols * kDCh, 3)
 depth_fwd_reg_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, int C, int Dz,
                      int od, int cols) {
   extern __shared__ float2 sm[];   // [FD][kDCols][kDCh + 1]
