@@ -382,8 +382,8 @@ constexpr int kDCols = 16, kDCh = 16;
 template <int FD>
 size_t depth_reg_smem() { return static_cast<size_t>(FD) * kDCols * (kDCh + 1) * sizeof(float2); }
 
-// Three CTAs per SM (80 registers, no spills; cfg 4a op 484 -> 479 us); the
-// inverse, with all FD loads in flight, needs 128 registers and runs two.
+// Three CTAs per SM (80 registers, no spills; cfg 4a op 484 -> 479 us), as
+// the inverse below.
 template <int FD>
 __global__ void __launch_bounds__(kDCols * kDCh, 3)
 depth_fwd_reg_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P, int C, int Dz,
@@ -421,7 +421,7 @@ depth_fwd_reg_kernel(const float2* __restrict__ G, float2* __restrict__ Z, int P
 }
 
 template <int FD>
-__global__ void __launch_bounds__(kDCols * kDCh, 2)
+__global__ void __launch_bounds__(kDCols * kDCh, 3)
 depth_inv_reg_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int P, int C, int Do,
                      int cols) {
   extern __shared__ float2 sm[];   // [FD][kDCols][kDCh + 1]
@@ -431,9 +431,10 @@ depth_inv_reg_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int 
   const int coltile = b % ctiles;
   b /= ctiles;
   const int chtile = b % chtiles, p = b / chtiles;
-  // All FD loads of a thread in flight at once (the registers are free until
-  // the transform).
-  gather_smem<FD>(
+  // Half of a thread's FD loads in flight at once (two batches): all FD at
+  // once needed 128 registers (two CTAs per SM, 47 us at cfg 4a); two batches
+  // fit three CTAs per SM at 80 (op 479 -> 474 us).
+  gather_smem<(FD + 1) / 2>(
       sm, FD * kDCols * kDCh,
       [&](int i) {
         const int cc = i % kDCh, r = i / kDCh, q = r % kDCols, f = r / kDCols;
