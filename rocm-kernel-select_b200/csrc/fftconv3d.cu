@@ -30,10 +30,12 @@ namespace b200 {
 namespace {
 
 constexpr int kThreads = 256;
-// Residency: the transforms run three CTAs per SM (<= 85 registers; a few
-// spilled bytes), the contraction two (<= 128 registers): at the unbounded
-// register counts (90-147) they ran one or two, too few warps to hide shared-
-// memory and HBM latency (cfg4a 1.10 -> 0.93 ms on one box).
+// Residency: every kernel here is latency-bound at low occupancy, so each
+// carries a launch bound picked by measurement: the transforms three CTAs per
+// SM (the 80 x 80 forward plane kernel four, at 64 registers), the
+// contraction three for fp16 spectra and narrow outputs, two for fp32.  At
+// the unbounded register counts (90-147) they ran one or two CTAs, too few
+// warps to hide shared-memory and HBM latency.
 constexpr int kMaxDim = 256;
 constexpr int kCols = 4;   // transform columns per depth-FFT CTA
 
