@@ -202,6 +202,9 @@ def test_fftconv3d_golden(cuda, case):
     (2, 24, 5, 8, 8, 64, (3, 3, 3), (1, 1, 1), "f16"),
     (3, 10, 4, 6, 6, 128, (3, 3, 3), (1, 1, 1), "bf16"),
     (2, 16, 5, 6, 8, 64, (3, 3, 3), (1, 1, 1), "f32"),
+    # 80 x 80 planes (the compile-time 16 x 5 plane kernels), ragged data
+    # rows inside the plane, an odd batch
+    (3, 4, 4, 70, 66, 6, (3, 11, 15), (1, 5, 7), "f16"),
 ])
 def test_fftconv3d_shapes(cuda, N, Cin, D, H, W, Cout, k, p, dt):
     from amd_tuned_torch import fftconv_ops
