@@ -465,13 +465,13 @@ depth_inv_reg_kernel(const float2* __restrict__ U, float2* __restrict__ G2, int 
 
 // --------------------------------------------------------------- K3 -----
 // U[f][p][co] = sum_ci Z[f][p][ci] H[hb][ci][co], and the partner -f with
-// conj(H).  One warp per stored bin; lane l owns output channels 2l, 2l + 1
-// of each 64-channel block, whose two fp16-complex weights are one 8-byte
-// load.  The input-channel loop runs in steps of 8 with every load of a step
-// issued first.  H is stored scaled by `hscale` (a power of two, see the
-// spectrum header); the sums are scaled back before they are written.
-// Input-channel pairs per step: as many weight loads in flight as the
-// registers hold (16 for fp16-complex weights, 8 for fp32-complex).
+// conj(H).  One warp per stored bin; the lane mapping (groups of lanes over
+// input channels, 4 output channels per lane, one 16-byte weight load) is
+// described in the kernel.  Every weight load of a step is issued before
+// the step's arithmetic.  H is stored scaled by `hscale` (a power of two, see
+// the spectrum header); the sums are scaled back before they are written.
+// Weight loads per lane per step at KDIV = 1 (the kernel takes ci_step /
+// KDIV): 16 for fp16-complex weights, 8 for fp32-complex.
 template <typename S>
 constexpr int ci_step() { return sizeof(S) == 4 ? 16 : 8; }
 
